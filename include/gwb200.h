@@ -1,0 +1,105 @@
+/* gwb200 — C ABI of the B200 (sm_100a) SVDQuant quantized-linear hot path.
+ *
+ * Plain pointers and sizes only; every compute entry point enqueues work on
+ * the given CUDA stream (cudaStream_t passed as void*; NULL = legacy default
+ * stream), never synchronises, never allocates, and returns a GwbStatus code
+ * (0 = success). Device buffers must be 16-byte aligned and row-major
+ * contiguous. Layouts:
+ *   x            bf16 [M, K]
+ *   smooth       bf16 [K] (or NULL)
+ *   proj_down_t  bf16 [rank_pad, K]   (L1 transposed; rows >= rank are zero)
+ *   codes        u8   [M, K/2]        INT4 two's-complement nibbles, even k low
+ *   ascale       f16  [M, K/64]       one scale per 64-group
+ *   la           bf16 [M, rank_pad]   x·L1 on raw x
+ *   w_codes      u8   [N, K/2], w_scale_gn f32 [K/64, N], proj_up bf16 [N, rank_pad]
+ *   bias         bf16 [N] (or NULL); out bf16 [M, N]
+ * Constraints: K % 128 == 0; N % 128 == 0 (W4A4) / N % 256 == 0 (W8A8);
+ * rank_pad in {0, 16, 32, 48, 64}.
+ */
+#ifndef GWB200_H
+#define GWB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Replaces `build_info` (reference csrc/cozy_kernels/ops.cpp:24-27): torch
+ * pin replaced by the CUDA runtime version and fatbin arch. Writes a NUL-
+ * terminated string; returns its length. */
+int gwb_build_info(char* buf, size_t len);
+
+/* Replaces `probe_add_one` (reference csrc/cozy_kernels/probe.cu:9-27;
+ * registered at csrc/cozy_kernels/ops.cpp:29-36): y = x + 1 on `n` floats. */
+int gwb_probe_add_one(const float* x, float* y, int64_t n, void* stream);
+
+/* Replaces `cozy_gen_worker::svdq_quant(x2, smooth, s2, blocked)`
+ * (reference src/gen_worker/models/svdq_fused.py:293-296, kernel :116-155)
+ * fused with the low-rank down-projection `la = x2 @ proj_down`
+ * (svdq_fused.py:524, svdq_native.py:153). INT4 group-64 with fp16 scales in
+ * place of NVFP4; no per-tensor second-level scale. */
+int gwb_svdq_w4a4_quant(const void* x, const void* smooth, const void* proj_down_t,
+                        int64_t M, int64_t K, int rank_pad,
+                        void* codes, void* ascale, void* la, void* stream);
+
+/* Replaces `cozy_gen_worker::svdq_gemm_w4a4_lora(qa, sa, wq_kn, ws, s2,
+ * second, lora_act, up, bias)` (reference svdq_fused.py:379-383, kernel
+ * :180-238) and the baseline chain `_gemm_w4a4` + scale + low-rank + bias of
+ * `SvdqLinear.forward` (svdq_native.py:148-155). gelu != 0 applies
+ * GELU(tanh) after the bias. */
+int gwb_svdq_w4a4_gemm(const void* codes, const void* ascale, const void* w_codes,
+                       const float* w_scale_gn, const void* la, const void* proj_up,
+                       const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
+                       int gelu, void* out, void* stream);
+
+/* Debug/parity entry (no reference counterpart beyond the int32 group sums
+ * the reference's GEMM forms internally, svdq_fused.py:213-222): the same
+ * tcgen05 GEMM with the epilogue replaced by a dump of every 64-group s32
+ * partial sum, partials s32 [K/64, M, N]. */
+int gwb_svdq_w4a4_group_partials(const void* codes, const void* w_codes, int64_t M, int64_t N,
+                                 int64_t K, int32_t* partials, void* stream);
+
+/* Whole SvdqLinear forward (reference svdq_native.py:140-156): quantise +
+ * GEMM. The caller supplies the scratch buffers codes / ascale / la (sizes
+ * as above). */
+int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_down_t,
+                         const void* w_codes, const float* w_scale_gn, const void* proj_up,
+                         const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
+                         int gelu, void* codes, void* ascale, void* la, void* out,
+                         void* stream);
+
+/* Replaces the W8A8 activation quantiser `_quant_src` rowwise branch
+ * (reference src/gen_worker/models/w8a8.py:261-273): per-token symmetric
+ * INT8, q s8 [M, K], scale f32 [M]. */
+int gwb_w8a8_quant(const void* x, int64_t M, int64_t K, void* q, void* scale, void* stream);
+
+/* Replaces `torch._scaled_mm(xq, w.t(), scale_a, scale_b, bias)` rowwise in
+ * `Fp8ScaledLinear.forward` (reference w8a8.py:374-378) with INT8 operands;
+ * w_q s8 [N, K], w_scale f32 [N]; gelu != 0 fuses GELU(tanh). */
+int gwb_w8a8_gemm(const void* q, const float* scale, const void* w_q, const float* w_scale,
+                  const void* bias, int64_t M, int64_t N, int64_t K, int gelu, void* out,
+                  void* stream);
+
+/* Whole `Fp8ScaledLinear.forward` rowwise (reference w8a8.py:359-381) with
+ * INT8: quantise into the caller's scratch q / scale, then GEMM. */
+int gwb_w8a8_linear(const void* x, const void* w_q, const float* w_scale, const void* bias,
+                    int64_t M, int64_t N, int64_t K, int gelu, void* q, void* scale,
+                    void* out, void* stream);
+
+/* Reads and clears the device-side error flag set by a bounded wait that
+ * expired (0 = none). Synchronises the device. */
+int gwb_device_error(int* code);
+
+/* 0 when the current device is sm_100 (B200), GWB_E_ARCH otherwise. */
+int gwb_device_check(void);
+
+/* Static description of a status code. */
+const char* gwb_status_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GWB200_H */

@@ -1,0 +1,174 @@
+// C-ABI entry points of libgwb200.so (declared in include/gwb200.h). The
+// library is one translation unit: the kernel sources are included here.
+#include <cuda_runtime.h>
+#include <cstdio>
+#include <cstring>
+#include "gwb.h"
+#include "ptx.cuh"
+#include "act_quant.cu"
+#include "gemm.cu"
+#include "../../include/gwb200.h"
+
+#ifndef GWB_ARCH_STRING
+#define GWB_ARCH_STRING "sm_100a"
+#endif
+
+namespace {
+
+__global__ void probe_add_one_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                     int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = x[i] + 1.0f;
+}
+
+inline cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+
+inline bool fits_int(int64_t v) { return v >= 0 && v <= 0x7fffffff; }
+
+inline int check_w4a4_shape(int64_t M, int64_t N, int64_t K, int rank_pad) {
+  if (!fits_int(M) || !fits_int(N) || !fits_int(K) || M == 0) return GWB_E_SHAPE;
+  if (K % 128 || N % 128) return GWB_E_SHAPE;
+  if (rank_pad < 0 || rank_pad > 64 || rank_pad % 16) return GWB_E_SHAPE;
+  return GWB_SUCCESS;
+}
+
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int gwb_build_info(char* buf, size_t len) {
+  int rt = 0;
+  cudaRuntimeGetVersion(&rt);
+  char tmp[160];
+  int n = snprintf(tmp, sizeof(tmp), "gwb200 cuda_runtime=%d.%d archs=%s", rt / 1000,
+                   (rt % 1000) / 10, GWB_ARCH_STRING);
+  if (buf && len) {
+    strncpy(buf, tmp, len - 1);
+    buf[len - 1] = '\0';
+  }
+  return n;
+}
+
+int gwb_probe_add_one(const float* x, float* y, int64_t n, void* stream) {
+  if (n < 0) return GWB_E_SHAPE;
+  if (n == 0) return GWB_SUCCESS;
+  int blocks = (int)((n + 255) / 256);
+  if (blocks > 4096) blocks = 4096;
+  probe_add_one_kernel<<<blocks, 256, 0, S(stream)>>>(x, y, n);
+  return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
+}
+
+int gwb_svdq_w4a4_quant(const void* x, const void* smooth, const void* proj_down_t, int64_t M,
+                        int64_t K, int rank_pad, void* codes, void* ascale, void* la,
+                        void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  if (!fits_int(M) || !fits_int(K) || K % 64) return GWB_E_SHAPE;
+  if (rank_pad < 0 || rank_pad > 64 || rank_pad % 16) return GWB_E_SHAPE;
+  if (rank_pad > 0 && (!proj_down_t || !la)) return GWB_E_SHAPE;
+  if (!al16(x) || !al16(codes) || (smooth && !al16(smooth)) ||
+      (proj_down_t && !al16(proj_down_t)) || (la && !al16(la)) ||
+      (reinterpret_cast<uintptr_t>(ascale) & 1u))
+    return GWB_E_ALIGN;
+  return gwb::launch_act_int4(x, smooth, rank_pad ? proj_down_t : nullptr, codes, ascale,
+                              rank_pad ? la : nullptr, (int)M, (int)K, rank_pad, S(stream));
+}
+
+int gwb_svdq_w4a4_gemm(const void* codes, const void* ascale, const void* w_codes,
+                       const float* w_scale_gn, const void* la, const void* proj_up,
+                       const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
+                       int gelu, void* out, void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  int rc = check_w4a4_shape(M, N, K, rank_pad);
+  if (rc) return rc;
+  gwb::W4A4Args a{codes, ascale, w_codes, w_scale_gn, la, proj_up, bias, out, nullptr,
+                  (int)M, (int)N, (int)K, rank_pad, gelu ? 1 : 0};
+  return gwb::launch_gemm_w4a4(a, S(stream));
+}
+
+int gwb_svdq_w4a4_group_partials(const void* codes, const void* w_codes, int64_t M, int64_t N,
+                                 int64_t K, int32_t* partials, void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  int rc = check_w4a4_shape(M, N, K, 0);
+  if (rc) return rc;
+  if ((K / 64) * M * N > (int64_t)1 << 31) return GWB_E_CAPACITY;
+  // the partial dump path reads no scales; pass the codes pointer as a
+  // 16-byte-aligned placeholder for the unused scale operands
+  gwb::W4A4Args a{codes, codes, w_codes, reinterpret_cast<const float*>(w_codes), nullptr,
+                  nullptr, nullptr, nullptr, partials, (int)M, (int)N, (int)K, 0, 0};
+  return gwb::launch_gemm_w4a4(a, S(stream));
+}
+
+int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_down_t,
+                         const void* w_codes, const float* w_scale_gn, const void* proj_up,
+                         const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
+                         int gelu, void* codes, void* ascale, void* la, void* out,
+                         void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  int rc = check_w4a4_shape(M, N, K, rank_pad);
+  if (rc) return rc;
+  rc = gwb_svdq_w4a4_quant(x, smooth, proj_down_t, M, K, rank_pad, codes, ascale, la, stream);
+  if (rc) return rc;
+  return gwb_svdq_w4a4_gemm(codes, ascale, w_codes, w_scale_gn, la, proj_up, bias, M, N, K,
+                            rank_pad, gelu, out, stream);
+}
+
+int gwb_w8a8_quant(const void* x, int64_t M, int64_t K, void* q, void* scale, void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  if (!fits_int(M) || !fits_int(K) || K % 8 || K == 0) return GWB_E_SHAPE;
+  if (!al16(x) || !al16(q) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return GWB_E_ALIGN;
+  return gwb::launch_act_int8(x, q, scale, (int)M, (int)K, S(stream));
+}
+
+int gwb_w8a8_gemm(const void* q, const float* scale, const void* w_q, const float* w_scale,
+                  const void* bias, int64_t M, int64_t N, int64_t K, int gelu, void* out,
+                  void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  if (!fits_int(M) || !fits_int(N) || !fits_int(K)) return GWB_E_SHAPE;
+  gwb::W8A8Args a{q, scale, w_q, w_scale, bias, out, (int)M, (int)N, (int)K, gelu ? 1 : 0};
+  return gwb::launch_gemm_w8a8(a, S(stream));
+}
+
+int gwb_w8a8_linear(const void* x, const void* w_q, const float* w_scale, const void* bias,
+                    int64_t M, int64_t N, int64_t K, int gelu, void* q, void* scale, void* out,
+                    void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  if (!fits_int(N) || K % 128 || N % 256) return GWB_E_SHAPE;
+  int rc = gwb_w8a8_quant(x, M, K, q, scale, stream);
+  if (rc) return rc;
+  return gwb_w8a8_gemm(q, static_cast<const float*>(scale), w_q, w_scale, bias, M, N, K, gelu,
+                       out, stream);
+}
+
+int gwb_device_error(int* code) {
+  if (!code) return GWB_E_SHAPE;
+  if (cudaDeviceSynchronize() != cudaSuccess) return GWB_E_LAUNCH;
+  return gwb::device_error_read_and_clear(code);
+}
+
+int gwb_device_check(void) {
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GWB_E_ARCH;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  return (major == 10 && minor == 0) ? GWB_SUCCESS : GWB_E_ARCH;
+}
+
+const char* gwb_status_string(int status) {
+  switch (status) {
+    case GWB_SUCCESS: return "success";
+    case GWB_E_SHAPE: return "unsupported or inconsistent sizes";
+    case GWB_E_ALIGN: return "pointer not 16-byte aligned";
+    case GWB_E_LAUNCH: return "kernel launch failed";
+    case GWB_E_TMAP: return "TMA tensor-map encode failed";
+    case GWB_E_DRIVER: return "driver entry point cuTensorMapEncodeTiled unavailable";
+    case GWB_E_DEVICE: return "device-side bounded wait expired";
+    case GWB_E_ARCH: return "device is not sm_100 (B200)";
+    case GWB_E_CAPACITY: return "request exceeds a fixed capacity";
+    default: return "unknown status";
+  }
+}
+
+}  // extern "C"

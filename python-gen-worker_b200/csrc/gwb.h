@@ -1,0 +1,50 @@
+// Internal declarations shared by the CUDA translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+// Host-visible status codes (also returned through the C ABI).
+enum GwbStatus : int {
+  GWB_SUCCESS = 0,
+  GWB_E_SHAPE = 1,      // unsupported / inconsistent sizes
+  GWB_E_ALIGN = 2,      // pointer not 16-byte aligned
+  GWB_E_LAUNCH = 3,     // kernel launch failed
+  GWB_E_TMAP = 4,       // tensor-map encode failed
+  GWB_E_DRIVER = 5,     // driver entry point unavailable
+  GWB_E_DEVICE = 6,     // device-side error flag was set (bounded wait expired)
+  GWB_E_ARCH = 7,       // device is not sm_100
+  GWB_E_CAPACITY = 8,   // request exceeds a fixed capacity
+};
+
+namespace gwb {
+int launch_act_int4(const void* x, const void* smooth, const void* down_t, void* codes,
+                    void* ascale, void* la, int M, int K, int rank_pad, cudaStream_t st);
+int launch_act_int8(const void* x, void* q, void* scale, int M, int K, cudaStream_t st);
+
+struct W4A4Args {
+  const void* a_codes;   // u8 [M, K/2]
+  const void* a_scale;   // f16 [M, K/64]
+  const void* w_codes;   // u8 [N, K/2]
+  const float* w_scale_gn;  // f32 [K/64, N] (load-time transposed weight scales)
+  const void* la;        // bf16 [M, rank_pad] or null
+  const void* up;        // bf16 [N, rank_pad] or null
+  const void* bias;      // bf16 [N] or null
+  void* out;             // bf16 [M, N]
+  int32_t* partials;     // optional debug: s32 [K/64, M, N]; disables the epilogue
+  int M, N, K, rank_pad, gelu;
+};
+int launch_gemm_w4a4(const W4A4Args& a, cudaStream_t st);
+
+struct W8A8Args {
+  const void* a_q;        // s8 [M, K]
+  const float* a_scale;   // f32 [M]
+  const void* w_q;        // s8 [N, K]
+  const float* w_scale;   // f32 [N]
+  const void* bias;       // bf16 [N] or null
+  void* out;              // bf16 [M, N]
+  int M, N, K, gelu;
+};
+int launch_gemm_w8a8(const W8A8Args& a, cudaStream_t st);
+
+int device_error_read_and_clear(int* code);
+}  // namespace gwb

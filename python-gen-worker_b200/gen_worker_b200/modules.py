@@ -1,0 +1,255 @@
+"""Drop-in quantized linear modules and the module-swap seam.
+
+``SvdqInt4Linear`` keeps the buffer names of the reference's ``SvdqLinear``
+(``src/gen_worker/models/svdq_native.py:94-138``): ``weight`` (packed nibbles,
+u8 [N, K/2]), ``weight_scale``, ``smooth_factor`` [K], ``proj_down`` [K, r],
+``proj_up`` [N, r], ``bias`` [N]; its layout tag ``int4-g64-lownib`` names the
+INT4 group-64 format (fp16 scale per 64-group, ``weight_scale`` f16
+[N, K/64], even k in the low nibble). ``W8A8Int8Linear`` keeps
+``Fp8ScaledLinear``'s (``src/gen_worker/models/w8a8.py:313-354``): ``weight``
+s8 [N, K], ``weight_scale`` f32 [N, 1], ``bias``.
+
+The forward is the reference's dataflow (smooth -> quantise -> GEMM -> scale
+-> + (x·L1)·L2ᵀ -> + bias) executed by two native kernels; an optional
+fused GELU(tanh) covers the FF projection that diffusers follows with GELU.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Dict, Optional
+
+import torch
+import torch.nn as nn
+
+from . import ops
+
+LAYOUT_INT4 = "int4-g64-lownib"
+GROUP = 64
+_K_ALIGN = 128
+_N_ALIGN = 128
+
+
+class SvdqB200LayoutError(ValueError):
+    """A buffer set this module does not understand (``SvdqLayoutError``
+    counterpart, ``svdq_layout.py:41``)."""
+
+
+# ---------------------------------------------------------------- producer
+def quantize_int4_rows(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Symmetric INT4 group-64 quantisation of a [R, K] matrix (fp32 math):
+    s = fp16(clamp(amax/7, 2^-24, 65504)); q = clamp(rint(w/s), -8, 7);
+    packed two per byte, even k in the low nibble."""
+    r, k = w.shape
+    if k % GROUP:
+        raise SvdqB200LayoutError(f"K={k} is not a multiple of {GROUP}")
+    g = w.float().reshape(r, k // GROUP, GROUP)
+    s = (g.abs().amax(dim=-1) / 7.0).clamp(min=2.0 ** -24, max=65504.0).to(torch.float16)
+    q = torch.round(g / s.float().unsqueeze(-1)).clamp(-8, 7).reshape(r, k).to(torch.int16) & 0xF
+    packed = ((q[:, 1::2] << 4) | q[:, 0::2]).to(torch.uint8).contiguous()
+    return packed, s
+
+
+def quantize_int8_rows(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row symmetric INT8 (``quantize_tree_w8a8``'s per-out-channel
+    producer, ``w8a8.py:774-779``, with qmax 127)."""
+    wf = w.float()
+    s = (wf.abs().amax(dim=-1) / 127.0).clamp(min=1e-12)
+    q = torch.round(wf / s.unsqueeze(-1)).clamp(-127, 127).to(torch.int8)
+    return q, s
+
+
+# ---------------------------------------------------------------- modules
+class SvdqInt4Linear(nn.Module):
+    _cozy_svdq_linear = True
+    layout = LAYOUT_INT4
+
+    def __init__(self, in_features: int, out_features: int, *, rank: int, bias: bool,
+                 compute_dtype: Any = torch.bfloat16, smooth: bool = True,
+                 gelu: bool = False, device: Any = None) -> None:
+        super().__init__()
+        if in_features % _K_ALIGN or out_features % _N_ALIGN:
+            raise SvdqB200LayoutError(
+                f"SvdqInt4Linear dims [{out_features}, {in_features}] break the "
+                f"tile alignment (in%{_K_ALIGN}, out%{_N_ALIGN})")
+        if compute_dtype != torch.bfloat16:
+            raise SvdqB200LayoutError("compute dtype must be bf16")
+        self.in_features = int(in_features)
+        self.out_features = int(out_features)
+        self.rank = int(rank)
+        self.gelu = bool(gelu)
+        self.compute_dtype = compute_dtype
+        dev = device or torch.device("meta")
+        self.register_buffer("weight", torch.empty(out_features, in_features // 2,
+                                                   dtype=torch.uint8, device=dev))
+        self.register_buffer("weight_scale", torch.empty(out_features, in_features // GROUP,
+                                                         dtype=torch.float16, device=dev))
+        if smooth:
+            self.register_buffer("smooth_factor", torch.empty(in_features, dtype=compute_dtype,
+                                                              device=dev))
+        else:
+            self.smooth_factor = None
+        if self.rank:
+            self.register_buffer("proj_down", torch.empty(in_features, self.rank,
+                                                          dtype=compute_dtype, device=dev))
+            self.register_buffer("proj_up", torch.empty(out_features, self.rank,
+                                                        dtype=compute_dtype, device=dev))
+        else:
+            self.proj_down = None
+            self.proj_up = None
+        if bias:
+            self.bias: Optional[nn.Parameter] = nn.Parameter(
+                torch.empty(out_features, dtype=compute_dtype, device=dev), requires_grad=False)
+        else:
+            self.bias = None
+        self._packed: Optional[Dict[str, Any]] = None
+
+    def prepare(self) -> Dict[str, Any]:
+        """Kernel-layout copies of the scale and low-rank buffers (built once,
+        on the buffers' device)."""
+        dev = self.weight.device
+        if self._packed is None or self._packed["device"] != dev:
+            p = ops.prepare_w4a4_weights(self.weight_scale, self.proj_down, self.proj_up)
+            p["device"] = dev
+            self._packed = p
+        return self._packed
+
+    def _apply(self, fn, recurse=True):  # noqa: ANN001 — drop stale repacks on .to()
+        self._packed = None
+        return super()._apply(fn, recurse)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        x2 = x.reshape(-1, self.in_features)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        p = self.prepare()
+        codes, ascale, la = ops.svdq_w4a4_quant(x2, self.smooth_factor, p["proj_down_t"])
+        y = ops.svdq_w4a4_gemm(codes, ascale, self.weight, p["w_scale_gn"],
+                               la if p["proj_down_t"] is not None else None,
+                               p["proj_up_pad"],
+                               self.bias.detach() if self.bias is not None else None,
+                               self.gelu)
+        return y.reshape(*shape[:-1], self.out_features)
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, "
+                f"rank={self.rank}, bias={self.bias is not None}, "
+                f"smooth={self.smooth_factor is not None}, gelu={self.gelu}, "
+                f"layout={self.layout}")
+
+
+class W8A8Int8Linear(nn.Module):
+    _cozy_w8a8_linear = True
+
+    def __init__(self, in_features: int, out_features: int, *, bias: bool,
+                 compute_dtype: Any = torch.bfloat16, gelu: bool = False,
+                 device: Any = None) -> None:
+        super().__init__()
+        if in_features % 128 or out_features % 256:
+            raise SvdqB200LayoutError(
+                f"W8A8Int8Linear dims [{out_features}, {in_features}] break the tile "
+                f"alignment (in%128, out%256)")
+        self.in_features = int(in_features)
+        self.out_features = int(out_features)
+        self.gelu = bool(gelu)
+        self.compute_dtype = compute_dtype
+        dev = device or torch.device("meta")
+        self.register_buffer("weight", torch.empty(out_features, in_features, dtype=torch.int8,
+                                                   device=dev))
+        self.register_buffer("weight_scale", torch.empty(out_features, 1, dtype=torch.float32,
+                                                         device=dev))
+        if bias:
+            self.bias: Optional[nn.Parameter] = nn.Parameter(
+                torch.empty(out_features, dtype=compute_dtype, device=dev), requires_grad=False)
+        else:
+            self.bias = None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        x2 = x.reshape(-1, self.in_features)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        q, s = ops.w8a8_quant(x2)
+        y = ops.w8a8_gemm(q, s, self.weight, self.weight_scale.reshape(-1),
+                          self.bias.detach() if self.bias is not None else None, self.gelu)
+        return y.reshape(*shape[:-1], self.out_features)
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, "
+                f"bias={self.bias is not None}, gelu={self.gelu}, mode=int8-rowwise")
+
+
+# ---------------------------------------------------------------- builders / swap
+def build_svdq_int4_linear(buf: Dict[str, Any], *, gelu: bool = False,
+                           device: Any = None) -> SvdqInt4Linear:
+    """A device-resident module from a buffer dict with the ``SvdqBuffers``
+    field names (``svdq_layout.py:66-78``; ``build_svdq_linear``,
+    ``svdq_native.py:173-197``)."""
+    w = buf["weight"]
+    n, k2 = w.shape
+    down = buf.get("proj_down")
+    rank = 0 if down is None else int(down.shape[1])
+    mod = SvdqInt4Linear(k2 * 2, n, rank=rank, bias=buf.get("bias") is not None,
+                         smooth=buf.get("smooth_factor") is not None, gelu=gelu,
+                         device=torch.device("cpu"))
+    dev = device or w.device
+    ws = buf["weight_scale"]
+    if tuple(ws.shape) != (n, k2 * 2 // GROUP):
+        raise SvdqB200LayoutError(f"weight_scale shape {tuple(ws.shape)} != {(n, k2 * 2 // GROUP)}")
+    mod.weight = w.contiguous().to(dev)
+    mod.weight_scale = ws.to(torch.float16).contiguous().to(dev)
+    if mod.smooth_factor is not None:
+        mod.smooth_factor = buf["smooth_factor"].to(torch.bfloat16).reshape(-1).contiguous().to(dev)
+    if rank:
+        mod.proj_down = down.to(torch.bfloat16).contiguous().to(dev)
+        mod.proj_up = buf["proj_up"].to(torch.bfloat16).contiguous().to(dev)
+    if mod.bias is not None:
+        mod.bias = nn.Parameter(buf["bias"].detach().to(torch.bfloat16).reshape(-1).to(dev),
+                                requires_grad=False)
+    return mod
+
+
+def build_w8a8_int8_linear(buf: Dict[str, Any], *, gelu: bool = False,
+                           device: Any = None) -> W8A8Int8Linear:
+    w = buf["weight"]
+    n, k = w.shape
+    mod = W8A8Int8Linear(k, n, bias=buf.get("bias") is not None, gelu=gelu,
+                         device=torch.device("cpu"))
+    dev = device or w.device
+    mod.weight = w.to(torch.int8).contiguous().to(dev)
+    mod.weight_scale = buf["weight_scale"].float().reshape(n, 1).contiguous().to(dev)
+    if mod.bias is not None:
+        mod.bias = nn.Parameter(buf["bias"].detach().to(torch.bfloat16).reshape(-1).to(dev),
+                                requires_grad=False)
+    return mod
+
+
+def svdq_int4_from_linear(lin: nn.Linear, smooth: Optional[torch.Tensor] = None,
+                          proj_down: Optional[torch.Tensor] = None,
+                          proj_up: Optional[torch.Tensor] = None,
+                          gelu: bool = False) -> SvdqInt4Linear:
+    """Data-free producer: quantise a dense linear's W·diag(smooth) to INT4
+    group-64 (the stored weight that ``fold_to_dense`` divides back by smooth,
+    ``svdq_native.py:207-208``)."""
+    w = lin.weight.detach().float()
+    if smooth is not None:
+        w = w * smooth.to(torch.bfloat16).float().reshape(1, -1).to(w.device)
+    packed, scale = quantize_int4_rows(w)
+    buf = {"weight": packed, "weight_scale": scale, "smooth_factor": smooth,
+           "proj_down": proj_down, "proj_up": proj_up,
+           "bias": lin.bias.detach() if lin.bias is not None else None}
+    return build_svdq_int4_linear(buf, gelu=gelu, device=lin.weight.device)
+
+
+def swap_linears(model: nn.Module, replacements: Dict[str, nn.Module]) -> int:
+    """Install modules by dotted path with ``setattr`` — the seam of
+    ``swap_svdq_linears`` (``svdq_native.py:266-321``). Returns the count."""
+    n = 0
+    for path, mod in replacements.items():
+        parent_path, _, leaf = path.rpartition(".")
+        parent = model.get_submodule(parent_path) if parent_path else model
+        if not hasattr(parent, leaf):
+            raise SvdqB200LayoutError(f"no module at {path!r}")
+        setattr(parent, leaf, mod)
+        n += 1
+    return n

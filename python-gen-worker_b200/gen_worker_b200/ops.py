@@ -1,0 +1,210 @@
+"""Torch-facing ops over the C ABI (``torch.ops.gwb200.*``).
+
+Counterparts of the reference's custom ops
+``cozy_gen_worker::svdq_quant`` / ``svdq_gemm_w4a4_lora`` /
+``svdq_epilogue_lora`` (``src/gen_worker/models/svdq_fused.py:293-391``):
+outputs are allocated with ``torch.empty`` on the input device, inputs are
+never copied (they must already be contiguous CUDA tensors of the stated
+dtype), work is enqueued on the current stream, and every op has a fake
+(meta) implementation so ``torch.compile`` can trace through it. There is no
+CPU implementation: a CPU tensor raises.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import native
+
+GROUP = 64
+
+
+class SvdqB200Error(RuntimeError):
+    """Typed failure of a gwb200 op (``SvdqFusedError`` counterpart,
+    ``svdq_fused.py:34``)."""
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _need(t: Optional[torch.Tensor], name: str, dtype: torch.dtype, ndim: int) -> None:
+    if t is None:
+        return
+    if not t.is_cuda:
+        raise SvdqB200Error(f"{name} must be a CUDA tensor (no CPU path), got {t.device}")
+    if t.dtype != dtype:
+        raise SvdqB200Error(f"{name} must be {dtype}, got {t.dtype}")
+    if t.dim() != ndim:
+        raise SvdqB200Error(f"{name} must be {ndim}-D, got shape {tuple(t.shape)}")
+    if not t.is_contiguous():
+        raise SvdqB200Error(f"{name} must be contiguous")
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def rank_pad_of(rank: int) -> int:
+    return 0 if rank <= 0 else ((rank + 15) // 16) * 16
+
+
+# ---------------------------------------------------------------- W4A4
+@torch.library.custom_op("gwb200::svdq_w4a4_quant", mutates_args=())
+def svdq_w4a4_quant(x2: torch.Tensor, smooth: Optional[torch.Tensor],
+                    proj_down_t: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """x2 bf16 [M, K] -> (codes u8 [M, K/2], ascale f16 [M, K/64],
+    la bf16 [M, rank_pad]) with la = x2 · L1 (raw x)."""
+    _need(x2, "x2", torch.bfloat16, 2)
+    _need(smooth, "smooth", torch.bfloat16, 1)
+    _need(proj_down_t, "proj_down_t", torch.bfloat16, 2)
+    m, k = x2.shape
+    rp = 0 if proj_down_t is None else int(proj_down_t.shape[0])
+    codes = torch.empty(m, k // 2, dtype=torch.uint8, device=x2.device)
+    ascale = torch.empty(m, k // GROUP, dtype=torch.float16, device=x2.device)
+    la = torch.empty(m, rp, dtype=torch.bfloat16, device=x2.device)
+    lib = native.require()
+    native.check(lib.gwb_svdq_w4a4_quant(x2.data_ptr(), _ptr(smooth), _ptr(proj_down_t), m, k, rp,
+                                         codes.data_ptr(), ascale.data_ptr(),
+                                         la.data_ptr() if rp else None, _stream()),
+                 "svdq_w4a4_quant")
+    return codes, ascale, la
+
+
+@svdq_w4a4_quant.register_fake
+def _(x2, smooth, proj_down_t):
+    m, k = x2.shape
+    rp = 0 if proj_down_t is None else int(proj_down_t.shape[0])
+    return (x2.new_empty(m, k // 2, dtype=torch.uint8),
+            x2.new_empty(m, k // GROUP, dtype=torch.float16),
+            x2.new_empty(m, rp, dtype=torch.bfloat16))
+
+
+@torch.library.custom_op("gwb200::svdq_w4a4_gemm", mutates_args=())
+def svdq_w4a4_gemm(codes: torch.Tensor, ascale: torch.Tensor, w_codes: torch.Tensor,
+                   w_scale_gn: torch.Tensor, la: Optional[torch.Tensor],
+                   proj_up: Optional[torch.Tensor], bias: Optional[torch.Tensor],
+                   gelu: bool) -> torch.Tensor:
+    """INT4 GEMM + group promotion + low-rank up-projection + bias
+    (+ GELU) -> bf16 [M, N]."""
+    _need(codes, "codes", torch.uint8, 2)
+    _need(ascale, "ascale", torch.float16, 2)
+    _need(w_codes, "w_codes", torch.uint8, 2)
+    _need(w_scale_gn, "w_scale_gn", torch.float32, 2)
+    _need(bias, "bias", torch.bfloat16, 1)
+    m, k = codes.shape[0], codes.shape[1] * 2
+    n = w_codes.shape[0]
+    rp = 0
+    if la is not None and proj_up is not None and la.shape[1] > 0:
+        _need(la, "la", torch.bfloat16, 2)
+        _need(proj_up, "proj_up", torch.bfloat16, 2)
+        rp = int(la.shape[1])
+        if int(proj_up.shape[1]) != rp:
+            raise SvdqB200Error(f"la rank {rp} != proj_up rank {proj_up.shape[1]}")
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=codes.device)
+    lib = native.require()
+    native.check(lib.gwb_svdq_w4a4_gemm(codes.data_ptr(), ascale.data_ptr(), w_codes.data_ptr(),
+                                        w_scale_gn.data_ptr(), _ptr(la) if rp else None,
+                                        _ptr(proj_up) if rp else None, _ptr(bias), m, n, k, rp,
+                                        int(bool(gelu)), out.data_ptr(), _stream()),
+                 "svdq_w4a4_gemm")
+    return out
+
+
+@svdq_w4a4_gemm.register_fake
+def _(codes, ascale, w_codes, w_scale_gn, la, proj_up, bias, gelu):
+    return codes.new_empty(codes.shape[0], w_codes.shape[0], dtype=torch.bfloat16)
+
+
+@torch.library.custom_op("gwb200::svdq_w4a4_group_partials", mutates_args=())
+def svdq_w4a4_group_partials(codes: torch.Tensor, w_codes: torch.Tensor) -> torch.Tensor:
+    """Debug: every 64-group s32 partial sum of the tcgen05 GEMM,
+    s32 [K/64, M, N]."""
+    _need(codes, "codes", torch.uint8, 2)
+    _need(w_codes, "w_codes", torch.uint8, 2)
+    m, k = codes.shape[0], codes.shape[1] * 2
+    n = w_codes.shape[0]
+    out = torch.empty(k // GROUP, m, n, dtype=torch.int32, device=codes.device)
+    lib = native.require()
+    native.check(lib.gwb_svdq_w4a4_group_partials(codes.data_ptr(), w_codes.data_ptr(), m, n, k,
+                                                  out.data_ptr(), _stream()),
+                 "svdq_w4a4_group_partials")
+    return out
+
+
+@svdq_w4a4_group_partials.register_fake
+def _(codes, w_codes):
+    return codes.new_empty(codes.shape[1] * 2 // GROUP, codes.shape[0], w_codes.shape[0],
+                           dtype=torch.int32)
+
+
+# ---------------------------------------------------------------- W8A8
+@torch.library.custom_op("gwb200::w8a8_quant", mutates_args=())
+def w8a8_quant(x2: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-token INT8: x2 bf16 [M, K] -> (q s8 [M, K], scale f32 [M])."""
+    _need(x2, "x2", torch.bfloat16, 2)
+    m, k = x2.shape
+    q = torch.empty(m, k, dtype=torch.int8, device=x2.device)
+    s = torch.empty(m, dtype=torch.float32, device=x2.device)
+    lib = native.require()
+    native.check(lib.gwb_w8a8_quant(x2.data_ptr(), m, k, q.data_ptr(), s.data_ptr(), _stream()),
+                 "w8a8_quant")
+    return q, s
+
+
+@w8a8_quant.register_fake
+def _(x2):
+    return x2.new_empty(x2.shape, dtype=torch.int8), x2.new_empty(x2.shape[0], dtype=torch.float32)
+
+
+@torch.library.custom_op("gwb200::w8a8_gemm", mutates_args=())
+def w8a8_gemm(q: torch.Tensor, scale: torch.Tensor, w_q: torch.Tensor, w_scale: torch.Tensor,
+              bias: Optional[torch.Tensor], gelu: bool) -> torch.Tensor:
+    _need(q, "q", torch.int8, 2)
+    _need(scale, "scale", torch.float32, 1)
+    _need(w_q, "w_q", torch.int8, 2)
+    _need(w_scale, "w_scale", torch.float32, 1)
+    _need(bias, "bias", torch.bfloat16, 1)
+    m, k = q.shape
+    n = w_q.shape[0]
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=q.device)
+    lib = native.require()
+    native.check(lib.gwb_w8a8_gemm(q.data_ptr(), scale.data_ptr(), w_q.data_ptr(),
+                                   w_scale.data_ptr(), _ptr(bias), m, n, k, int(bool(gelu)),
+                                   out.data_ptr(), _stream()), "w8a8_gemm")
+    return out
+
+
+@w8a8_gemm.register_fake
+def _(q, scale, w_q, w_scale, bias, gelu):
+    return q.new_empty(q.shape[0], w_q.shape[0], dtype=torch.bfloat16)
+
+
+# ---------------------------------------------------------------- load-time repacks
+def prepare_w4a4_weights(w_scale: torch.Tensor, proj_down: Optional[torch.Tensor],
+                         proj_up: Optional[torch.Tensor]) -> dict:
+    """Load-time repack of the module buffers into the kernel operand layouts
+    (the reference repacks at load too: ``to_buffers``,
+    ``svdq_layout.py:473-483``):
+      weight_scale f16 [N, K/64] -> w_scale_gn f32 [K/64, N]
+      proj_down bf16 [K, r]      -> proj_down_t bf16 [rank_pad, K] (zero rows)
+      proj_up bf16 [N, r]        -> proj_up_pad bf16 [N, rank_pad] (zero cols)"""
+    out = {"w_scale_gn": w_scale.float().t().contiguous()}
+    if proj_down is not None and proj_up is not None and proj_down.shape[1] > 0:
+        k, r = proj_down.shape
+        n = proj_up.shape[0]
+        rp = rank_pad_of(r)
+        if rp > 64:
+            raise SvdqB200Error(f"low-rank rank {r} > 64 is not supported")
+        dt = torch.zeros(rp, k, dtype=torch.bfloat16, device=proj_down.device)
+        dt[:r] = proj_down.to(torch.bfloat16).t()
+        up = torch.zeros(n, rp, dtype=torch.bfloat16, device=proj_up.device)
+        up[:, :r] = proj_up.to(torch.bfloat16)
+        out["proj_down_t"] = dt
+        out["proj_up_pad"] = up
+    else:
+        out["proj_down_t"] = None
+        out["proj_up_pad"] = None
+    return out

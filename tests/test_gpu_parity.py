@@ -1,0 +1,104 @@
+"""GPU parity of the CUDA path against the CPU oracle.
+
+Bit-exact: INT4/INT8 activation codes and scales, int32 group partials.
+bf16 outputs: rel-L2 <= 1e-3 against the oracle's bf16 output (the
+correctly rounded bf16 of its float64 result), and max-abs <= 2e-2 beyond
+the bf16 rounding of the float64 result itself."""
+import pytest
+import torch
+
+from oracle import svdq_oracle as O
+from gen_worker_b200 import ops, native
+from gen_worker_b200.modules import build_svdq_int4_linear, build_w8a8_int8_linear
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-3
+ABS_TOL = 2e-2
+
+
+def _layer_case(m, k, n, rank, seed, lora=0, bias=True, smooth=True):
+    x = O.synth_activation(m, k, seed)
+    L = O.synth_svdq_layer(k, n, rank, seed + 1, x, lora_rank=lora, bias=bias, smooth=smooth)
+    return x, L
+
+
+def _quant_gpu(x, L):
+    p = ops.prepare_w4a4_weights(L["w_scale"].cuda(), None if L["proj_down"] is None else L["proj_down"].cuda(),
+                                 None if L["proj_up"] is None else L["proj_up"].cuda())
+    sm = None if L["smooth"] is None else L["smooth"].cuda()
+    codes, ascale, la = ops.svdq_w4a4_quant(x.cuda(), sm, p["proj_down_t"])
+    torch.cuda.synchronize()
+    return p, codes, ascale, la
+
+
+@pytest.mark.parametrize("m,k", [(1, 128), (16, 256), (77, 3072), (333, 3072), (128, 12288)])
+def test_int4_activation_codes_and_scales_bit_exact(cuda_ready, m, k):
+    x, L = _layer_case(m, k, 128, 32, seed=m + k)
+    _, codes, ascale, la = _quant_gpu(x, L)
+    want_codes, want_scale = O.quant_int4(O.smooth_bf16(x, L["smooth"]))
+    assert torch.equal(codes.cpu(), want_codes)
+    assert torch.equal(ascale.cpu().view(torch.int16), want_scale.view(torch.int16))
+    la_ref = O.lowrank_down(x, L["proj_down"])
+    assert O.rel_l2(la.cpu()[:, :32], la_ref) < 1e-2
+
+
+def test_int4_activation_without_smoothing(cuda_ready):
+    x, L = _layer_case(64, 512, 128, 0, seed=5, smooth=False)
+    _, codes, ascale, _ = _quant_gpu(x, L)
+    want_codes, want_scale = O.quant_int4(O.smooth_bf16(x, None))
+    assert torch.equal(codes.cpu(), want_codes)
+    assert torch.equal(ascale.cpu().view(torch.int16), want_scale.view(torch.int16))
+
+
+@pytest.mark.parametrize("m,k,n", [(128, 128, 128), (200, 384, 256), (256, 3072, 384)])
+def test_int4_group_partials_bit_exact(cuda_ready, m, k, n):
+    x, L = _layer_case(m, k, n, 0, seed=m + n)
+    _, codes, _, _ = _quant_gpu(x, L)
+    got = ops.svdq_w4a4_group_partials(codes, L["w_packed"].cuda())
+    want = O.int4_group_partials(codes.cpu(), L["w_packed"])
+    assert torch.equal(got.cpu(), want)
+    assert native.device_error() == 0
+
+
+@pytest.mark.parametrize("m,k,n,rank,lora,gelu", [
+    (128, 128, 128, 0, 0, False),
+    (256, 3072, 384, 32, 0, False),
+    (77, 512, 256, 32, 0, True),
+    (300, 1024, 128, 32, 16, False),   # rank 48 (LoRA folded)
+    (64, 256, 128, 16, 0, False),
+])
+def test_int4_linear_matches_oracle(cuda_ready, m, k, n, rank, lora, gelu):
+    x, L = _layer_case(m, k, n, rank, seed=3 * m + n, lora=lora)
+    buf = {"weight": L["w_packed"], "weight_scale": L["w_scale"], "smooth_factor": L["smooth"],
+           "proj_down": L["proj_down"], "proj_up": L["proj_up"], "bias": L["bias"]}
+    mod = build_svdq_int4_linear(buf, gelu=gelu, device="cuda")
+    y = mod(x.cuda()).cpu()
+    want = O.svdq_int4_linear(x, L["smooth"], L["w_packed"], L["w_scale"], L["proj_down"],
+                              L["proj_up"], L["bias"], gelu=gelu)
+    assert O.rel_l2(y, want["y"]) <= REL_TOL
+    assert O.max_abs_beyond_bf16(y, want["y64"]) <= ABS_TOL
+    assert native.device_error() == 0
+
+
+@pytest.mark.parametrize("m,k", [(1, 128), (77, 3072), (256, 12288)])
+def test_int8_activation_bit_exact(cuda_ready, m, k):
+    x = O.synth_activation(m, k, seed=m)
+    q, s = ops.w8a8_quant(x.cuda())
+    wq, ws = O.quant_int8_rows(x)
+    assert torch.equal(q.cpu(), wq)
+    assert torch.equal(s.cpu(), ws)
+
+
+@pytest.mark.parametrize("m,k,n,gelu", [(128, 128, 256, False), (333, 3072, 512, True),
+                                         (64, 1024, 256, False)])
+def test_w8a8_linear_matches_oracle(cuda_ready, m, k, n, gelu):
+    x = O.synth_activation(m, k, seed=k + n)
+    L = O.synth_w8a8_layer(k, n, seed=m)
+    mod = build_w8a8_int8_linear({"weight": L["w_q"], "weight_scale": L["w_scale"],
+                                  "bias": L["bias"]}, gelu=gelu, device="cuda")
+    y = mod(x.cuda()).cpu()
+    want = O.w8a8_int8_linear(x, L["w_q"], L["w_scale"], L["bias"], gelu=gelu)
+    assert O.rel_l2(y, want["y"]) <= REL_TOL
+    assert O.max_abs_beyond_bf16(y, want["y64"]) <= ABS_TOL
+    assert native.device_error() == 0
