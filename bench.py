@@ -247,6 +247,86 @@ def cpu_reference(steps: int, warmup: int, sample_tokens: int = 64) -> dict:
             "ms_per_stack_sample": per_stack * 1e3}
 
 
+# --------------------------------------------------------------------------- per-config cases
+CASES = {
+    # name: list of (kind, M, K, N, rank, gelu)
+    "cfg0": [("w4a4", 256, 3072, 3072, 32, False)],
+    "cfg1": [("w8a8", 4096, 3072, 12288, 0, True)],
+    "cfg2": [("w4a4", 4608, 3072, 9216, 32, False), ("w4a4", 4608, 3072, 3072, 32, False),
+             ("w4a4", 4608, 3072, 12288, 32, True), ("w4a4", 4608, 12288, 3072, 32, False)],
+    "cfg3": [("w4a4", 4608, 3072, 3072, 48, False)],
+}
+
+
+def run_case(name: str, steps: int, warmup: int) -> dict:
+    """Time one BASELINE config's linears (quantiser + GEMM, the module's two
+    launches) with CUDA events on the current stream; inputs are resident in
+    HBM and a 256 MB buffer is overwritten between iterations to flush L2."""
+    from gen_worker_b200.modules import (build_svdq_int4_linear, build_w8a8_int8_linear,
+                                         quantize_int4_rows, quantize_int8_rows)
+    from gen_worker_b200 import ops
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    rows = []
+    for kind, m, k, n, r, gelu in CASES[name]:
+        x = torch.randn(m, k, generator=g, device=dev)
+        x[:, torch.randperm(k, generator=g, device=dev)[:max(1, round(0.01 * k))]] *= 20
+        w = torch.randn(n, k, generator=g, device=dev) * 0.02
+        b = (torch.randn(n, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        if kind == "w4a4":
+            sm = (x.abs().amax(0).clamp(min=1e-5).sqrt() / w.abs().amax(0).clamp(min=1e-5).sqrt()
+                  ).to(torch.bfloat16)
+            pk, sc = quantize_int4_rows(w * sm.float())
+            mod = build_svdq_int4_linear(
+                {"weight": pk, "weight_scale": sc, "smooth_factor": sm,
+                 "proj_down": (torch.randn(k, r, generator=g, device=dev) * 0.02).to(torch.bfloat16),
+                 "proj_up": (torch.randn(n, r, generator=g, device=dev) * 0.02).to(torch.bfloat16),
+                 "bias": b}, gelu=gelu, device=dev)
+        else:
+            q, s_ = quantize_int8_rows(w)
+            mod = build_w8a8_int8_linear({"weight": q, "weight_scale": s_, "bias": b},
+                                         gelu=gelu, device=dev)
+        xb = x.to(torch.bfloat16)
+        del x, w
+        tot, gemm = 0.0, 0.0
+        for it in range(warmup + steps):
+            flush.fill_(it & 0xFF)
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            e[0].record()
+            if kind == "w4a4":
+                p = mod.prepare()
+                c, a, la = ops.svdq_w4a4_quant(xb, mod.smooth_factor, p["proj_down_t"])
+                e[1].record()
+                ops.svdq_w4a4_gemm(c, a, mod.weight, p["w_scale_gn"], la, p["proj_up_pad"],
+                                   mod.bias.detach(), gelu)
+            else:
+                q, s_ = ops.w8a8_quant(xb)
+                e[1].record()
+                ops.w8a8_gemm(q, s_, mod.weight, mod.weight_scale.reshape(-1),
+                              mod.bias.detach(), gelu)
+            e[2].record()
+            torch.cuda.synchronize()
+            if it >= warmup:
+                tot += e[0].elapsed_time(e[2]) / steps
+                gemm += e[1].elapsed_time(e[2]) / steps
+        ops_ = 2.0 * m * n * k
+        act_bytes = m * k * 2 + (m * k // 2 + m * k // 32 + m * r * 2 if kind == "w4a4"
+                                 else m * k + m * 4)
+        rows.append({"kind": kind, "M": m, "K": k, "N": n, "rank": r, "gelu": gelu,
+                     "ms": tot, "gemm_ms": gemm, "act_ms": tot - gemm,
+                     "tops": ops_ / (tot / 1e3) / 1e12, "gemm_tops": ops_ / (gemm / 1e3) / 1e12,
+                     "act_gbs": act_bytes / ((tot - gemm) / 1e3) / 1e9})
+    total_ms = sum(r_["ms"] for r_ in rows)
+    total_ops = sum(2.0 * r_["M"] * r_["N"] * r_["K"] for r_ in rows)
+    tops = total_ops / (total_ms / 1e3) / 1e12
+    return {"metric": f"{name} quantized-linear effective TOPS", "value": tops,
+            "unit": "TOP/s", "ms_total": total_ms, "peak_int8_tops": INT8_DENSE_PEAK_TOPS,
+            "frac_int8_peak": tops / INT8_DENSE_PEAK_TOPS,
+            "linears": rows, "steps": steps, "warmup": warmup,
+            "l2": "256 MB flush between iterations"}
+
+
 # --------------------------------------------------------------------------- main
 def main() -> int:
     ap = argparse.ArgumentParser()
@@ -255,8 +335,16 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", choices=sorted(CASES), default=None,
+                    help="time one BASELINE config's linears instead of the cfg4 stack")
     args = ap.parse_args()
     world, rank, local = dist_env()
+
+    if args.case is not None:
+        from gen_worker_b200 import native
+        native.require()
+        print(json.dumps(run_case(args.case, args.steps, args.warmup)))
+        return 0
 
     if args.impl == "reference":
         if rank != 0:

@@ -171,20 +171,27 @@ constexpr int PSTAGE_BYTES = PA_BYTES + PB_BYTES;
 constexpr int UA_BYTES = kBM * kBK;        // 16 KB
 constexpr int UB_BYTES = BN * kBK;         // 16 KB
 constexpr int USTAGE_BYTES = UA_BYTES + UB_BYTES;
-constexpr int SMEM_BYTES = USTAGES * USTAGE_BYTES + PSTAGES * PSTAGE_BYTES + 1024 + 512;
+constexpr int SSTAGES = 8;                 // weight-scale ring (one k-block = 2 groups each)
+constexpr int SSTAGE_BYTES = 2 * BN * 4;   // f32 [2 groups][BN]
+constexpr int SMEM_BYTES = USTAGES * USTAGE_BYTES + PSTAGES * PSTAGE_BYTES +
+                           SSTAGES * SSTAGE_BYTES + 1024 + 512;
 constexpr int TMEM_COLS = 256;             // two s32 group buffers of BN columns
 constexpr int UNPACK_THREADS = 64;         // warps 2-3
+constexpr int EPI_WARPS = 8;               // warps 4-11
+constexpr int EC = BN / 2;                 // columns per epilogue warp
+constexpr int THREADS = 128 + 32 * EPI_WARPS;
 }  // namespace w4
 
-// 8 packed nibbles (element 0 in the low nibble) -> 8 sign-extended int8.
+// 8 packed nibbles -> 8 int8 holding 16*q each: the nibble is moved to the
+// high half of its byte, which makes the byte the two's-complement value 16*q
+// with no sign extension. Output order is (q0 q2 q4 q6)(q1 q3 q5 q7): the
+// same k permutation inside every 8-element block of A and of B, which
+// leaves each 64-group dot product unchanged; the MMA then sums 256*v, exact
+// in s32, and the 1/256 is folded into the activation scale (a power of two,
+// so every product and rounding is unchanged).
 __device__ __forceinline__ void unpack8(uint32_t w, uint32_t& o0, uint32_t& o1) {
-  uint32_t a = w & 0x0F0F0F0Fu;          // elements 0,2,4,6
-  uint32_t b = (w >> 4) & 0x0F0F0F0Fu;   // elements 1,3,5,7
-  // per-byte sign extension of a 4-bit value without cross-byte carries
-  a = ((a ^ 0x08080808u) + 0x78787878u) ^ 0x80808080u;
-  b = ((b ^ 0x08080808u) + 0x78787878u) ^ 0x80808080u;
-  o0 = __byte_perm(a, b, 0x5140);
-  o1 = __byte_perm(a, b, 0x7362);
+  o0 = (w << 4) & 0xF0F0F0F0u;
+  o1 = w & 0xF0F0F0F0u;
 }
 
 // Unpack `rows` rows of 64 packed bytes (row-major, no swizzle) into rows of
@@ -205,9 +212,10 @@ __device__ __forceinline__ void unpack_tile(const uint8_t* __restrict__ src, uin
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(w4::THREADS, 1)
 gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmUP,
+                 const __grid_constant__ CUtensorMap tmWS,
                  const __half* __restrict__ a_scale, const float* __restrict__ w_scale_gn,
                  const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out,
                  int32_t* __restrict__ partials, int M, int N, int K, int rank_pad, int gelu) {
@@ -217,14 +225,17 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                                              ~uintptr_t(1023));
   uint8_t* ustage = smem;
   uint8_t* pstage = smem + USTAGES * USTAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pstage + PSTAGES * PSTAGE_BYTES);
+  uint8_t* sstage = pstage + PSTAGES * PSTAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sstage + SSTAGES * SSTAGE_BYTES);
   uint64_t* p_full = bars;
   uint64_t* p_empty = p_full + PSTAGES;
   uint64_t* u_full = p_empty + PSTAGES;
   uint64_t* u_empty = u_full + USTAGES;
   uint64_t* acc_full = u_empty + USTAGES;   // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* s_full = acc_empty + 2;         // [SSTAGES]
+  uint64_t* s_empty = s_full + SSTAGES;     // [SSTAGES]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_empty + SSTAGES);
   uint32_t* unpack_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -237,7 +248,8 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   if (threadIdx.x == 0) {
     for (int i = 0; i < PSTAGES; ++i) { mbar_init(&p_full[i], 1); mbar_init(&p_empty[i], 1); }
     for (int i = 0; i < USTAGES; ++i) { mbar_init(&u_full[i], 1); mbar_init(&u_empty[i], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], EPI_WARPS); }
+    for (int i = 0; i < SSTAGES; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_empty[i], EPI_WARPS); }
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -263,6 +275,13 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       mbar_arrive_expect_tx(&p_full[s], PSTAGE_BYTES);
       tma_load_2d(dst, &tmA, &p_full[s], kb * (kBK / 2), m0);
       tma_load_2d(dst + PA_BYTES, &tmB, &p_full[s], kb * (kBK / 2), n0);
+      if (!dump) {
+        // this k-block's two groups of weight scales, f32 [2][BN]
+        const int ss = kb % SSTAGES;
+        if (!mbar_wait(&s_empty[ss], ((kb / SSTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
+        mbar_arrive_expect_tx(&s_full[ss], SSTAGE_BYTES);
+        tma_load_2d(sstage + ss * SSTAGE_BYTES, &tmWS, &s_full[ss], n0, 2 * kb);
+      }
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------------- MMA
@@ -272,7 +291,7 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     if (has_lr) {
       // group slot 0 <- la · proj_upᵀ (f32), into accumulator buffer 0
       if (!mbar_wait(&u_full[0], 0, GWB_ERR_TIMEOUT_MMA)) ok = false;
-      if (ok && !mbar_wait(&acc_empty[0], 1, GWB_ERR_TIMEOUT_MMA)) ok = false;
+      if (ok && !mbar_wait(&acc_empty[0], 0, GWB_ERR_TIMEOUT_MMA)) ok = false;
       if (ok) {
         tc_fence_after();
         const uint32_t a_base = smem_u32(ustage), b_base = a_base + UA_BYTES;
@@ -293,10 +312,13 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       for (int gs = 0; gs < 2 && ok; ++gs) {
         const int gi = kb * 2 + gs + has_lr;
         const int b = gi & 1;
-        if (!mbar_wait(&acc_empty[b], ((gi >> 1) & 1) ^ 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
+        // completion #(gi>>1) of acc_empty[b]: #0 is the epilogue's initial
+        // magic-bias fill, #j the drain (+ re-bias) of the buffer's use j-1
+        if (!mbar_wait(&acc_empty[b], (gi >> 1) & 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d = tmem + b * BN;
-        mma_i8(d, sdesc_k128(a_base + 64 * gs), sdesc_k128(b_base + 64 * gs), idesc, 0u);
+        // accumulate onto the magic bias already in TMEM
+        mma_i8(d, sdesc_k128(a_base + 64 * gs), sdesc_k128(b_base + 64 * gs), idesc, 1u);
         mma_i8(d, sdesc_k128(a_base + 64 * gs + 32), sdesc_k128(b_base + 64 * gs + 32), idesc, 1u);
         mma_commit(&acc_full[b]);
       }
@@ -331,75 +353,132 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     }
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- epilogue
-    const int q = warp - 4;
+    // Each s32 group buffer is pre-filled with the bits of 1.5*2^23
+    // (0x4B400000); the MMA accumulates the group sum v onto it, so the word
+    // read back is the float 1.5*2^23 + v exactly (|v| <= 64*64 < 2^22) and
+    // float(v) costs one subtraction instead of an I2F conversion (I2F runs
+    // on the narrow conversion pipe). After draining, the epilogue writes the
+    // bias back for the buffer's next use. Eight epilogue warps: warp 4+i
+    // reads lane quarter i%4 and column slice (i/4)*EC.
+    const int q = warp & 3;                  // TMEM lane quarter = tile rows 32q..
+    const int cb = ((warp - 4) >> 2) * EC;   // this warp's column slice
     const int row = m0 + 32 * q + lane;
     const bool rv = row < M;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-    float acc[BN];
+    constexpr uint32_t kMagic = 0x4B400000u;
+    const float kMagicF = 12582912.0f;
+    uint32_t bias16[16];
 #pragma unroll
-    for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+    for (int j = 0; j < 16; ++j) bias16[j] = kMagic;
+#pragma unroll
+    for (int bb = 0; bb < 2; ++bb)
+#pragma unroll
+      for (int c = 0; c < EC; c += 16) tmem_st16(lane_base + bb * BN + cb + c, bias16);
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) { mbar_arrive(&acc_empty[0]); mbar_arrive(&acc_empty[1]); }
+
+    float2 acc[EC / 2];
+#pragma unroll
+    for (int j = 0; j < EC / 2; ++j) acc[j] = make_float2(0.f, 0.f);
+    const float2 negm = make_float2(-kMagicF, -kMagicF);
     const int total = G + has_lr;
     bool ok = true;
+    // the activation scale of the next group is fetched one group ahead
+    float sa_next = (rv && !dump) ? __half2float(a_scale[(size_t)row * G]) * (1.0f / 256.0f) : 0.f;
     for (int gi = 0; gi < total; ++gi) {
       const int b = gi & 1;
       if (!mbar_wait(&acc_full[b], (gi >> 1) & 1, GWB_ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t col0 = lane_base + b * BN;
+      const uint32_t col0 = lane_base + b * BN + cb;
       if (has_lr && gi == 0) {
+        // f32 low-rank product la·proj_upᵀ seeds the accumulator
 #pragma unroll
-        for (int c = 0; c < BN; c += 16) {
+        for (int c = 0; c < EC; c += 16) {
           uint32_t v[16];
           tmem_ld16(col0 + c, v);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[c + j] = __uint_as_float(v[j]);
+          for (int j = 0; j < 16; j += 2)
+            acc[(c + j) / 2] = make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+          tmem_st16(col0 + c, bias16);
+        }
+      } else if (dump) {
+        const int g = gi - has_lr;
+#pragma unroll
+        for (int c = 0; c < EC; c += 16) {
+          uint32_t v[16];
+          tmem_ld16(col0 + c, v);
+          tmem_wait_ld();
+          tmem_st16(col0 + c, bias16);
+          if (rv) {
+            // the MMA summed 256*v (operands hold 16*q)
+            uint4* dp = reinterpret_cast<uint4*>(partials + ((size_t)g * M + row) * N + n0 + cb + c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              dp[j] = make_uint4((uint32_t)((int32_t)(v[4 * j] - kMagic) >> 8),
+                                 (uint32_t)((int32_t)(v[4 * j + 1] - kMagic) >> 8),
+                                 (uint32_t)((int32_t)(v[4 * j + 2] - kMagic) >> 8),
+                                 (uint32_t)((int32_t)(v[4 * j + 3] - kMagic) >> 8));
+          }
         }
       } else {
         const int g = gi - has_lr;
-        if (dump) {
+        const float sa = sa_next;
+        if (rv && g + 1 < G)
+          sa_next = __half2float(a_scale[(size_t)row * G + g + 1]) * (1.0f / 256.0f);
+        const float2 sa2 = make_float2(sa, sa);
+        const int ss = (g >> 1) % SSTAGES;
+        if ((g & 1) == 0 &&
+            !mbar_wait(&s_full[ss], ((g >> 1) / SSTAGES) & 1, GWB_ERR_TIMEOUT_EPILOGUE)) {
+          ok = false;
+          break;
+        }
+        const float* wsg = reinterpret_cast<const float*>(sstage + ss * SSTAGE_BYTES) + (g & 1) * BN + cb;
+        uint32_t v[2][16];
+        tmem_ld16(col0, v[0]);
+        tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < BN; c += 16) {
-            uint32_t v[16];
-            tmem_ld16(col0 + c, v);
-            tmem_wait_ld();
-            if (rv) {
-              uint4* dp = reinterpret_cast<uint4*>(partials + ((size_t)g * M + row) * N + n0 + c);
+        for (int c = 0; c < EC / 16; ++c) {
+          if (c + 1 < EC / 16) tmem_ld16(col0 + (c + 1) * 16, v[(c + 1) & 1]);
 #pragma unroll
-              for (int j = 0; j < 4; ++j)
-                dp[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            }
+          for (int j = 0; j < 16; j += 4) {
+            const float4 ws = *reinterpret_cast<const float4*>(wsg + c * 16 + j);
+            const float2 s01 = __fmul2_rn(sa2, make_float2(ws.x, ws.y));
+            const float2 s23 = __fmul2_rn(sa2, make_float2(ws.z, ws.w));
+            const float2 f01 = __fadd2_rn(
+                make_float2(__uint_as_float(v[c & 1][j]), __uint_as_float(v[c & 1][j + 1])), negm);
+            const float2 f23 = __fadd2_rn(
+                make_float2(__uint_as_float(v[c & 1][j + 2]), __uint_as_float(v[c & 1][j + 3])),
+                negm);
+            acc[(c * 16 + j) / 2] = __ffma2_rn(f01, s01, acc[(c * 16 + j) / 2]);
+            acc[(c * 16 + j) / 2 + 1] = __ffma2_rn(f23, s23, acc[(c * 16 + j) / 2 + 1]);
           }
-        } else {
-          const float sa = rv ? __half2float(a_scale[(size_t)row * G + g]) : 0.f;
-          const float* wsg = w_scale_gn + (size_t)g * N + n0;
-#pragma unroll
-          for (int c = 0; c < BN; c += 16) {
-            uint32_t v[16];
-            tmem_ld16(col0 + c, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              const float4 ws = __ldg(reinterpret_cast<const float4*>(wsg + c + j));
-              acc[c + j + 0] = fmaf((float)(int)v[j + 0], sa * ws.x, acc[c + j + 0]);
-              acc[c + j + 1] = fmaf((float)(int)v[j + 1], sa * ws.y, acc[c + j + 1]);
-              acc[c + j + 2] = fmaf((float)(int)v[j + 2], sa * ws.z, acc[c + j + 2]);
-              acc[c + j + 3] = fmaf((float)(int)v[j + 3], sa * ws.w, acc[c + j + 3]);
-            }
-          }
+          tmem_st16(col0 + c * 16, bias16);
+          tmem_wait_ld();
         }
       }
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (lane == 0) {
+        mbar_arrive(&acc_empty[b]);
+        const int g = gi - has_lr;
+        if (!dump && g >= 0 && (g & 1) == 1) mbar_arrive(&s_empty[(g >> 1) % SSTAGES]);
+      }
     }
     if (ok && !dump && rv) {
 #pragma unroll
-      for (int c = 0; c < BN; c += 8) {
+      for (int c = 0; c < EC; c += 8) {
         float f[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) f[j] = acc[c + j];
+        for (int j = 0; j < 8; j += 2) {
+          f[j] = acc[(c + j) / 2].x;
+          f[j + 1] = acc[(c + j) / 2].y;
+        }
         if (bias != nullptr) {
-          const uint4 bw = __ldg(reinterpret_cast<const uint4*>(bias + n0 + c));
+          const uint4 bw = __ldg(reinterpret_cast<const uint4*>(bias + n0 + cb + c));
           const uint32_t w[4] = {bw.x, bw.y, bw.z, bw.w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -411,7 +490,7 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
           for (int j = 0; j < 8; ++j) f[j] = gelu_tanh(f[j]);
         }
-        *reinterpret_cast<uint4*>(out + (size_t)row * N + n0 + c) =
+        *reinterpret_cast<uint4*>(out + (size_t)row * N + n0 + cb + c) =
             make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
                        pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
       }
@@ -497,7 +576,7 @@ int launch_gemm_w4a4(const W4A4Args& a, cudaStream_t st) {
       (a.up && !al16(a.up)) || (a.partials && !al16(a.partials)))
     return GWB_E_ALIGN;
   if (!a.partials && !a.out) return GWB_E_SHAPE;
-  CUtensorMap tA, tB, tLA, tUP;
+  CUtensorMap tA, tB, tLA, tUP, tWS;
   int rc = make_tmap(&tA, a.a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K / 2, a.M, kBK / 2,
                      kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
@@ -506,6 +585,12 @@ int launch_gemm_w4a4(const W4A4Args& a, cudaStream_t st) {
   if (rc) return rc;
   tLA = tA;
   tUP = tB;
+  tWS = tA;
+  if (!a.partials) {
+    rc = make_tmap(&tWS, a.w_scale_gn, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.N, a.K / 64, w4::BN,
+                   2, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
   if (a.rank_pad > 0 && !a.partials) {
     rc = make_tmap(&tLA, a.la, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.rank_pad, a.M, 64, kBM,
                    CU_TENSOR_MAP_SWIZZLE_128B);
@@ -521,8 +606,8 @@ int launch_gemm_w4a4(const W4A4Args& a, cudaStream_t st) {
     attr = true;
   }
   dim3 grid(a.N / w4::BN, (a.M + kBM - 1) / kBM);
-  gemm_w4a4_kernel<<<grid, kThreads, w4::SMEM_BYTES, st>>>(
-      tA, tB, tLA, tUP, static_cast<const __half*>(a.a_scale), a.w_scale_gn,
+  gemm_w4a4_kernel<<<grid, w4::THREADS, w4::SMEM_BYTES, st>>>(
+      tA, tB, tLA, tUP, tWS, static_cast<const __half*>(a.a_scale), a.w_scale_gn,
       static_cast<const __nv_bfloat16*>(a.bias), static_cast<__nv_bfloat16*>(a.out), a.partials,
       a.M, a.N, a.K, a.partials ? 0 : a.rank_pad, a.gelu);
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
