@@ -1,0 +1,100 @@
+"""Host-side logic without a GPU: library load + exported symbols, producer
+rules vs the oracle, load-time repacks, op validation."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from oracle import svdq_oracle as O
+from gen_worker_b200 import native, ops
+from gen_worker_b200.modules import (SvdqInt4Linear, W8A8Int8Linear, SvdqB200LayoutError,
+                                     quantize_int4_rows, quantize_int8_rows, swap_linears,
+                                     build_svdq_int4_linear)
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _declared_symbols():
+    text = (ROOT / "include" / "gwb200.h").read_text()
+    return sorted(set(re.findall(r"\b(gwb_\w+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = native.lib()
+    declared = _declared_symbols()
+    assert declared, "no declarations found"
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert set(declared) == set(native.EXPORTED)
+    assert "sm_100a" in native.build_info()
+
+
+def test_status_strings():
+    assert native.status_string(0) == "success"
+    assert "aligned" in native.status_string(2)
+
+
+def test_without_gpu_the_ops_refuse_loudly():
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    with pytest.raises(ops.SvdqB200Error):
+        ops.svdq_w4a4_quant(torch.zeros(4, 128, dtype=torch.bfloat16), None, None)
+    assert native.extension_reason() is not None
+
+
+def test_entry_points_reject_bad_shapes_before_touching_memory():
+    lib = native.lib()
+    # K not a multiple of 128 / N not a multiple of 128 -> GWB_E_SHAPE (1), no launch
+    assert lib.gwb_svdq_w4a4_gemm(None, None, None, None, None, None, None, 4, 128, 100, 0, 0,
+                                  None, None) == 1
+    assert lib.gwb_svdq_w4a4_gemm(None, None, None, None, None, None, None, 4, 100, 128, 0, 0,
+                                  None, None) == 1
+    assert lib.gwb_svdq_w4a4_quant(None, None, None, 4, 128, 24, None, None, None, None) == 1
+    assert lib.gwb_w8a8_linear(None, None, None, None, 4, 128, 100, 0, None, None, None, None) == 1
+    # M == 0 is a no-op success
+    assert lib.gwb_svdq_w4a4_linear(*([None] * 7), 0, 128, 128, 0, 0, *([None] * 5)) == 0
+
+
+def test_producer_matches_oracle_rules():
+    w = O.synth_activation(16, 256, seed=1).float()
+    p, s = quantize_int4_rows(w)
+    op, os_ = O.quant_int4(w)
+    assert torch.equal(p, op) and torch.equal(s, os_)
+    q8, s8 = quantize_int8_rows(w)
+    oq, osc = O.quant_int8_rows(w)
+    assert torch.equal(q8, oq) and torch.equal(s8, osc)
+
+
+def test_prepare_repacks_layouts():
+    ws = torch.rand(256, 4).to(torch.float16)
+    down = torch.randn(256, 20).to(torch.bfloat16)
+    up = torch.randn(128, 20).to(torch.bfloat16)
+    p = ops.prepare_w4a4_weights(ws, down, up)
+    assert p["w_scale_gn"].shape == (4, 256) and p["w_scale_gn"].dtype == torch.float32
+    assert p["proj_down_t"].shape == (32, 256) and torch.all(p["proj_down_t"][20:] == 0)
+    assert torch.equal(p["proj_down_t"][:20], down.t())
+    assert p["proj_up_pad"].shape == (128, 32) and torch.all(p["proj_up_pad"][:, 20:] == 0)
+    with pytest.raises(ops.SvdqB200Error):
+        ops.prepare_w4a4_weights(ws, torch.zeros(256, 80), torch.zeros(128, 80))
+
+
+def test_module_surface_and_swap():
+    with pytest.raises(SvdqB200LayoutError):
+        SvdqInt4Linear(100, 128, rank=0, bias=False)
+    with pytest.raises(SvdqB200LayoutError):
+        W8A8Int8Linear(128, 128, bias=False)
+    m = SvdqInt4Linear(256, 128, rank=32, bias=True)
+    names = {n for n, _ in m.named_buffers()} | {n for n, _ in m.named_parameters()}
+    assert {"weight", "weight_scale", "smooth_factor", "proj_down", "proj_up", "bias"} <= names
+    assert m.layout == "int4-g64-lownib"
+    model = torch.nn.Sequential(torch.nn.Linear(256, 128), torch.nn.Linear(128, 128))
+    x = O.synth_activation(4, 256, seed=0)
+    L = O.synth_svdq_layer(256, 128, 32, seed=1, x_calib=x)
+    mod = build_svdq_int4_linear({"weight": L["w_packed"], "weight_scale": L["w_scale"],
+                                  "smooth_factor": L["smooth"], "proj_down": L["proj_down"],
+                                  "proj_up": L["proj_up"], "bias": L["bias"]}, device="cpu")
+    assert swap_linears(model, {"0": mod}) == 1 and model[0] is mod
+    with pytest.raises(SvdqB200LayoutError):
+        swap_linears(model, {"7": mod})
