@@ -36,10 +36,11 @@ def _rank(rank, world, port, q):
     m = M // world
     y = O.svdq_int4_linear(x[rank * m:(rank + 1) * m], L["smooth"], L["w_packed"], L["w_scale"],
                            L["proj_down"], L["proj_up"], L["bias"])["y"]
-    parts = [torch.empty_like(y.view(torch.int16)) for _ in range(world)]
-    dist.all_gather(parts, y.view(torch.int16).contiguous())
+    yf = y.float().contiguous()            # bf16 -> f32 is exact; gloo has no bf16
+    parts = [torch.empty_like(yf) for _ in range(world)]
+    dist.all_gather(parts, yf)
     if rank == 0:
-        q.put(torch.cat(parts).view(torch.bfloat16))
+        q.put(torch.cat(parts).to(torch.bfloat16))
     dist.barrier()
     dist.destroy_process_group()
 
