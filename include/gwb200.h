@@ -70,6 +70,21 @@ int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_dow
                          int gelu, void* codes, void* ascale, void* la, void* out,
                          void* stream);
 
+/* No counterpart in the reference. The same computation as
+ * gwb_svdq_w4a4_linear for callers that cannot allocate device memory (their
+ * device memory belongs to another framework's pool or a fixed start-up
+ * budget, or their serving loop forbids cudaMalloc once running): the
+ * intermediates live in a 32 MiB array inside the library, held on every GPU
+ * that loads it until exit. Needs M*(K/2) + M*(K/64)*2 + M*rank_pad*2 bytes
+ * (each part rounded up to 256); larger calls return GWB_E_CAPACITY. Calls
+ * share the array: work from calls that overlap on the GPU races. The first
+ * call on a device looks up the array's address; make it before any stream
+ * capture. Allocates nothing. */
+int gwb_svdq_w4a4_linear_noalloc(const void* x, const void* smooth, const void* proj_down_t,
+                                 const void* w_codes, const float* w_scale_gn,
+                                 const void* proj_up, const void* bias, int64_t M, int64_t N,
+                                 int64_t K, int rank_pad, int gelu, void* out, void* stream);
+
 /* Replaces the W8A8 activation quantiser `_quant_src` rowwise branch
  * (reference src/gen_worker/models/w8a8.py:261-273): per-token symmetric
  * INT8, q s8 [M, K], scale f32 [M]. */

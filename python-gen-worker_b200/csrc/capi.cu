@@ -172,3 +172,7 @@ const char* gwb_status_string(int status) {
 }
 
 }  // extern "C"
+
+// The no-allocation variant of gwb_svdq_w4a4_linear (its own file: the scratch
+// array and the host code that looks up its address live together).
+#include "noalloc.cu"

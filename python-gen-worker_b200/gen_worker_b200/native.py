@@ -37,6 +37,9 @@ _SIGNATURES = {
     "gwb_svdq_w4a4_linear": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                              c_void_p, c_i64, c_i64, c_i64, c_int, c_int, c_void_p, c_void_p,
                              c_void_p, c_void_p, c_void_p],
+    "gwb_svdq_w4a4_linear_noalloc": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                     c_void_p, c_void_p, c_i64, c_i64, c_i64, c_int, c_int,
+                                     c_void_p, c_void_p],
     "gwb_w8a8_quant": [c_void_p, c_i64, c_i64, c_void_p, c_void_p, c_void_p],
     "gwb_w8a8_gemm": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64,
                       c_int, c_void_p, c_void_p],
