@@ -184,7 +184,7 @@ class GemmTimer:
         codes, ascale, la = ops.svdq_w4a4_quant(x2, mod.smooth_factor, p["proj_down_t"])
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        y = ops.svdq_w4a4_gemm(codes, ascale, mod.weight, p["w_scale_gn"], la,
+        y = ops.svdq_w4a4_gemm(codes, ascale, p["w_q8"], p["w_scale_gn"], la,
                                p["proj_up_pad"], mod.bias.detach(), mod.gelu)
         e.record()
         self.pairs.append((s, e, 2.0 * x2.shape[0] * mod.in_features * mod.out_features))
@@ -298,7 +298,7 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
                 p = mod.prepare()
                 c, a, la = ops.svdq_w4a4_quant(xb, mod.smooth_factor, p["proj_down_t"])
                 e[1].record()
-                ops.svdq_w4a4_gemm(c, a, mod.weight, p["w_scale_gn"], la, p["proj_up_pad"],
+                ops.svdq_w4a4_gemm(c, a, p["w_q8"], p["w_scale_gn"], la, p["proj_up_pad"],
                                    mod.bias.detach(), gelu)
             else:
                 q, s_ = ops.w8a8_quant(xb)

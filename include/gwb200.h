@@ -8,10 +8,14 @@
  *   x            bf16 [M, K]
  *   smooth       bf16 [K] (or NULL)
  *   proj_down_t  bf16 [rank_pad, K]   (L1 transposed; rows >= rank are zero)
- *   codes        u8   [M, K/2]        INT4 two's-complement nibbles, even k low
+ *   codes        u8   [M, K/2]        INT4 sign-magnitude nibbles (bit 3 = sign,
+ *                                     bits 0-2 = |q|, q in -7..7), even k low
  *   ascale       f16  [M, K/64]       one scale per 64-group
  *   la           bf16 [M, rank_pad]   x·L1 on raw x
- *   w_codes      u8   [N, K/2], w_scale_gn f32 [K/64, N], proj_up bf16 [N, rank_pad]
+ *   w_codes      u8   [N, K/2] packed weight (same nibble format as codes)
+ *   w_q8         u8   [N, K] expanded weight: gwb_svdq_w4a4_weight_expand(w_codes)
+ *   w_scale_gn   f32  [K/64, N] (fp16-representable values, |w_scale| <= 127)
+ *   proj_up      bf16 [N, rank_pad]
  *   bias         bf16 [N] (or NULL); out bf16 [M, N]
  * Constraints: K % 128 == 0; N % 128 == 0 (W4A4) / N % 256 == 0 (W8A8);
  * rank_pad in {0, 16, 32, 48, 64}.
@@ -44,12 +48,20 @@ int gwb_svdq_w4a4_quant(const void* x, const void* smooth, const void* proj_down
                         int64_t M, int64_t K, int rank_pad,
                         void* codes, void* ascale, void* la, void* stream);
 
+/* Load-time weight repack (the counterpart of the reference's load-time
+ * `to_buffers` / `pack_e2m1` repacks, src/gen_worker/models/svdq_layout.py:
+ * 473-483): packed INT4 w_codes u8 [N, K/2] -> w_q8 u8 [N, K], each code as
+ * an e4m3 integer, in the within-8-element order the GEMM's operand unpack
+ * uses. */
+int gwb_svdq_w4a4_weight_expand(const void* w_codes, int64_t N, int64_t K, void* w_q8,
+                                void* stream);
+
 /* Replaces `cozy_gen_worker::svdq_gemm_w4a4_lora(qa, sa, wq_kn, ws, s2,
  * second, lora_act, up, bias)` (reference svdq_fused.py:379-383, kernel
  * :180-238) and the baseline chain `_gemm_w4a4` + scale + low-rank + bias of
  * `SvdqLinear.forward` (svdq_native.py:148-155). gelu != 0 applies
  * GELU(tanh) after the bias. */
-int gwb_svdq_w4a4_gemm(const void* codes, const void* ascale, const void* w_codes,
+int gwb_svdq_w4a4_gemm(const void* codes, const void* ascale, const void* w_q8,
                        const float* w_scale_gn, const void* la, const void* proj_up,
                        const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
                        int gelu, void* out, void* stream);
@@ -58,14 +70,14 @@ int gwb_svdq_w4a4_gemm(const void* codes, const void* ascale, const void* w_code
  * the reference's GEMM forms internally, svdq_fused.py:213-222): the same
  * tcgen05 GEMM with the epilogue replaced by a dump of every 64-group s32
  * partial sum, partials s32 [K/64, M, N]. */
-int gwb_svdq_w4a4_group_partials(const void* codes, const void* w_codes, int64_t M, int64_t N,
+int gwb_svdq_w4a4_group_partials(const void* codes, const void* w_q8, int64_t M, int64_t N,
                                  int64_t K, int32_t* partials, void* stream);
 
 /* Whole SvdqLinear forward (reference svdq_native.py:140-156): quantise +
  * GEMM. The caller supplies the scratch buffers codes / ascale / la (sizes
  * as above). */
 int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_down_t,
-                         const void* w_codes, const float* w_scale_gn, const void* proj_up,
+                         const void* w_q8, const float* w_scale_gn, const void* proj_up,
                          const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
                          int gelu, void* codes, void* ascale, void* la, void* out,
                          void* stream);
@@ -81,7 +93,7 @@ int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_dow
  * call on a device looks up the array's address; make it before any stream
  * capture. Allocates nothing. */
 int gwb_svdq_w4a4_linear_noalloc(const void* x, const void* smooth, const void* proj_down_t,
-                                 const void* w_codes, const float* w_scale_gn,
+                                 const void* w_q8, const float* w_scale_gn,
                                  const void* proj_up, const void* bias, int64_t M, int64_t N,
                                  int64_t K, int rank_pad, int gelu, void* out, void* stream);
 

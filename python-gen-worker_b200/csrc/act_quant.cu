@@ -1,6 +1,6 @@
 // Activation kernels (memory-bound, one pass over x):
 //  * act_int4_kernel: smoothing divide -> bf16, per-64-group symmetric INT4
-//    with fp16 scale, packed nibbles (even k in the low nibble), fused with the
+//    with fp16 scale, packed sign-magnitude nibbles (even k in the low nibble), fused with the
 //    rank-r low-rank down-projection la = x·L1 on RAW x (mma.sync bf16).
 //  * act_int8_kernel: per-token symmetric INT8 with fp32 scale.
 // Numerics follow the reference's quantiser structure
@@ -21,10 +21,12 @@ constexpr int kActWarps = 8;    // warps per CTA, splitting K round-robin
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// sign-magnitude nibble of clamp(rint(v/s), -7, 7): bit 3 = sign, bits 0-2 = |q|
 __device__ __forceinline__ uint32_t q4(float v, float s) {
   float q = rintf(__fdiv_rn(v, s));
-  q = fminf(fmaxf(q, -8.0f), 7.0f);
-  return static_cast<uint32_t>(static_cast<int>(q)) & 0xFu;
+  q = fminf(fmaxf(q, -7.0f), 7.0f);
+  const int qi = static_cast<int>(q);
+  return qi < 0 ? (8u | static_cast<uint32_t>(-qi)) : static_cast<uint32_t>(qi);
 }
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],

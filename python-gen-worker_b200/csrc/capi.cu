@@ -76,19 +76,19 @@ int gwb_svdq_w4a4_quant(const void* x, const void* smooth, const void* proj_down
                               rank_pad ? la : nullptr, (int)M, (int)K, rank_pad, S(stream));
 }
 
-int gwb_svdq_w4a4_gemm(const void* codes, const void* ascale, const void* w_codes,
+int gwb_svdq_w4a4_gemm(const void* codes, const void* ascale, const void* w_q8,
                        const float* w_scale_gn, const void* la, const void* proj_up,
                        const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
                        int gelu, void* out, void* stream) {
   if (M == 0) return GWB_SUCCESS;
   int rc = check_w4a4_shape(M, N, K, rank_pad);
   if (rc) return rc;
-  gwb::W4A4Args a{codes, ascale, w_codes, w_scale_gn, la, proj_up, bias, out, nullptr,
+  gwb::W4A4Args a{codes, ascale, w_q8, w_scale_gn, la, proj_up, bias, out, nullptr,
                   (int)M, (int)N, (int)K, rank_pad, gelu ? 1 : 0};
   return gwb::launch_gemm_w4a4(a, S(stream));
 }
 
-int gwb_svdq_w4a4_group_partials(const void* codes, const void* w_codes, int64_t M, int64_t N,
+int gwb_svdq_w4a4_group_partials(const void* codes, const void* w_q8, int64_t M, int64_t N,
                                  int64_t K, int32_t* partials, void* stream) {
   if (M == 0) return GWB_SUCCESS;
   int rc = check_w4a4_shape(M, N, K, 0);
@@ -96,13 +96,13 @@ int gwb_svdq_w4a4_group_partials(const void* codes, const void* w_codes, int64_t
   if ((K / 64) * M * N > (int64_t)1 << 31) return GWB_E_CAPACITY;
   // the partial dump path reads no scales; pass the codes pointer as a
   // 16-byte-aligned placeholder for the unused scale operands
-  gwb::W4A4Args a{codes, codes, w_codes, reinterpret_cast<const float*>(w_codes), nullptr,
+  gwb::W4A4Args a{codes, codes, w_q8, reinterpret_cast<const float*>(w_q8), nullptr,
                   nullptr, nullptr, nullptr, partials, (int)M, (int)N, (int)K, 0, 0};
   return gwb::launch_gemm_w4a4(a, S(stream));
 }
 
 int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_down_t,
-                         const void* w_codes, const float* w_scale_gn, const void* proj_up,
+                         const void* w_q8, const float* w_scale_gn, const void* proj_up,
                          const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
                          int gelu, void* codes, void* ascale, void* la, void* out,
                          void* stream) {
@@ -111,8 +111,15 @@ int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_dow
   if (rc) return rc;
   rc = gwb_svdq_w4a4_quant(x, smooth, proj_down_t, M, K, rank_pad, codes, ascale, la, stream);
   if (rc) return rc;
-  return gwb_svdq_w4a4_gemm(codes, ascale, w_codes, w_scale_gn, la, proj_up, bias, M, N, K,
+  return gwb_svdq_w4a4_gemm(codes, ascale, w_q8, w_scale_gn, la, proj_up, bias, M, N, K,
                             rank_pad, gelu, out, stream);
+}
+
+int gwb_svdq_w4a4_weight_expand(const void* w_codes, int64_t N, int64_t K, void* w_q8,
+                                void* stream) {
+  if (N == 0) return GWB_SUCCESS;
+  if (!fits_int(N) || !fits_int(K)) return GWB_E_SHAPE;
+  return gwb::launch_w4a4_weight_expand(w_codes, w_q8, N, K, S(stream));
 }
 
 int gwb_w8a8_quant(const void* x, int64_t M, int64_t K, void* q, void* scale, void* stream) {

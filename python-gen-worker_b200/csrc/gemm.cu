@@ -23,6 +23,16 @@
 #include "ptx.cuh"
 
 
+#ifdef GWB_TRACE
+// Optional pipeline trace (compile with -DGWB_TRACE): CTA (0,0) of the W4A4
+// GEMM records clock64() at each role's events; gwb_trace_read copies it out.
+__device__ long long gwb_trace[8][512];
+#define GWB_TRACE_AT(role, idx) do { if (blockIdx.x == 0 && blockIdx.y == 0 && (idx) < 512) \
+    gwb_trace[role][idx] = clock64(); } while (0)
+#else
+#define GWB_TRACE_AT(role, idx) do { } while (0)
+#endif
+
 namespace gwb {
 
 constexpr int kThreads = 256;
@@ -163,59 +173,115 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 // ======================================================================
 namespace w4 {
 constexpr int BN = 128;
-constexpr int PSTAGES = 4;                 // packed staging ring (TMA destination)
-constexpr int USTAGES = 3;                 // unpacked ring (MMA operands)
-constexpr int PA_BYTES = kBM * kBK / 2;    // 8 KB packed A
-constexpr int PB_BYTES = BN * kBK / 2;     // 8 KB packed B
-constexpr int PSTAGE_BYTES = PA_BYTES + PB_BYTES;
-constexpr int UA_BYTES = kBM * kBK;        // 16 KB
-constexpr int UB_BYTES = BN * kBK;         // 16 KB
-constexpr int USTAGE_BYTES = UA_BYTES + UB_BYTES;
-constexpr int SSTAGES = 8;                 // weight-scale ring (one k-block = 2 groups each)
-constexpr int SSTAGE_BYTES = 2 * BN * 4;   // f32 [2 groups][BN]
-constexpr int SMEM_BYTES = USTAGES * USTAGE_BYTES + PSTAGES * PSTAGE_BYTES +
-                           SSTAGES * SSTAGE_BYTES + 1024 + 512;
-constexpr int TMEM_COLS = 256;             // two s32 group buffers of BN columns
+constexpr int PSTAGES = 4;                 // packed A staging ring (TMA destination)
+constexpr int USTAGES = 4;                 // operand ring read by the MMA
+constexpr int PA_BYTES = kBM * kBK / 2;    // 8 KB packed A per k-block
+constexpr int UA_BYTES = kBM * kBK;        // 16 KB e4m3 A (unpacked here)
+constexpr int UB_BYTES = BN * kBK;         // 16 KB e4m3 B (TMA from the expanded weight)
+// Scale operands of one group: A_s [128 rows x 16 k] and B_s [BN x 16 k] f16,
+// no-swizzle K-major core-matrix layout, only k = 0 non-zero.
+constexpr int SA_BYTES = kBM * 16 * 2;     // 4 KB
+constexpr int SB_BYTES = BN * 16 * 2;      // 4 KB
+constexpr int SGROUP_BYTES = SA_BYTES + SB_BYTES;
+constexpr int USTAGE_BYTES = UA_BYTES + UB_BYTES + 2 * SGROUP_BYTES;   // 48 KB
+constexpr int SMEM_BYTES = USTAGES * USTAGE_BYTES + PSTAGES * PA_BYTES + 1024 + 512;
+// TMEM: [0, 2*BN) f32 group sums V0/V1, [2*BN, 4*BN) f32 scale products S0/S1
+constexpr int TMEM_COLS = 512;
 constexpr int UNPACK_THREADS = 64;         // warps 2-3
 constexpr int EPI_WARPS = 8;               // warps 4-11
 constexpr int EC = BN / 2;                 // columns per epilogue warp
 constexpr int THREADS = 128 + 32 * EPI_WARPS;
+// The weight side holds q as an e4m3 integer and the activation side q*2^-9
+// (an e4m3 subnormal), so each group sum is 2^-9 * v; B_s carries
+// w_scale * 2^9 so that S = a_scale * w_scale * 2^9 undoes it exactly.
+constexpr float kWScaleMul = 512.0f;
 }  // namespace w4
 
-// 8 packed nibbles -> 8 int8 holding 16*q each: the nibble is moved to the
-// high half of its byte, which makes the byte the two's-complement value 16*q
-// with no sign extension. Output order is (q0 q2 q4 q6)(q1 q3 q5 q7): the
-// same k permutation inside every 8-element block of A and of B, which
-// leaves each 64-group dot product unchanged; the MMA then sums 256*v, exact
-// in s32, and the 1/256 is folded into the activation scale (a power of two,
-// so every product and rounding is unchanged).
-__device__ __forceinline__ void unpack8(uint32_t w, uint32_t& o0, uint32_t& o1) {
-  o0 = (w << 4) & 0xF0F0F0F0u;
-  o1 = w & 0xF0F0F0F0u;
+static_assert(w4::SMEM_BYTES <= 232448, "W4A4 shared memory exceeds 227 KB");
+
+// 8 sign-magnitude nibbles (element 0 in the low nibble of byte 0) -> 8 e4m3
+// bytes s000_0mmm = (-1)^s * |q| * 2^-9 (e4m3 subnormals; exact). Output
+// order (q0 q2 q4 q6)(q1 q3 q5 q7): the same permutation inside every
+// 8-element block of A and B (the expanded weight uses it too), which leaves
+// every 64-group dot product unchanged.
+__device__ __forceinline__ void unpack8_e4m3(uint32_t w, uint32_t& o0, uint32_t& o1) {
+  o0 = (w & 0x07070707u) | ((w << 4) & 0x80808080u);
+  o1 = ((w >> 4) & 0x07070707u) | (w & 0x80808080u);
 }
 
-// Unpack `rows` rows of 64 packed bytes (row-major, no swizzle) into rows of
-// 128 int8 in the SWIZZLE_128B K-major layout. Each thread converts one 16B
-// packed chunk into two 16B output chunks per iteration.
+// Unpack 128 rows of 64 packed bytes (row-major, no swizzle) into rows of 128
+// e4m3 bytes in the SWIZZLE_128B K-major layout. 512 16-byte chunks over the
+// 64 unpack threads: all 8 loads of a thread are issued before any store.
 __device__ __forceinline__ void unpack_tile(const uint8_t* __restrict__ src, uint8_t* dst,
-                                            int rows, int tid) {
-  for (int i = tid; i < rows * 4; i += w4::UNPACK_THREADS) {
+                                            int tid) {
+  constexpr int kChunks = kBM * 4 / w4::UNPACK_THREADS;   // 8
+  uint4 p[kChunks];
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j) {
+    const int i = tid + j * w4::UNPACK_THREADS;
+    p[j] = *reinterpret_cast<const uint4*>(src + (i >> 2) * 64 + (i & 3) * 16);
+  }
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j) {
+    const int i = tid + j * w4::UNPACK_THREADS;
     const int r = i >> 2, cj = i & 3;
-    const uint4 p = *reinterpret_cast<const uint4*>(src + r * 64 + cj * 16);
     uint4 o0, o1;
-    unpack8(p.x, o0.x, o0.y);
-    unpack8(p.y, o0.z, o0.w);
-    unpack8(p.z, o1.x, o1.y);
-    unpack8(p.w, o1.z, o1.w);
+    unpack8_e4m3(p[j].x, o0.x, o0.y);
+    unpack8_e4m3(p[j].y, o0.z, o0.w);
+    unpack8_e4m3(p[j].z, o1.x, o1.y);
+    unpack8_e4m3(p[j].w, o1.z, o1.w);
     *reinterpret_cast<uint4*>(dst + swz128(r, cj * 32)) = o0;
     *reinterpret_cast<uint4*>(dst + swz128(r, cj * 32 + 16)) = o1;
+  }
+}
+
+// Shared-memory descriptor, K-major, no swizzle: 8-row x 16-byte core
+// matrices; the two k-halves of a row block are LBO = 128 B apart and
+// consecutive 8-row blocks SBO = 256 B apart (layout type 0).
+__device__ __forceinline__ uint64_t sdesc_k16_noswz(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)(128u >> 4) << 16;
+  d |= (uint64_t)(256u >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  return d;
+}
+
+// byte offset of element (row r, k = 0) in that layout
+__device__ __forceinline__ uint32_t sofs_k0(int r) { return (r >> 3) * 256 + (r & 7) * 16; }
+
+// e4m3 bytes of the integers 0..7 (normal numbers; 0 -> 0x00)
+__device__ __forceinline__ uint32_t e4m3_int(uint32_t m) {
+  // 0, 1.0, 2.0, 3.0, 4.0, 5.0, 6.0, 7.0
+  return __byte_perm(0x44403800u, 0x4E4C4A48u, m);
+}
+
+// Load-time weight expansion: packed sign-magnitude nibbles u8 [N, K/2] ->
+// e4m3 integers u8 [N, K] in the within-8 order of unpack8_e4m3.
+__global__ void w4a4_weight_expand_kernel(const uint32_t* __restrict__ packed,
+                                          uint2* __restrict__ out, int64_t nwords) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nwords;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t w = packed[i];
+    uint32_t o[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {   // h = 0: low nibbles (even k), 1: high nibbles
+      uint32_t r = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t n = (w >> (8 * b + 4 * h)) & 0xFu;
+        const uint32_t e = e4m3_int(n & 7u) | ((n & 8u) ? 0x80u : 0u);
+        r |= (e & 0xFFu) << (8 * b);
+      }
+      o[h] = r;
+    }
+    out[i] = make_uint2(o[0], o[1]);
   }
 }
 
 __global__ void __launch_bounds__(w4::THREADS, 1)
 gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmUP,
-                 const __grid_constant__ CUtensorMap tmWS,
                  const __half* __restrict__ a_scale, const float* __restrict__ w_scale_gn,
                  const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out,
                  int32_t* __restrict__ partials, int M, int N, int K, int rank_pad, int gelu) {
@@ -225,17 +291,14 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                                              ~uintptr_t(1023));
   uint8_t* ustage = smem;
   uint8_t* pstage = smem + USTAGES * USTAGE_BYTES;
-  uint8_t* sstage = pstage + PSTAGES * PSTAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sstage + SSTAGES * SSTAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pstage + PSTAGES * PA_BYTES);
   uint64_t* p_full = bars;
   uint64_t* p_empty = p_full + PSTAGES;
-  uint64_t* u_full = p_empty + PSTAGES;
+  uint64_t* u_full = p_empty + PSTAGES;     // 2 arrivals: unpack warps + B TMA
   uint64_t* u_empty = u_full + USTAGES;
   uint64_t* acc_full = u_empty + USTAGES;   // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
-  uint64_t* s_full = acc_empty + 2;         // [SSTAGES]
-  uint64_t* s_empty = s_full + SSTAGES;     // [SSTAGES]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_empty + SSTAGES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   uint32_t* unpack_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -247,9 +310,8 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < PSTAGES; ++i) { mbar_init(&p_full[i], 1); mbar_init(&p_empty[i], 1); }
-    for (int i = 0; i < USTAGES; ++i) { mbar_init(&u_full[i], 1); mbar_init(&u_empty[i], 1); }
+    for (int i = 0; i < USTAGES; ++i) { mbar_init(&u_full[i], 2); mbar_init(&u_empty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], EPI_WARPS); }
-    for (int i = 0; i < SSTAGES; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_empty[i], EPI_WARPS); }
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -259,39 +321,38 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) GWB_TRACE_AT(7, 0);
 
   if (warp == 0 && lane == 0) {
     // ---------------------------------------------------------------- TMA
     if (has_lr) {
-      // low-rank operands go straight into unpacked stage 0 (ring slot 0)
+      // low-rank operands go straight into operand stage 0 (ring slot 0)
       mbar_arrive_expect_tx(&u_full[0], kBM * 128 + BN * 128);
+      mbar_arrive(&u_full[0]);
       tma_load_2d(ustage, &tmLA, &u_full[0], 0, m0);
       tma_load_2d(ustage + UA_BYTES, &tmUP, &u_full[0], 0, n0);
     }
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % PSTAGES;
       if (!mbar_wait(&p_empty[s], ((kb / PSTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
-      uint8_t* dst = pstage + s * PSTAGE_BYTES;
-      mbar_arrive_expect_tx(&p_full[s], PSTAGE_BYTES);
-      tma_load_2d(dst, &tmA, &p_full[s], kb * (kBK / 2), m0);
-      tma_load_2d(dst + PA_BYTES, &tmB, &p_full[s], kb * (kBK / 2), n0);
-      if (!dump) {
-        // this k-block's two groups of weight scales, f32 [2][BN]
-        const int ss = kb % SSTAGES;
-        if (!mbar_wait(&s_empty[ss], ((kb / SSTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&s_full[ss], SSTAGE_BYTES);
-        tma_load_2d(sstage + ss * SSTAGE_BYTES, &tmWS, &s_full[ss], n0, 2 * kb);
-      }
+      GWB_TRACE_AT(0, kb);
+      mbar_arrive_expect_tx(&p_full[s], PA_BYTES);
+      tma_load_2d(pstage + s * PA_BYTES, &tmA, &p_full[s], kb * (kBK / 2), m0);
+      const int ui = kb + has_lr, u = ui % USTAGES;
+      if (!mbar_wait(&u_empty[u], ((ui / USTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
+      mbar_arrive_expect_tx(&u_full[u], UB_BYTES);
+      tma_load_2d(ustage + u * USTAGE_BYTES + UA_BYTES, &tmB, &u_full[u], kb * kBK, n0);
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------------- MMA
-    constexpr uint32_t idesc = idesc_i8(kBM, BN);
+    constexpr uint32_t idesc = idesc_fmt0_f32(kBM, BN);      // e4m3 x e4m3 -> f32
     constexpr uint32_t idesc_lr = idesc_bf16(kBM, BN);
+    constexpr uint32_t idesc_s = idesc_fmt0_f32(kBM, BN);    // f16 x f16 -> f32
     bool ok = true;
     if (has_lr) {
       // group slot 0 <- la · proj_upᵀ (f32), into accumulator buffer 0
       if (!mbar_wait(&u_full[0], 0, GWB_ERR_TIMEOUT_MMA)) ok = false;
-      if (ok && !mbar_wait(&acc_empty[0], 0, GWB_ERR_TIMEOUT_MMA)) ok = false;
+      if (ok && !mbar_wait(&acc_empty[0], 1, GWB_ERR_TIMEOUT_MMA)) ok = false;
       if (ok) {
         tc_fence_after();
         const uint32_t a_base = smem_u32(ustage), b_base = a_base + UA_BYTES;
@@ -306,20 +367,26 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       const int ui = kb + has_lr;
       const int u = ui % USTAGES;
       if (!mbar_wait(&u_full[u], (ui / USTAGES) & 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
+      GWB_TRACE_AT(1, kb);
       tc_fence_after();
       const uint32_t a_base = smem_u32(ustage + u * USTAGE_BYTES);
       const uint32_t b_base = a_base + UA_BYTES;
+      const uint32_t s_base = b_base + UB_BYTES;
       for (int gs = 0; gs < 2 && ok; ++gs) {
         const int gi = kb * 2 + gs + has_lr;
         const int b = gi & 1;
-        // completion #(gi>>1) of acc_empty[b]: #0 is the epilogue's initial
-        // magic-bias fill, #j the drain (+ re-bias) of the buffer's use j-1
-        if (!mbar_wait(&acc_empty[b], (gi >> 1) & 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
+        if (!mbar_wait(&acc_empty[b], ((gi >> 1) & 1) ^ 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
+        GWB_TRACE_AT(2, gi);
         tc_fence_after();
         const uint32_t d = tmem + b * BN;
-        // accumulate onto the magic bias already in TMEM
-        mma_i8(d, sdesc_k128(a_base + 64 * gs), sdesc_k128(b_base + 64 * gs), idesc, 1u);
-        mma_i8(d, sdesc_k128(a_base + 64 * gs + 32), sdesc_k128(b_base + 64 * gs + 32), idesc, 1u);
+        mma_f8(d, sdesc_k128(a_base + 64 * gs), sdesc_k128(b_base + 64 * gs), idesc, 0u);
+        mma_f8(d, sdesc_k128(a_base + 64 * gs + 32), sdesc_k128(b_base + 64 * gs + 32), idesc, 1u);
+        if (!dump) {
+          // S_b = a_scale[:, g] ⊗ (w_scale[:, g] * 2^9), exact in f32 (11-bit x 11-bit)
+          const uint32_t sa = s_base + gs * SGROUP_BYTES;
+          mma_f16(tmem + 2 * BN + b * BN, sdesc_k16_noswz(sa), sdesc_k16_noswz(sa + SA_BYTES),
+                  idesc_s, 0u);
+        }
         mma_commit(&acc_full[b]);
       }
       mma_commit(&u_empty[u]);
@@ -327,10 +394,30 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   } else if (warp == 2 || warp == 3) {
     // ---------------------------------------------------------------- unpack
     const int tid = threadIdx.x - 64;
+    // the scale operands are zero except at k = 0: clear every stage's scale
+    // area once; later only the k = 0 column is rewritten
+    for (int u = 0; u < USTAGES; ++u) {
+      uint4* z = reinterpret_cast<uint4*>(ustage + u * USTAGE_BYTES + UA_BYTES + UB_BYTES);
+      for (int i = tid; i < 2 * SGROUP_BYTES / 16; i += UNPACK_THREADS) z[i] = make_uint4(0, 0, 0, 0);
+    }
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % PSTAGES;
       const int ui = kb + has_lr;
       const int u = ui % USTAGES;
+      // scale loads (global, L2-resident) first, so their latency overlaps the waits
+      __half2 av[2];
+      float w0[2], w1[2];
+      if (!dump) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = tid + 64 * h;
+          av[h] = __float2half2_rn(0.f);
+          if (m0 + r < M)
+            av[h] = *reinterpret_cast<const __half2*>(a_scale + (size_t)(m0 + r) * G + 2 * kb);
+          w0[h] = __ldg(w_scale_gn + (size_t)(2 * kb) * N + n0 + r);
+          w1[h] = __ldg(w_scale_gn + (size_t)(2 * kb + 1) * N + n0 + r);
+        }
+      }
       // one thread waits, the named barrier broadcasts the outcome so both
       // unpack warps always leave the loop together
       if (tid == 0) {
@@ -340,133 +427,96 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       }
       asm volatile("bar.sync 1, 64;" ::: "memory");
       if (*reinterpret_cast<volatile uint32_t*>(unpack_flag) == 0u) break;
-      const uint8_t* src = pstage + s * PSTAGE_BYTES;
+      if (tid == 0) GWB_TRACE_AT(3, kb);
       uint8_t* dst = ustage + u * USTAGE_BYTES;
-      unpack_tile(src, dst, kBM, tid);
-      unpack_tile(src + PA_BYTES, dst + UA_BYTES, BN, tid);
+      unpack_tile(pstage + s * PA_BYTES, dst, tid);
+      if (!dump) {
+        // k = 0 column of this k-block's two scale-operand pairs
+        uint8_t* sdst = dst + UA_BYTES + UB_BYTES;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = tid + 64 * h;
+          *reinterpret_cast<__half*>(sdst + sofs_k0(r)) = __low2half(av[h]);
+          *reinterpret_cast<__half*>(sdst + SGROUP_BYTES + sofs_k0(r)) = __high2half(av[h]);
+          *reinterpret_cast<__half*>(sdst + SA_BYTES + sofs_k0(r)) =
+              __float2half_rn(w0[h] * kWScaleMul);
+          *reinterpret_cast<__half*>(sdst + SGROUP_BYTES + SA_BYTES + sofs_k0(r)) =
+              __float2half_rn(w1[h] * kWScaleMul);
+        }
+      }
       fence_proxy_async_smem();
       asm volatile("bar.sync 1, 64;" ::: "memory");
       if (tid == 0) {
+        GWB_TRACE_AT(4, kb);
         mbar_arrive(&p_empty[s]);
         mbar_arrive(&u_full[u]);
       }
     }
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- epilogue
-    // Each s32 group buffer is pre-filled with the bits of 1.5*2^23
-    // (0x4B400000); the MMA accumulates the group sum v onto it, so the word
-    // read back is the float 1.5*2^23 + v exactly (|v| <= 64*64 < 2^22) and
-    // float(v) costs one subtraction instead of an I2F conversion (I2F runs
-    // on the narrow conversion pipe). After draining, the epilogue writes the
-    // bias back for the buffer's next use. Eight epilogue warps: warp 4+i
-    // reads lane quarter i%4 and column slice (i/4)*EC.
-    const int q = warp & 3;                  // TMEM lane quarter = tile rows 32q..
-    const int cb = ((warp - 4) >> 2) * EC;   // this warp's column slice
+    // Per group: load the f32 group sum V (= 2^-9 * v, exact) of this warp's
+    // 32 rows x EC columns and the scale product S = a_scale * w_scale * 2^9
+    // the tensor core wrote beside it, wait once, hand the TMEM buffer
+    // straight back to the MMA warp, then acc += V * S (one FFMA per element).
+    // Eight epilogue warps: warp 4+i reads lane quarter i%4 (tile rows
+    // 32*(i%4)..) and column slice (i/4)*EC.
+    const int q = warp & 3;
+    const int cb = ((warp - 4) >> 2) * EC;
     const int row = m0 + 32 * q + lane;
     const bool rv = row < M;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-    constexpr uint32_t kMagic = 0x4B400000u;
-    const float kMagicF = 12582912.0f;
-    uint32_t bias16[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) bias16[j] = kMagic;
-#pragma unroll
-    for (int bb = 0; bb < 2; ++bb)
-#pragma unroll
-      for (int c = 0; c < EC; c += 16) tmem_st16(lane_base + bb * BN + cb + c, bias16);
-    tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) { mbar_arrive(&acc_empty[0]); mbar_arrive(&acc_empty[1]); }
-
     float2 acc[EC / 2];
 #pragma unroll
     for (int j = 0; j < EC / 2; ++j) acc[j] = make_float2(0.f, 0.f);
-    const float2 negm = make_float2(-kMagicF, -kMagicF);
     const int total = G + has_lr;
     bool ok = true;
-    // the activation scale of the next group is fetched one group ahead
-    float sa_next = (rv && !dump) ? __half2float(a_scale[(size_t)row * G]) * (1.0f / 256.0f) : 0.f;
     for (int gi = 0; gi < total; ++gi) {
       const int b = gi & 1;
       if (!mbar_wait(&acc_full[b], (gi >> 1) & 1, GWB_ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      if (warp == 4 && lane == 0) GWB_TRACE_AT(5, gi);
       tc_fence_after();
       const uint32_t col0 = lane_base + b * BN + cb;
-      if (has_lr && gi == 0) {
-        // f32 low-rank product la·proj_upᵀ seeds the accumulator
+      const bool lr = has_lr && gi == 0;
+      const int g = gi - has_lr;
+      // two halves of 32 columns: V and S of a half are loaded together; the
+      // TMEM buffer is released once the second half's loads have landed
 #pragma unroll
-        for (int c = 0; c < EC; c += 16) {
-          uint32_t v[16];
-          tmem_ld16(col0 + c, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 16; j += 2)
-            acc[(c + j) / 2] = make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
-          tmem_st16(col0 + c, bias16);
-        }
-      } else if (dump) {
-        const int g = gi - has_lr;
-#pragma unroll
-        for (int c = 0; c < EC; c += 16) {
-          uint32_t v[16];
-          tmem_ld16(col0 + c, v);
-          tmem_wait_ld();
-          tmem_st16(col0 + c, bias16);
-          if (rv) {
-            // the MMA summed 256*v (operands hold 16*q)
-            uint4* dp = reinterpret_cast<uint4*>(partials + ((size_t)g * M + row) * N + n0 + cb + c);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dp[j] = make_uint4((uint32_t)((int32_t)(v[4 * j] - kMagic) >> 8),
-                                 (uint32_t)((int32_t)(v[4 * j + 1] - kMagic) >> 8),
-                                 (uint32_t)((int32_t)(v[4 * j + 2] - kMagic) >> 8),
-                                 (uint32_t)((int32_t)(v[4 * j + 3] - kMagic) >> 8));
-          }
-        }
-      } else {
-        const int g = gi - has_lr;
-        const float sa = sa_next;
-        if (rv && g + 1 < G)
-          sa_next = __half2float(a_scale[(size_t)row * G + g + 1]) * (1.0f / 256.0f);
-        const float2 sa2 = make_float2(sa, sa);
-        const int ss = (g >> 1) % SSTAGES;
-        if ((g & 1) == 0 &&
-            !mbar_wait(&s_full[ss], ((g >> 1) / SSTAGES) & 1, GWB_ERR_TIMEOUT_EPILOGUE)) {
-          ok = false;
-          break;
-        }
-        const float* wsg = reinterpret_cast<const float*>(sstage + ss * SSTAGE_BYTES) + (g & 1) * BN + cb;
-        uint32_t v[2][16];
-        tmem_ld16(col0, v[0]);
+      for (int h = 0; h < EC / 32; ++h) {
+        uint32_t v[32], sc[32];
+        tmem_ld32(col0 + 32 * h, v);
+        if (!lr && !dump) tmem_ld32(col0 + 2 * BN + 32 * h, sc);
         tmem_wait_ld();
+        if (h == EC / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+        if (lr) {
+          // f32 low-rank product la·proj_upᵀ seeds the accumulator
 #pragma unroll
-        for (int c = 0; c < EC / 16; ++c) {
-          if (c + 1 < EC / 16) tmem_ld16(col0 + (c + 1) * 16, v[(c + 1) & 1]);
+          for (int j = 0; j < 32; j += 2)
+            acc[16 * h + j / 2] = make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+        } else if (dump) {
+          if (rv) {
+            uint4* dp = reinterpret_cast<uint4*>(partials + ((size_t)g * M + row) * N + n0 + cb +
+                                                 32 * h);
 #pragma unroll
-          for (int j = 0; j < 16; j += 4) {
-            const float4 ws = *reinterpret_cast<const float4*>(wsg + c * 16 + j);
-            const float2 s01 = __fmul2_rn(sa2, make_float2(ws.x, ws.y));
-            const float2 s23 = __fmul2_rn(sa2, make_float2(ws.z, ws.w));
-            const float2 f01 = __fadd2_rn(
-                make_float2(__uint_as_float(v[c & 1][j]), __uint_as_float(v[c & 1][j + 1])), negm);
-            const float2 f23 = __fadd2_rn(
-                make_float2(__uint_as_float(v[c & 1][j + 2]), __uint_as_float(v[c & 1][j + 3])),
-                negm);
-            acc[(c * 16 + j) / 2] = __ffma2_rn(f01, s01, acc[(c * 16 + j) / 2]);
-            acc[(c * 16 + j) / 2 + 1] = __ffma2_rn(f23, s23, acc[(c * 16 + j) / 2 + 1]);
+            for (int j = 0; j < 8; ++j)   // V = 2^-9 * v, exact
+              dp[j] = make_uint4((uint32_t)__float2int_rn(__uint_as_float(v[4 * j]) * 512.0f),
+                                 (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 1]) * 512.0f),
+                                 (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 2]) * 512.0f),
+                                 (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 3]) * 512.0f));
           }
-          tmem_st16(col0 + c * 16, bias16);
-          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j += 2)
+            acc[16 * h + j / 2] =
+                __ffma2_rn(make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])),
+                           make_float2(__uint_as_float(sc[j]), __uint_as_float(sc[j + 1])),
+                           acc[16 * h + j / 2]);
         }
       }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&acc_empty[b]);
-        const int g = gi - has_lr;
-        if (!dump && g >= 0 && (g & 1) == 1) mbar_arrive(&s_empty[(g >> 1) % SSTAGES]);
-      }
+      if (warp == 4 && lane == 0) GWB_TRACE_AT(6, gi);
     }
     if (ok && !dump && rv) {
 #pragma unroll
@@ -571,26 +621,21 @@ int launch_gemm_w4a4(const W4A4Args& a, cudaStream_t st) {
   if (a.M <= 0 || a.K <= 0 || a.K % kBK || a.N % w4::BN) return GWB_E_SHAPE;
   if (a.rank_pad < 0 || a.rank_pad > 64 || a.rank_pad % 16) return GWB_E_SHAPE;
   if (a.rank_pad > 0 && (!a.la || !a.up)) return GWB_E_SHAPE;
-  if (!al16(a.a_codes) || !al16(a.w_codes) || !al16(a.w_scale_gn) ||
-      (a.out && !al16(a.out)) || (a.bias && !al16(a.bias)) || (a.la && !al16(a.la)) ||
-      (a.up && !al16(a.up)) || (a.partials && !al16(a.partials)))
-    return GWB_E_ALIGN;
   if (!a.partials && !a.out) return GWB_E_SHAPE;
-  CUtensorMap tA, tB, tLA, tUP, tWS;
+  if (!al16(a.a_codes) || !al16(a.w_q8) || !al16(a.w_scale_gn) ||
+      (a.out && !al16(a.out)) || (a.bias && !al16(a.bias)) || (a.la && !al16(a.la)) ||
+      (a.up && !al16(a.up)) || (a.partials && !al16(a.partials)) ||
+      (reinterpret_cast<uintptr_t>(a.a_scale) & 3u))
+    return GWB_E_ALIGN;
+  CUtensorMap tA, tB, tLA, tUP;
   int rc = make_tmap(&tA, a.a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K / 2, a.M, kBK / 2,
                      kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  rc = make_tmap(&tB, a.w_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K / 2, a.N, kBK / 2,
-                 w4::BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+  rc = make_tmap(&tB, a.w_q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.N, kBK, w4::BN,
+                 CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   tLA = tA;
   tUP = tB;
-  tWS = tA;
-  if (!a.partials) {
-    rc = make_tmap(&tWS, a.w_scale_gn, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.N, a.K / 64, w4::BN,
-                   2, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc) return rc;
-  }
   if (a.rank_pad > 0 && !a.partials) {
     rc = make_tmap(&tLA, a.la, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.rank_pad, a.M, 64, kBM,
                    CU_TENSOR_MAP_SWIZZLE_128B);
@@ -607,11 +652,32 @@ int launch_gemm_w4a4(const W4A4Args& a, cudaStream_t st) {
   }
   dim3 grid(a.N / w4::BN, (a.M + kBM - 1) / kBM);
   gemm_w4a4_kernel<<<grid, w4::THREADS, w4::SMEM_BYTES, st>>>(
-      tA, tB, tLA, tUP, tWS, static_cast<const __half*>(a.a_scale), a.w_scale_gn,
+      tA, tB, tLA, tUP, static_cast<const __half*>(a.a_scale), a.w_scale_gn,
       static_cast<const __nv_bfloat16*>(a.bias), static_cast<__nv_bfloat16*>(a.out), a.partials,
       a.M, a.N, a.K, a.partials ? 0 : a.rank_pad, a.gelu);
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }
+
+int launch_w4a4_weight_expand(const void* w_codes, void* w_q8, int64_t N, int64_t K,
+                              cudaStream_t st) {
+  if (N <= 0 || K <= 0 || K % 64) return GWB_E_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(w_codes) & 3u) || (reinterpret_cast<uintptr_t>(w_q8) & 7u))
+    return GWB_E_ALIGN;
+  const int64_t nwords = N * K / 8;
+  int64_t blocks = (nwords + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  w4a4_weight_expand_kernel<<<(int)blocks, 256, 0, st>>>(
+      static_cast<const uint32_t*>(w_codes), static_cast<uint2*>(w_q8), nwords);
+  return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
+}
+
+#ifdef GWB_TRACE
+}  // namespace gwb
+extern "C" int gwb_trace_read(long long* dst) {
+  return cudaMemcpyFromSymbol(dst, gwb_trace, sizeof(long long) * 8 * 512) == cudaSuccess ? 0 : 3;
+}
+namespace gwb {
+#endif
 
 int device_error_read_and_clear(int* code) {
   int v = 0;

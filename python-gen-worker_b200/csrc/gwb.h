@@ -24,7 +24,7 @@ int launch_act_int8(const void* x, void* q, void* scale, int M, int K, cudaStrea
 struct W4A4Args {
   const void* a_codes;   // u8 [M, K/2]
   const void* a_scale;   // f16 [M, K/64]
-  const void* w_codes;   // u8 [N, K/2]
+  const void* w_q8;      // e4m3 [N, K] expanded weight (launch_w4a4_weight_expand)
   const float* w_scale_gn;  // f32 [K/64, N] (load-time transposed weight scales)
   const void* la;        // bf16 [M, rank_pad] or null
   const void* up;        // bf16 [N, rank_pad] or null
@@ -34,6 +34,8 @@ struct W4A4Args {
   int M, N, K, rank_pad, gelu;
 };
 int launch_gemm_w4a4(const W4A4Args& a, cudaStream_t st);
+int launch_w4a4_weight_expand(const void* w_codes, void* w_q8, int64_t N, int64_t K,
+                              cudaStream_t st);
 
 struct W8A8Args {
   const void* a_q;        // s8 [M, K]

@@ -61,7 +61,7 @@ inline uint64_t round256(uint64_t v) { return (v + 255u) & ~uint64_t(255u); }
 }  // namespace
 
 extern "C" int gwb_svdq_w4a4_linear_noalloc(const void* x, const void* smooth,
-                                            const void* proj_down_t, const void* w_codes,
+                                            const void* proj_down_t, const void* w_q8,
                                             const float* w_scale_gn, const void* proj_up,
                                             const void* bias, int64_t M, int64_t N, int64_t K,
                                             int rank_pad, int gelu, void* out, void* stream) {
@@ -78,6 +78,6 @@ extern "C" int gwb_svdq_w4a4_linear_noalloc(const void* x, const void* smooth,
   void* codes = base;
   void* ascale = base + codes_b;
   void* la = rank_pad ? static_cast<void*>(base + codes_b + scale_b) : nullptr;
-  return gwb_svdq_w4a4_linear(x, smooth, proj_down_t, w_codes, w_scale_gn, proj_up, bias, M, N,
+  return gwb_svdq_w4a4_linear(x, smooth, proj_down_t, w_q8, w_scale_gn, proj_up, bias, M, N,
                               K, rank_pad, gelu, codes, ascale, la, out, stream);
 }

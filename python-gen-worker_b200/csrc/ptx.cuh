@@ -6,9 +6,9 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
-#ifndef GWB_SPIN_LIMIT
-// ~ several seconds of polling at the try_wait suspend granularity.
-#define GWB_SPIN_LIMIT (1u << 26)
+#ifndef GWB_WAIT_LIMIT_CYCLES
+// A bounded wait gives up after this many SM clock cycles (~2 s at 2 GHz).
+#define GWB_WAIT_LIMIT_CYCLES (4000000000ll)
 #endif
 
 // Error codes written to gwb_dev_error (first writer wins).
@@ -56,22 +56,32 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// try_wait suspends the thread until the phase completes or this many ns
+// pass, instead of returning at once: waiting roles then stop competing with
+// working warps for issue slots.
+constexpr uint32_t kSuspendHintNs = 1000000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs) : "memory");
   return ok != 0;
 }
 
 // Bounded wait. Returns false (after recording `err`) on timeout or when
 // another role already failed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int err) {
-  for (uint32_t i = 0; i < GWB_SPIN_LIMIT; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long start = clock64();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023u) == 1023u && error_seen()) return false;
+    if ((i & 15u) == 0u) {
+      if (error_seen()) return false;
+      if (clock64() - start > GWB_WAIT_LIMIT_CYCLES) break;
+    }
   }
   set_error(err);
   return false;
@@ -124,6 +134,15 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f8f6f4 (here e4m3 x e4m3 -> f32).
+__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (bf16 x bf16 -> f32).
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                         uint32_t idesc, uint32_t accumulate) {
@@ -153,6 +172,30 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
         "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+
+// 32 lanes x 32 bit, 32 consecutive columns -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// Per-warpgroup register budget hand-off (all threads of the warpgroup).
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // 32 lanes x 32 bit, 16 consecutive columns <- 16 registers per thread.
@@ -191,6 +234,10 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
          | (1u << 7)          // A = s8
          | (1u << 10)         // B = s8
          | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// f16 x f16 -> f32 and e4m3 x e4m3 -> f32 share the encoding (format 0).
+__host__ __device__ constexpr uint32_t idesc_fmt0_f32(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4)            // D = f32

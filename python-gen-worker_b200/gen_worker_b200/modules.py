@@ -5,7 +5,7 @@
 u8 [N, K/2]), ``weight_scale``, ``smooth_factor`` [K], ``proj_down`` [K, r],
 ``proj_up`` [N, r], ``bias`` [N]; its layout tag ``int4-g64-lownib`` names the
 INT4 group-64 format (fp16 scale per 64-group, ``weight_scale`` f16
-[N, K/64], even k in the low nibble). ``W8A8Int8Linear`` keeps
+[N, K/64], even k in the low nibble, sign-magnitude nibbles). ``W8A8Int8Linear`` keeps
 ``Fp8ScaledLinear``'s (``src/gen_worker/models/w8a8.py:313-354``): ``weight``
 s8 [N, K], ``weight_scale`` f32 [N, 1], ``bias``.
 
@@ -37,14 +37,16 @@ class SvdqB200LayoutError(ValueError):
 # ---------------------------------------------------------------- producer
 def quantize_int4_rows(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Symmetric INT4 group-64 quantisation of a [R, K] matrix (fp32 math):
-    s = fp16(clamp(amax/7, 2^-24, 65504)); q = clamp(rint(w/s), -8, 7);
-    packed two per byte, even k in the low nibble."""
+    s = fp16(clamp(amax/7, 2^-24, 65504)); q = clamp(rint(w/s), -7, 7);
+    packed two per byte, even k in the low nibble, sign-magnitude nibbles
+    (bit 3 = sign, bits 0-2 = |q|)."""
     r, k = w.shape
     if k % GROUP:
         raise SvdqB200LayoutError(f"K={k} is not a multiple of {GROUP}")
     g = w.float().reshape(r, k // GROUP, GROUP)
     s = (g.abs().amax(dim=-1) / 7.0).clamp(min=2.0 ** -24, max=65504.0).to(torch.float16)
-    q = torch.round(g / s.float().unsqueeze(-1)).clamp(-8, 7).reshape(r, k).to(torch.int16) & 0xF
+    q = torch.round(g / s.float().unsqueeze(-1)).clamp(-7, 7).reshape(r, k).to(torch.int16)
+    q = torch.where(q < 0, 8 | (-q), q)
     packed = ((q[:, 1::2] << 4) | q[:, 0::2]).to(torch.uint8).contiguous()
     return packed, s
 
@@ -109,6 +111,7 @@ class SvdqInt4Linear(nn.Module):
         dev = self.weight.device
         if self._packed is None or self._packed["device"] != dev:
             p = ops.prepare_w4a4_weights(self.weight_scale, self.proj_down, self.proj_up)
+            p["w_q8"] = ops.expand_w4a4_weight(self.weight)
             p["device"] = dev
             self._packed = p
         return self._packed
@@ -124,7 +127,7 @@ class SvdqInt4Linear(nn.Module):
             x2 = x2.contiguous()
         p = self.prepare()
         codes, ascale, la = ops.svdq_w4a4_quant(x2, self.smooth_factor, p["proj_down_t"])
-        y = ops.svdq_w4a4_gemm(codes, ascale, self.weight, p["w_scale_gn"],
+        y = ops.svdq_w4a4_gemm(codes, ascale, p["w_q8"], p["w_scale_gn"],
                                la if p["proj_down_t"] is not None else None,
                                p["proj_up_pad"],
                                self.bias.detach() if self.bias is not None else None,

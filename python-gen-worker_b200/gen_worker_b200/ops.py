@@ -82,8 +82,21 @@ def _(x2, smooth, proj_down_t):
             x2.new_empty(m, rp, dtype=torch.bfloat16))
 
 
+def expand_w4a4_weight(w_codes: torch.Tensor) -> torch.Tensor:
+    """Load-time repack of the packed INT4 weight u8 [N, K/2] into the GEMM's
+    operand form u8 [N, K] (each code an e4m3 integer, within-8 order of the
+    operand unpack), on the weight's CUDA device."""
+    _need(w_codes, "w_codes", torch.uint8, 2)
+    n, k = w_codes.shape[0], w_codes.shape[1] * 2
+    out = torch.empty(n, k, dtype=torch.uint8, device=w_codes.device)
+    lib = native.require()
+    native.check(lib.gwb_svdq_w4a4_weight_expand(w_codes.data_ptr(), n, k, out.data_ptr(),
+                                                 _stream()), "svdq_w4a4_weight_expand")
+    return out
+
+
 @torch.library.custom_op("gwb200::svdq_w4a4_gemm", mutates_args=())
-def svdq_w4a4_gemm(codes: torch.Tensor, ascale: torch.Tensor, w_codes: torch.Tensor,
+def svdq_w4a4_gemm(codes: torch.Tensor, ascale: torch.Tensor, w_q8: torch.Tensor,
                    w_scale_gn: torch.Tensor, la: Optional[torch.Tensor],
                    proj_up: Optional[torch.Tensor], bias: Optional[torch.Tensor],
                    gelu: bool) -> torch.Tensor:
@@ -91,11 +104,11 @@ def svdq_w4a4_gemm(codes: torch.Tensor, ascale: torch.Tensor, w_codes: torch.Ten
     (+ GELU) -> bf16 [M, N]."""
     _need(codes, "codes", torch.uint8, 2)
     _need(ascale, "ascale", torch.float16, 2)
-    _need(w_codes, "w_codes", torch.uint8, 2)
+    _need(w_q8, "w_q8", torch.uint8, 2)
     _need(w_scale_gn, "w_scale_gn", torch.float32, 2)
     _need(bias, "bias", torch.bfloat16, 1)
     m, k = codes.shape[0], codes.shape[1] * 2
-    n = w_codes.shape[0]
+    n = w_q8.shape[0]
     rp = 0
     if la is not None and proj_up is not None and la.shape[1] > 0:
         _need(la, "la", torch.bfloat16, 2)
@@ -105,7 +118,7 @@ def svdq_w4a4_gemm(codes: torch.Tensor, ascale: torch.Tensor, w_codes: torch.Ten
             raise SvdqB200Error(f"la rank {rp} != proj_up rank {proj_up.shape[1]}")
     out = torch.empty(m, n, dtype=torch.bfloat16, device=codes.device)
     lib = native.require()
-    native.check(lib.gwb_svdq_w4a4_gemm(codes.data_ptr(), ascale.data_ptr(), w_codes.data_ptr(),
+    native.check(lib.gwb_svdq_w4a4_gemm(codes.data_ptr(), ascale.data_ptr(), w_q8.data_ptr(),
                                         w_scale_gn.data_ptr(), _ptr(la) if rp else None,
                                         _ptr(proj_up) if rp else None, _ptr(bias), m, n, k, rp,
                                         int(bool(gelu)), out.data_ptr(), _stream()),
@@ -114,29 +127,29 @@ def svdq_w4a4_gemm(codes: torch.Tensor, ascale: torch.Tensor, w_codes: torch.Ten
 
 
 @svdq_w4a4_gemm.register_fake
-def _(codes, ascale, w_codes, w_scale_gn, la, proj_up, bias, gelu):
-    return codes.new_empty(codes.shape[0], w_codes.shape[0], dtype=torch.bfloat16)
+def _(codes, ascale, w_q8, w_scale_gn, la, proj_up, bias, gelu):
+    return codes.new_empty(codes.shape[0], w_q8.shape[0], dtype=torch.bfloat16)
 
 
 @torch.library.custom_op("gwb200::svdq_w4a4_group_partials", mutates_args=())
-def svdq_w4a4_group_partials(codes: torch.Tensor, w_codes: torch.Tensor) -> torch.Tensor:
-    """Debug: every 64-group s32 partial sum of the tcgen05 GEMM,
-    s32 [K/64, M, N]."""
+def svdq_w4a4_group_partials(codes: torch.Tensor, w_q8: torch.Tensor) -> torch.Tensor:
+    """Debug: every 64-group integer partial sum of the tcgen05 GEMM,
+    s32 [K/64, M, N] (w_q8 = expand_w4a4_weight(weight))."""
     _need(codes, "codes", torch.uint8, 2)
-    _need(w_codes, "w_codes", torch.uint8, 2)
+    _need(w_q8, "w_q8", torch.uint8, 2)
     m, k = codes.shape[0], codes.shape[1] * 2
-    n = w_codes.shape[0]
+    n = w_q8.shape[0]
     out = torch.empty(k // GROUP, m, n, dtype=torch.int32, device=codes.device)
     lib = native.require()
-    native.check(lib.gwb_svdq_w4a4_group_partials(codes.data_ptr(), w_codes.data_ptr(), m, n, k,
+    native.check(lib.gwb_svdq_w4a4_group_partials(codes.data_ptr(), w_q8.data_ptr(), m, n, k,
                                                   out.data_ptr(), _stream()),
                  "svdq_w4a4_group_partials")
     return out
 
 
 @svdq_w4a4_group_partials.register_fake
-def _(codes, w_codes):
-    return codes.new_empty(codes.shape[1] * 2 // GROUP, codes.shape[0], w_codes.shape[0],
+def _(codes, w_q8):
+    return codes.new_empty(codes.shape[1] * 2 // GROUP, codes.shape[0], w_q8.shape[0],
                            dtype=torch.int32)
 
 
@@ -188,9 +201,12 @@ def prepare_w4a4_weights(w_scale: torch.Tensor, proj_down: Optional[torch.Tensor
     """Load-time repack of the module buffers into the kernel operand layouts
     (the reference repacks at load too: ``to_buffers``,
     ``svdq_layout.py:473-483``):
-      weight_scale f16 [N, K/64] -> w_scale_gn f32 [K/64, N]
+      weight_scale f16 [N, K/64] -> w_scale_gn f32 [K/64, N] (|scale| <= 127)
       proj_down bf16 [K, r]      -> proj_down_t bf16 [rank_pad, K] (zero rows)
       proj_up bf16 [N, r]        -> proj_up_pad bf16 [N, rank_pad] (zero cols)"""
+    if w_scale.numel() and float(w_scale.float().abs().max()) > 127.0:
+        raise SvdqB200Error("weight scales above 127 are not supported (the GEMM carries "
+                            "w_scale * 2^9 in fp16)")
     out = {"w_scale_gn": w_scale.float().t().contiguous()}
     if proj_down is not None and proj_up is not None and proj_down.shape[1] > 0:
         k, r = proj_down.shape

@@ -58,7 +58,9 @@ def main(ref_root: str = "/root/reference") -> None:
     out = {}
 
     # 1. nibble packing order
-    nib = torch.randint(0, 16, (8, 64), generator=gen, dtype=torch.uint8)
+    # nibbles 0..15 except 8 (e2m1 -0), which sign-magnitude INT4 never uses
+    nib = torch.randint(0, 15, (8, 64), generator=gen, dtype=torch.uint8)
+    nib = nib + (nib >= 8).to(torch.uint8)
     out["pack_codes"] = nib
     out["pack_packed"] = nq.pack_e2m1(nib)
 

@@ -55,7 +55,7 @@ def test_int4_activation_without_smoothing(cuda_ready):
 def test_int4_group_partials_bit_exact(cuda_ready, m, k, n):
     x, L = _layer_case(m, k, n, 0, seed=m + n)
     _, codes, _, _ = _quant_gpu(x, L)
-    got = ops.svdq_w4a4_group_partials(codes, L["w_packed"].cuda())
+    got = ops.svdq_w4a4_group_partials(codes, ops.expand_w4a4_weight(L["w_packed"].cuda()))
     want = O.int4_group_partials(codes.cpu(), L["w_packed"])
     assert torch.equal(got.cpu(), want)
     assert native.device_error() == 0

@@ -39,7 +39,7 @@ def test_noalloc_linear_matches_allocating_entry_point(cuda_ready, m, k, n, rank
                                  None if rank == 0 else L["proj_down"].to(dev),
                                  None if rank == 0 else L["proj_up"].to(dev))
     rp = 0 if rank == 0 else int(p["proj_down_t"].shape[0])
-    w = L["w_packed"].to(dev)
+    w = ops.expand_w4a4_weight(L["w_packed"].to(dev))
     smooth = L["smooth"].to(dev)
     bias = L["bias"].to(dev)
     down_t = p["proj_down_t"]
