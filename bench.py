@@ -181,10 +181,10 @@ class GemmTimer:
         from gen_worker_b200 import ops
         x2 = x.reshape(-1, mod.in_features)
         p = mod.prepare()
-        codes, ascale, la = ops.svdq_w4a4_quant(x2, mod.smooth_factor, p["proj_down_t"])
+        codes, ascale, la = ops.svdq_w4a4_quant_mma(x2, mod.smooth_factor, p["proj_down_t"])
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        y = ops.svdq_w4a4_gemm(codes, ascale, p["w_q8"], p["w_scale_gn"], la,
+        y = ops.svdq_w4a4_gemm(codes, ascale, p["w_q8"], p["w_scale_k8"], la,
                                p["proj_up_pad"], mod.bias.detach(), mod.gelu)
         e.record()
         self.pairs.append((s, e, 2.0 * x2.shape[0] * mod.in_features * mod.out_features))
@@ -296,9 +296,9 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
             e[0].record()
             if kind == "w4a4":
                 p = mod.prepare()
-                c, a, la = ops.svdq_w4a4_quant(xb, mod.smooth_factor, p["proj_down_t"])
+                c, a, la = ops.svdq_w4a4_quant_mma(xb, mod.smooth_factor, p["proj_down_t"])
                 e[1].record()
-                ops.svdq_w4a4_gemm(c, a, p["w_q8"], p["w_scale_gn"], la, p["proj_up_pad"],
+                ops.svdq_w4a4_gemm(c, a, p["w_q8"], p["w_scale_k8"], la, p["proj_up_pad"],
                                    mod.bias.detach(), gelu)
             else:
                 q, s_ = ops.w8a8_quant(xb)
@@ -311,7 +311,7 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
                 tot += e[0].elapsed_time(e[2]) / steps
                 gemm += e[1].elapsed_time(e[2]) / steps
         ops_ = 2.0 * m * n * k
-        act_bytes = m * k * 2 + (m * k // 2 + m * k // 32 + m * r * 2 if kind == "w4a4"
+        act_bytes = m * k * 2 + (m * k + m * k // 4 + m * r * 2 if kind == "w4a4"
                                  else m * k + m * 4)
         rows.append({"kind": kind, "M": m, "K": k, "N": n, "rank": r, "gelu": gelu,
                      "ms": tot, "gemm_ms": gemm, "act_ms": tot - gemm,

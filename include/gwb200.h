@@ -4,19 +4,22 @@
  * the given CUDA stream (cudaStream_t passed as void*; NULL = legacy default
  * stream), never synchronises, never allocates, and returns a GwbStatus code
  * (0 = success). Device buffers must be 16-byte aligned and row-major
- * contiguous. Layouts:
- *   x            bf16 [M, K]
- *   smooth       bf16 [K] (or NULL)
+ * contiguous. G = K/64 groups.
+ *
+ * Interchange (packed) form, as stored in checkpoints / module buffers:
+ *   codes        u8   [R, K/2]   INT4 sign-magnitude nibbles (bit 3 = sign,
+ *                                bits 0-2 = |q|, q in -7..7), even k low
+ *   scale        f16  [R, G]     one scale per 64-group
+ * GEMM operand form (what the tensor cores read; gwb_svdq_w4a4_to_operand
+ * converts, gwb_svdq_w4a4_quant_mma produces it directly):
+ *   q8           u8   [R, K]     each code as an e4m3 integer, elements of
+ *                                every 8-block in the order 0 2 4 6 1 3 5 7
+ *   scale_k8     f16  [G, R, 8]  scale at k = 0, zeros at k = 1..7
+ * Other tensors:
+ *   x            bf16 [M, K];  smooth bf16 [K] (or NULL)
  *   proj_down_t  bf16 [rank_pad, K]   (L1 transposed; rows >= rank are zero)
- *   codes        u8   [M, K/2]        INT4 sign-magnitude nibbles (bit 3 = sign,
- *                                     bits 0-2 = |q|, q in -7..7), even k low
- *   ascale       f16  [M, K/64]       one scale per 64-group
  *   la           bf16 [M, rank_pad]   x·L1 on raw x
- *   w_codes      u8   [N, K/2] packed weight (same nibble format as codes)
- *   w_q8         u8   [N, K] expanded weight: gwb_svdq_w4a4_weight_expand(w_codes)
- *   w_scale_gn   f32  [K/64, N] (fp16-representable values, |w_scale| <= 127)
- *   proj_up      bf16 [N, rank_pad]
- *   bias         bf16 [N] (or NULL); out bf16 [M, N]
+ *   proj_up      bf16 [N, rank_pad];  bias bf16 [N] (or NULL);  out bf16 [M, N]
  * Constraints: K % 128 == 0; N % 128 == 0 (W4A4) / N % 256 == 0 (W8A8);
  * rank_pad in {0, 16, 32, 48, 64}.
  */
@@ -43,43 +46,50 @@ int gwb_probe_add_one(const float* x, float* y, int64_t n, void* stream);
  * (reference src/gen_worker/models/svdq_fused.py:293-296, kernel :116-155)
  * fused with the low-rank down-projection `la = x2 @ proj_down`
  * (svdq_fused.py:524, svdq_native.py:153). INT4 group-64 with fp16 scales in
- * place of NVFP4; no per-tensor second-level scale. */
+ * place of NVFP4; no per-tensor second-level scale. Writes the packed
+ * interchange form (codes [M, K/2], ascale [M, G]). */
 int gwb_svdq_w4a4_quant(const void* x, const void* smooth, const void* proj_down_t,
                         int64_t M, int64_t K, int rank_pad,
                         void* codes, void* ascale, void* la, void* stream);
 
-/* Load-time weight repack (the counterpart of the reference's load-time
- * `to_buffers` / `pack_e2m1` repacks, src/gen_worker/models/svdq_layout.py:
- * 473-483): packed INT4 w_codes u8 [N, K/2] -> w_q8 u8 [N, K], each code as
- * an e4m3 integer, in the within-8-element order the GEMM's operand unpack
- * uses. */
-int gwb_svdq_w4a4_weight_expand(const void* w_codes, int64_t N, int64_t K, void* w_q8,
-                                void* stream);
+/* The same quantiser (identical codes and scales) writing the GEMM operand
+ * form instead (a_q8 [M, K], a_scale_k8 [G, M, 8]): the hot-path producer of
+ * `SvdqLinear.forward` (svdq_native.py:145-147). */
+int gwb_svdq_w4a4_quant_mma(const void* x, const void* smooth, const void* proj_down_t,
+                            int64_t M, int64_t K, int rank_pad,
+                            void* a_q8, void* a_scale_k8, void* la, void* stream);
+
+/* Packed interchange form -> GEMM operand form for R rows (weights at load
+ * time, or packed activations). Counterpart of the reference's load-time
+ * repacks `to_buffers` / `to_blocked_scales` (svdq_layout.py:473-483,
+ * nvfp4_quant.py:72-84). */
+int gwb_svdq_w4a4_to_operand(const void* codes, const void* scale, int64_t R, int64_t K,
+                             void* q8, void* scale_k8, void* stream);
 
 /* Replaces `cozy_gen_worker::svdq_gemm_w4a4_lora(qa, sa, wq_kn, ws, s2,
  * second, lora_act, up, bias)` (reference svdq_fused.py:379-383, kernel
  * :180-238) and the baseline chain `_gemm_w4a4` + scale + low-rank + bias of
- * `SvdqLinear.forward` (svdq_native.py:148-155). gelu != 0 applies
- * GELU(tanh) after the bias. */
-int gwb_svdq_w4a4_gemm(const void* codes, const void* ascale, const void* w_q8,
-                       const float* w_scale_gn, const void* la, const void* proj_up,
+ * `SvdqLinear.forward` (svdq_native.py:148-155). Operands in GEMM operand
+ * form; gelu != 0 applies GELU(tanh) after the bias. */
+int gwb_svdq_w4a4_gemm(const void* a_q8, const void* a_scale_k8, const void* w_q8,
+                       const void* w_scale_k8, const void* la, const void* proj_up,
                        const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
                        int gelu, void* out, void* stream);
 
-/* Debug/parity entry (no reference counterpart beyond the int32 group sums
- * the reference's GEMM forms internally, svdq_fused.py:213-222): the same
- * tcgen05 GEMM with the epilogue replaced by a dump of every 64-group s32
- * partial sum, partials s32 [K/64, M, N]. */
-int gwb_svdq_w4a4_group_partials(const void* codes, const void* w_q8, int64_t M, int64_t N,
+/* Debug/parity entry (no reference counterpart beyond the group sums the
+ * reference's GEMM forms internally, svdq_fused.py:213-222): the same
+ * tcgen05 GEMM with the epilogue replaced by a dump of every 64-group integer
+ * partial sum, partials s32 [G, M, N]. */
+int gwb_svdq_w4a4_group_partials(const void* a_q8, const void* w_q8, int64_t M, int64_t N,
                                  int64_t K, int32_t* partials, void* stream);
 
-/* Whole SvdqLinear forward (reference svdq_native.py:140-156): quantise +
- * GEMM. The caller supplies the scratch buffers codes / ascale / la (sizes
- * as above). */
+/* Whole SvdqLinear forward (reference svdq_native.py:140-156): quantise to
+ * operand form + GEMM. The caller supplies the scratch buffers a_q8 [M, K],
+ * a_scale_k8 [G, M, 8] and la [M, rank_pad]. */
 int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_down_t,
-                         const void* w_q8, const float* w_scale_gn, const void* proj_up,
+                         const void* w_q8, const void* w_scale_k8, const void* proj_up,
                          const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
-                         int gelu, void* codes, void* ascale, void* la, void* out,
+                         int gelu, void* a_q8, void* a_scale_k8, void* la, void* out,
                          void* stream);
 
 /* No counterpart in the reference. The same computation as
@@ -87,13 +97,13 @@ int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_dow
  * device memory belongs to another framework's pool or a fixed start-up
  * budget, or their serving loop forbids cudaMalloc once running): the
  * intermediates live in a 32 MiB array inside the library, held on every GPU
- * that loads it until exit. Needs M*(K/2) + M*(K/64)*2 + M*rank_pad*2 bytes
+ * that loads it until exit. Needs M*K + M*(K/64)*16 + M*rank_pad*2 bytes
  * (each part rounded up to 256); larger calls return GWB_E_CAPACITY. Calls
  * share the array: work from calls that overlap on the GPU races. The first
  * call on a device looks up the array's address; make it before any stream
  * capture. Allocates nothing. */
 int gwb_svdq_w4a4_linear_noalloc(const void* x, const void* smooth, const void* proj_down_t,
-                                 const void* w_q8, const float* w_scale_gn,
+                                 const void* w_q8, const void* w_scale_k8,
                                  const void* proj_up, const void* bias, int64_t M, int64_t N,
                                  int64_t K, int rank_pad, int gelu, void* out, void* stream);
 

@@ -73,53 +73,69 @@ int gwb_svdq_w4a4_quant(const void* x, const void* smooth, const void* proj_down
       (reinterpret_cast<uintptr_t>(ascale) & 1u))
     return GWB_E_ALIGN;
   return gwb::launch_act_int4(x, smooth, rank_pad ? proj_down_t : nullptr, codes, ascale,
-                              rank_pad ? la : nullptr, (int)M, (int)K, rank_pad, S(stream));
+                              rank_pad ? la : nullptr, (int)M, (int)K, rank_pad, false, S(stream));
 }
 
-int gwb_svdq_w4a4_gemm(const void* codes, const void* ascale, const void* w_q8,
-                       const float* w_scale_gn, const void* la, const void* proj_up,
-                       const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
-                       int gelu, void* out, void* stream) {
+int gwb_svdq_w4a4_quant_mma(const void* x, const void* smooth, const void* proj_down_t,
+                            int64_t M, int64_t K, int rank_pad, void* a_q8, void* a_scale_k8,
+                            void* la, void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  if (!fits_int(M) || !fits_int(K) || K % 64 || (K / 64) * M > 0x7fffffff) return GWB_E_SHAPE;
+  if (rank_pad < 0 || rank_pad > 64 || rank_pad % 16) return GWB_E_SHAPE;
+  if (rank_pad > 0 && (!proj_down_t || !la)) return GWB_E_SHAPE;
+  if (!al16(x) || !al16(a_q8) || !al16(a_scale_k8) || (smooth && !al16(smooth)) ||
+      (proj_down_t && !al16(proj_down_t)) || (la && !al16(la)))
+    return GWB_E_ALIGN;
+  return gwb::launch_act_int4(x, smooth, rank_pad ? proj_down_t : nullptr, a_q8, a_scale_k8,
+                              rank_pad ? la : nullptr, (int)M, (int)K, rank_pad, true, S(stream));
+}
+
+int gwb_svdq_w4a4_to_operand(const void* codes, const void* scale, int64_t R, int64_t K,
+                             void* q8, void* scale_k8, void* stream) {
+  if (R == 0) return GWB_SUCCESS;
+  if (!fits_int(R) || !fits_int(K) || K % 64 || (K / 64) * R > 0x7fffffff) return GWB_E_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(codes) & 3u) || (reinterpret_cast<uintptr_t>(q8) & 7u) ||
+      (reinterpret_cast<uintptr_t>(scale) & 1u) || !al16(scale_k8))
+    return GWB_E_ALIGN;
+  return gwb::launch_int4_to_operand(codes, scale, q8, scale_k8, (int)R, (int)K, S(stream));
+}
+
+int gwb_svdq_w4a4_gemm(const void* a_q8, const void* a_scale_k8, const void* w_q8,
+                       const void* w_scale_k8, const void* la, const void* proj_up,
+                       const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad, int gelu,
+                       void* out, void* stream) {
   if (M == 0) return GWB_SUCCESS;
   int rc = check_w4a4_shape(M, N, K, rank_pad);
   if (rc) return rc;
-  gwb::W4A4Args a{codes, ascale, w_q8, w_scale_gn, la, proj_up, bias, out, nullptr,
+  gwb::W4A4Args a{a_q8, a_scale_k8, w_q8, w_scale_k8, la, proj_up, bias, out, nullptr,
                   (int)M, (int)N, (int)K, rank_pad, gelu ? 1 : 0};
   return gwb::launch_gemm_w4a4(a, S(stream));
 }
 
-int gwb_svdq_w4a4_group_partials(const void* codes, const void* w_q8, int64_t M, int64_t N,
+int gwb_svdq_w4a4_group_partials(const void* a_q8, const void* w_q8, int64_t M, int64_t N,
                                  int64_t K, int32_t* partials, void* stream) {
   if (M == 0) return GWB_SUCCESS;
   int rc = check_w4a4_shape(M, N, K, 0);
   if (rc) return rc;
   if ((K / 64) * M * N > (int64_t)1 << 31) return GWB_E_CAPACITY;
-  // the partial dump path reads no scales; pass the codes pointer as a
-  // 16-byte-aligned placeholder for the unused scale operands
-  gwb::W4A4Args a{codes, codes, w_q8, reinterpret_cast<const float*>(w_q8), nullptr,
-                  nullptr, nullptr, nullptr, partials, (int)M, (int)N, (int)K, 0, 0};
+  gwb::W4A4Args a{a_q8, nullptr, w_q8, nullptr, nullptr, nullptr, nullptr, nullptr, partials,
+                  (int)M, (int)N, (int)K, 0, 0};
   return gwb::launch_gemm_w4a4(a, S(stream));
 }
 
 int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_down_t,
-                         const void* w_q8, const float* w_scale_gn, const void* proj_up,
+                         const void* w_q8, const void* w_scale_k8, const void* proj_up,
                          const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
-                         int gelu, void* codes, void* ascale, void* la, void* out,
+                         int gelu, void* a_q8, void* a_scale_k8, void* la, void* out,
                          void* stream) {
   if (M == 0) return GWB_SUCCESS;
   int rc = check_w4a4_shape(M, N, K, rank_pad);
   if (rc) return rc;
-  rc = gwb_svdq_w4a4_quant(x, smooth, proj_down_t, M, K, rank_pad, codes, ascale, la, stream);
+  rc = gwb_svdq_w4a4_quant_mma(x, smooth, proj_down_t, M, K, rank_pad, a_q8, a_scale_k8, la,
+                               stream);
   if (rc) return rc;
-  return gwb_svdq_w4a4_gemm(codes, ascale, w_q8, w_scale_gn, la, proj_up, bias, M, N, K,
+  return gwb_svdq_w4a4_gemm(a_q8, a_scale_k8, w_q8, w_scale_k8, la, proj_up, bias, M, N, K,
                             rank_pad, gelu, out, stream);
-}
-
-int gwb_svdq_w4a4_weight_expand(const void* w_codes, int64_t N, int64_t K, void* w_q8,
-                                void* stream) {
-  if (N == 0) return GWB_SUCCESS;
-  if (!fits_int(N) || !fits_int(K)) return GWB_E_SHAPE;
-  return gwb::launch_w4a4_weight_expand(w_codes, w_q8, N, K, S(stream));
 }
 
 int gwb_w8a8_quant(const void* x, int64_t M, int64_t K, void* q, void* scale, void* stream) {

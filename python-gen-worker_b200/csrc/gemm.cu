@@ -70,8 +70,9 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                  int M, int N, int K, int gelu) {
   using namespace w8;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  // 1024-byte alignment by offsetting the __shared__ array itself, so the
+  // compiler keeps emitting shared-space (not generic) loads and stores
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
@@ -173,133 +174,55 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 // ======================================================================
 namespace w4 {
 constexpr int BN = 128;
-constexpr int PSTAGES = 4;                 // packed A staging ring (TMA destination)
-constexpr int USTAGES = 4;                 // operand ring read by the MMA
-constexpr int PA_BYTES = kBM * kBK / 2;    // 8 KB packed A per k-block
-constexpr int UA_BYTES = kBM * kBK;        // 16 KB e4m3 A (unpacked here)
-constexpr int UB_BYTES = BN * kBK;         // 16 KB e4m3 B (TMA from the expanded weight)
-// Scale operands of one group: A_s [128 rows x 16 k] and B_s [BN x 16 k] f16,
-// no-swizzle K-major core-matrix layout, only k = 0 non-zero.
-constexpr int SA_BYTES = kBM * 16 * 2;     // 4 KB
-constexpr int SB_BYTES = BN * 16 * 2;      // 4 KB
-constexpr int SGROUP_BYTES = SA_BYTES + SB_BYTES;
-constexpr int USTAGE_BYTES = UA_BYTES + UB_BYTES + 2 * SGROUP_BYTES;   // 48 KB
-constexpr int SMEM_BYTES = USTAGES * USTAGE_BYTES + PSTAGES * PA_BYTES + 1024 + 512;
+constexpr int STAGES = 4;                  // operand ring (all TMA-fed)
+constexpr int A_BYTES = kBM * kBK;         // 16 KB e4m3 A (activation operand form)
+constexpr int B_BYTES = BN * kBK;          // 16 KB e4m3 B (expanded weight)
+// Scale operand of one group and side: [128 rows x 16 k] f16, no-swizzle
+// K-major. TMA writes the k = 0..7 half (one 16-byte row per matrix row, only
+// k = 0 non-zero); the k = 8..15 half is a 2 KB zero block LBO = 2 KB away.
+constexpr int SOP_DATA = 128 * 16;         // 2 KB
+constexpr int SOP_BYTES = 2 * SOP_DATA;    // 4 KB incl. the zero half
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + 4 * SOP_BYTES;   // 48 KB
+constexpr int TX_BYTES = A_BYTES + B_BYTES + 4 * SOP_DATA;       // 40 KB by TMA
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 // TMEM: [0, 2*BN) f32 group sums V0/V1, [2*BN, 4*BN) f32 scale products S0/S1
 constexpr int TMEM_COLS = 512;
-constexpr int UNPACK_THREADS = 64;         // warps 2-3
-constexpr int EPI_WARPS = 8;               // warps 4-11
+constexpr int EPI_WARPS = 8;               // warps 4-11 (warpgroups 1-2)
 constexpr int EC = BN / 2;                 // columns per epilogue warp
-constexpr int THREADS = 128 + 32 * EPI_WARPS;
-// The weight side holds q as an e4m3 integer and the activation side q*2^-9
-// (an e4m3 subnormal), so each group sum is 2^-9 * v; B_s carries
-// w_scale * 2^9 so that S = a_scale * w_scale * 2^9 undoes it exactly.
-constexpr float kWScaleMul = 512.0f;
+constexpr int THREADS = 128 + 32 * EPI_WARPS;   // warps 2-3 idle: warpgroup 0 padding
 }  // namespace w4
 
 static_assert(w4::SMEM_BYTES <= 232448, "W4A4 shared memory exceeds 227 KB");
 
-// 8 sign-magnitude nibbles (element 0 in the low nibble of byte 0) -> 8 e4m3
-// bytes s000_0mmm = (-1)^s * |q| * 2^-9 (e4m3 subnormals; exact). Output
-// order (q0 q2 q4 q6)(q1 q3 q5 q7): the same permutation inside every
-// 8-element block of A and B (the expanded weight uses it too), which leaves
-// every 64-group dot product unchanged.
-__device__ __forceinline__ void unpack8_e4m3(uint32_t w, uint32_t& o0, uint32_t& o1) {
-  o0 = (w & 0x07070707u) | ((w << 4) & 0x80808080u);
-  o1 = ((w >> 4) & 0x07070707u) | (w & 0x80808080u);
-}
-
-// Unpack 128 rows of 64 packed bytes (row-major, no swizzle) into rows of 128
-// e4m3 bytes in the SWIZZLE_128B K-major layout. 512 16-byte chunks over the
-// 64 unpack threads: all 8 loads of a thread are issued before any store.
-__device__ __forceinline__ void unpack_tile(const uint8_t* __restrict__ src, uint8_t* dst,
-                                            int tid) {
-  constexpr int kChunks = kBM * 4 / w4::UNPACK_THREADS;   // 8
-  uint4 p[kChunks];
-#pragma unroll
-  for (int j = 0; j < kChunks; ++j) {
-    const int i = tid + j * w4::UNPACK_THREADS;
-    p[j] = *reinterpret_cast<const uint4*>(src + (i >> 2) * 64 + (i & 3) * 16);
-  }
-#pragma unroll
-  for (int j = 0; j < kChunks; ++j) {
-    const int i = tid + j * w4::UNPACK_THREADS;
-    const int r = i >> 2, cj = i & 3;
-    uint4 o0, o1;
-    unpack8_e4m3(p[j].x, o0.x, o0.y);
-    unpack8_e4m3(p[j].y, o0.z, o0.w);
-    unpack8_e4m3(p[j].z, o1.x, o1.y);
-    unpack8_e4m3(p[j].w, o1.z, o1.w);
-    *reinterpret_cast<uint4*>(dst + swz128(r, cj * 32)) = o0;
-    *reinterpret_cast<uint4*>(dst + swz128(r, cj * 32 + 16)) = o1;
-  }
-}
-
-// Shared-memory descriptor, K-major, no swizzle: 8-row x 16-byte core
-// matrices; the two k-halves of a row block are LBO = 128 B apart and
-// consecutive 8-row blocks SBO = 256 B apart (layout type 0).
-__device__ __forceinline__ uint64_t sdesc_k16_noswz(uint32_t saddr) {
+// Shared-memory descriptor of a scale operand: K-major, no swizzle, 8-row x
+// 16-byte core matrices stored contiguously (SBO = 128 B between 8-row
+// blocks), the k = 8..15 half LBO = 2 KB away (layout type 0).
+__device__ __forceinline__ uint64_t sdesc_scale(uint32_t saddr) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)(128u >> 4) << 16;
-  d |= (uint64_t)(256u >> 4) << 32;
+  d |= (uint64_t)(w4::SOP_DATA >> 4) << 16;
+  d |= (uint64_t)(128u >> 4) << 32;
   d |= (uint64_t)1 << 46;
   return d;
 }
 
-// byte offset of element (row r, k = 0) in that layout
-__device__ __forceinline__ uint32_t sofs_k0(int r) { return (r >> 3) * 256 + (r & 7) * 16; }
-
-// e4m3 bytes of the integers 0..7 (normal numbers; 0 -> 0x00)
-__device__ __forceinline__ uint32_t e4m3_int(uint32_t m) {
-  // 0, 1.0, 2.0, 3.0, 4.0, 5.0, 6.0, 7.0
-  return __byte_perm(0x44403800u, 0x4E4C4A48u, m);
-}
-
-// Load-time weight expansion: packed sign-magnitude nibbles u8 [N, K/2] ->
-// e4m3 integers u8 [N, K] in the within-8 order of unpack8_e4m3.
-__global__ void w4a4_weight_expand_kernel(const uint32_t* __restrict__ packed,
-                                          uint2* __restrict__ out, int64_t nwords) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nwords;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const uint32_t w = packed[i];
-    uint32_t o[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {   // h = 0: low nibbles (even k), 1: high nibbles
-      uint32_t r = 0;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const uint32_t n = (w >> (8 * b + 4 * h)) & 0xFu;
-        const uint32_t e = e4m3_int(n & 7u) | ((n & 8u) ? 0x80u : 0u);
-        r |= (e & 0xFFu) << (8 * b);
-      }
-      o[h] = r;
-    }
-    out[i] = make_uint2(o[0], o[1]);
-  }
-}
-
 __global__ void __launch_bounds__(w4::THREADS, 1)
 gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmAS, const __grid_constant__ CUtensorMap tmBS,
                  const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmUP,
-                 const __half* __restrict__ a_scale, const float* __restrict__ w_scale_gn,
                  const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out,
                  int32_t* __restrict__ partials, int M, int N, int K, int rank_pad, int gelu) {
   using namespace w4;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
-  uint8_t* ustage = smem;
-  uint8_t* pstage = smem + USTAGES * USTAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pstage + PSTAGES * PA_BYTES);
-  uint64_t* p_full = bars;
-  uint64_t* p_empty = p_full + PSTAGES;
-  uint64_t* u_full = p_empty + PSTAGES;     // 2 arrivals: unpack warps + B TMA
-  uint64_t* u_empty = u_full + USTAGES;
-  uint64_t* acc_full = u_empty + USTAGES;   // [2]
+  // 1024-byte alignment by offsetting the __shared__ array itself, so the
+  // compiler keeps emitting shared-space (not generic) loads and stores
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;                    // [STAGES]
+  uint64_t* empty = full + STAGES;          // [STAGES]
+  uint64_t* acc_full = empty + STAGES;      // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  uint32_t* unpack_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
@@ -308,13 +231,22 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const bool dump = partials != nullptr;
   const int has_lr = (!dump && rank_pad > 0) ? 1 : 0;
 
+  // zero halves of the scale operands (never written by TMA)
+  for (int st = 0; st < STAGES; ++st)
+    for (int o = 0; o < 4; ++o) {
+      uint4* z = reinterpret_cast<uint4*>(smem + st * STAGE_BYTES + A_BYTES + B_BYTES +
+                                          o * SOP_BYTES + SOP_DATA);
+      for (int i = threadIdx.x; i < SOP_DATA / 16; i += THREADS) z[i] = make_uint4(0, 0, 0, 0);
+    }
+  fence_proxy_async_smem();
   if (threadIdx.x == 0) {
-    for (int i = 0; i < PSTAGES; ++i) { mbar_init(&p_full[i], 1); mbar_init(&p_empty[i], 1); }
-    for (int i = 0; i < USTAGES; ++i) { mbar_init(&u_full[i], 2); mbar_init(&u_empty[i], 1); }
+    for (int i = 0; i < STAGES; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], EPI_WARPS); }
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmAS);
+    tma_prefetch_desc(&tmBS);
   }
   if (warp == 1) { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
   tc_fence_before();
@@ -322,26 +254,36 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) GWB_TRACE_AT(7, 0);
-
+  // register hand-off: the launch gives 384 x 168 = 64512 registers;
+  // warpgroup 0 (producer, MMA, two idle warps) drops to 40 (5120) and the
+  // two epilogue warpgroups rise to 232 (59392): 64512 in total
+  if (warp < 4) {
+  regs_dec<40>();
   if (warp == 0 && lane == 0) {
     // ---------------------------------------------------------------- TMA
     if (has_lr) {
-      // low-rank operands go straight into operand stage 0 (ring slot 0)
-      mbar_arrive_expect_tx(&u_full[0], kBM * 128 + BN * 128);
-      mbar_arrive(&u_full[0]);
-      tma_load_2d(ustage, &tmLA, &u_full[0], 0, m0);
-      tma_load_2d(ustage + UA_BYTES, &tmUP, &u_full[0], 0, n0);
+      // low-rank operands go straight into stage 0 (ring slot 0)
+      mbar_arrive_expect_tx(&full[0], kBM * 128 + BN * 128);
+      tma_load_2d(smem, &tmLA, &full[0], 0, m0);
+      tma_load_2d(smem + A_BYTES, &tmUP, &full[0], 0, n0);
     }
     for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % PSTAGES;
-      if (!mbar_wait(&p_empty[s], ((kb / PSTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
+      const int ui = kb + has_lr, s = ui % STAGES;
+      if (!mbar_wait(&empty[s], ((ui / STAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
       GWB_TRACE_AT(0, kb);
-      mbar_arrive_expect_tx(&p_full[s], PA_BYTES);
-      tma_load_2d(pstage + s * PA_BYTES, &tmA, &p_full[s], kb * (kBK / 2), m0);
-      const int ui = kb + has_lr, u = ui % USTAGES;
-      if (!mbar_wait(&u_empty[u], ((ui / USTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
-      mbar_arrive_expect_tx(&u_full[u], UB_BYTES);
-      tma_load_2d(ustage + u * USTAGE_BYTES + UA_BYTES, &tmB, &u_full[u], kb * kBK, n0);
+      uint8_t* st = smem + s * STAGE_BYTES;
+      mbar_arrive_expect_tx(&full[s], dump ? A_BYTES + B_BYTES : TX_BYTES);
+      tma_load_2d(st, &tmA, &full[s], kb * kBK, m0);
+      tma_load_2d(st + A_BYTES, &tmB, &full[s], kb * kBK, n0);
+      if (!dump) {
+        uint8_t* so = st + A_BYTES + B_BYTES;
+#pragma unroll
+        for (int gs = 0; gs < 2; ++gs) {
+          const int g = 2 * kb + gs;
+          tma_load_2d(so + (2 * gs) * SOP_BYTES, &tmAS, &full[s], 0, g * M + m0);
+          tma_load_2d(so + (2 * gs + 1) * SOP_BYTES, &tmBS, &full[s], 0, g * N + n0);
+        }
+      }
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------------- MMA
@@ -351,27 +293,26 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     bool ok = true;
     if (has_lr) {
       // group slot 0 <- la · proj_upᵀ (f32), into accumulator buffer 0
-      if (!mbar_wait(&u_full[0], 0, GWB_ERR_TIMEOUT_MMA)) ok = false;
+      if (!mbar_wait(&full[0], 0, GWB_ERR_TIMEOUT_MMA)) ok = false;
       if (ok && !mbar_wait(&acc_empty[0], 1, GWB_ERR_TIMEOUT_MMA)) ok = false;
       if (ok) {
         tc_fence_after();
-        const uint32_t a_base = smem_u32(ustage), b_base = a_base + UA_BYTES;
+        const uint32_t a_base = smem_u32(smem), b_base = a_base + A_BYTES;
         for (int k = 0; k < rank_pad / 16; ++k)
           mma_f16(tmem, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k), idesc_lr,
                   k > 0 ? 1u : 0u);
         mma_commit(&acc_full[0]);
-        mma_commit(&u_empty[0]);
+        mma_commit(&empty[0]);
       }
     }
     for (int kb = 0; kb < nk && ok; ++kb) {
-      const int ui = kb + has_lr;
-      const int u = ui % USTAGES;
-      if (!mbar_wait(&u_full[u], (ui / USTAGES) & 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
+      const int ui = kb + has_lr, s = ui % STAGES;
+      if (!mbar_wait(&full[s], (ui / STAGES) & 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
       GWB_TRACE_AT(1, kb);
       tc_fence_after();
-      const uint32_t a_base = smem_u32(ustage + u * USTAGE_BYTES);
-      const uint32_t b_base = a_base + UA_BYTES;
-      const uint32_t s_base = b_base + UB_BYTES;
+      const uint32_t a_base = smem_u32(smem + s * STAGE_BYTES);
+      const uint32_t b_base = a_base + A_BYTES;
+      const uint32_t s_base = b_base + B_BYTES;
       for (int gs = 0; gs < 2 && ok; ++gs) {
         const int gi = kb * 2 + gs + has_lr;
         const int b = gi & 1;
@@ -382,84 +323,25 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         mma_f8(d, sdesc_k128(a_base + 64 * gs), sdesc_k128(b_base + 64 * gs), idesc, 0u);
         mma_f8(d, sdesc_k128(a_base + 64 * gs + 32), sdesc_k128(b_base + 64 * gs + 32), idesc, 1u);
         if (!dump) {
-          // S_b = a_scale[:, g] ⊗ (w_scale[:, g] * 2^9), exact in f32 (11-bit x 11-bit)
-          const uint32_t sa = s_base + gs * SGROUP_BYTES;
-          mma_f16(tmem + 2 * BN + b * BN, sdesc_k16_noswz(sa), sdesc_k16_noswz(sa + SA_BYTES),
-                  idesc_s, 0u);
+          // S_b = a_scale[:, g] ⊗ w_scale[:, g], exact in f32 (11-bit x 11-bit)
+          const uint32_t so = s_base + 2 * gs * SOP_BYTES;
+          mma_f16(tmem + 2 * BN + b * BN, sdesc_scale(so), sdesc_scale(so + SOP_BYTES), idesc_s,
+                  0u);
         }
         mma_commit(&acc_full[b]);
       }
-      mma_commit(&u_empty[u]);
+      mma_commit(&empty[s]);
     }
-  } else if (warp == 2 || warp == 3) {
-    // ---------------------------------------------------------------- unpack
-    const int tid = threadIdx.x - 64;
-    // the scale operands are zero except at k = 0: clear every stage's scale
-    // area once; later only the k = 0 column is rewritten
-    for (int u = 0; u < USTAGES; ++u) {
-      uint4* z = reinterpret_cast<uint4*>(ustage + u * USTAGE_BYTES + UA_BYTES + UB_BYTES);
-      for (int i = tid; i < 2 * SGROUP_BYTES / 16; i += UNPACK_THREADS) z[i] = make_uint4(0, 0, 0, 0);
-    }
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % PSTAGES;
-      const int ui = kb + has_lr;
-      const int u = ui % USTAGES;
-      // scale loads (global, L2-resident) first, so their latency overlaps the waits
-      __half2 av[2];
-      float w0[2], w1[2];
-      if (!dump) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int r = tid + 64 * h;
-          av[h] = __float2half2_rn(0.f);
-          if (m0 + r < M)
-            av[h] = *reinterpret_cast<const __half2*>(a_scale + (size_t)(m0 + r) * G + 2 * kb);
-          w0[h] = __ldg(w_scale_gn + (size_t)(2 * kb) * N + n0 + r);
-          w1[h] = __ldg(w_scale_gn + (size_t)(2 * kb + 1) * N + n0 + r);
-        }
-      }
-      // one thread waits, the named barrier broadcasts the outcome so both
-      // unpack warps always leave the loop together
-      if (tid == 0) {
-        bool ok = mbar_wait(&p_full[s], (kb / PSTAGES) & 1, GWB_ERR_TIMEOUT_UNPACK);
-        ok = ok && mbar_wait(&u_empty[u], ((ui / USTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_UNPACK);
-        *unpack_flag = ok ? 1u : 0u;
-      }
-      asm volatile("bar.sync 1, 64;" ::: "memory");
-      if (*reinterpret_cast<volatile uint32_t*>(unpack_flag) == 0u) break;
-      if (tid == 0) GWB_TRACE_AT(3, kb);
-      uint8_t* dst = ustage + u * USTAGE_BYTES;
-      unpack_tile(pstage + s * PA_BYTES, dst, tid);
-      if (!dump) {
-        // k = 0 column of this k-block's two scale-operand pairs
-        uint8_t* sdst = dst + UA_BYTES + UB_BYTES;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int r = tid + 64 * h;
-          *reinterpret_cast<__half*>(sdst + sofs_k0(r)) = __low2half(av[h]);
-          *reinterpret_cast<__half*>(sdst + SGROUP_BYTES + sofs_k0(r)) = __high2half(av[h]);
-          *reinterpret_cast<__half*>(sdst + SA_BYTES + sofs_k0(r)) =
-              __float2half_rn(w0[h] * kWScaleMul);
-          *reinterpret_cast<__half*>(sdst + SGROUP_BYTES + SA_BYTES + sofs_k0(r)) =
-              __float2half_rn(w1[h] * kWScaleMul);
-        }
-      }
-      fence_proxy_async_smem();
-      asm volatile("bar.sync 1, 64;" ::: "memory");
-      if (tid == 0) {
-        GWB_TRACE_AT(4, kb);
-        mbar_arrive(&p_empty[s]);
-        mbar_arrive(&u_full[u]);
-      }
-    }
-  } else if (warp >= 4) {
+  }
+  } else {
+    regs_inc<232>();
     // ---------------------------------------------------------------- epilogue
-    // Per group: load the f32 group sum V (= 2^-9 * v, exact) of this warp's
-    // 32 rows x EC columns and the scale product S = a_scale * w_scale * 2^9
-    // the tensor core wrote beside it, wait once, hand the TMEM buffer
-    // straight back to the MMA warp, then acc += V * S (one FFMA per element).
-    // Eight epilogue warps: warp 4+i reads lane quarter i%4 (tile rows
-    // 32*(i%4)..) and column slice (i/4)*EC.
+    // Per group: load the f32 group sum V (an exact integer: e4m3 operands
+    // hold the INT4 codes themselves) of this warp's 32 rows x EC columns and
+    // the scale product S = a_scale * w_scale the tensor core wrote beside it,
+    // wait once, hand the TMEM buffer straight back to the MMA warp, then
+    // acc += V * S (one FFMA per element). Warps 4..11: lane quarter warp % 4
+    // (tile rows 32*(warp%4)..), column slice ((warp-4)/4)*EC.
     const int q = warp & 3;
     const int cb = ((warp - 4) >> 2) * EC;
     const int row = m0 + 32 * q + lane;
@@ -477,46 +359,41 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       tc_fence_after();
       const uint32_t col0 = lane_base + b * BN + cb;
       const bool lr = has_lr && gi == 0;
-      const int g = gi - has_lr;
-      // two halves of 32 columns: V and S of a half are loaded together; the
-      // TMEM buffer is released once the second half's loads have landed
+      uint32_t v[EC], sc[EC];
 #pragma unroll
-      for (int h = 0; h < EC / 32; ++h) {
-        uint32_t v[32], sc[32];
-        tmem_ld32(col0 + 32 * h, v);
-        if (!lr && !dump) tmem_ld32(col0 + 2 * BN + 32 * h, sc);
-        tmem_wait_ld();
-        if (h == EC / 32 - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[b]);
-        }
-        if (lr) {
-          // f32 low-rank product la·proj_upᵀ seeds the accumulator
+      for (int c = 0; c < EC; c += 32) tmem_ld32(col0 + c, v + c);
+      if (!lr && !dump) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 2)
-            acc[16 * h + j / 2] = make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
-        } else if (dump) {
-          if (rv) {
-            uint4* dp = reinterpret_cast<uint4*>(partials + ((size_t)g * M + row) * N + n0 + cb +
-                                                 32 * h);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)   // V = 2^-9 * v, exact
-              dp[j] = make_uint4((uint32_t)__float2int_rn(__uint_as_float(v[4 * j]) * 512.0f),
-                                 (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 1]) * 512.0f),
-                                 (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 2]) * 512.0f),
-                                 (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 3]) * 512.0f));
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; j += 2)
-            acc[16 * h + j / 2] =
-                __ffma2_rn(make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])),
-                           make_float2(__uint_as_float(sc[j]), __uint_as_float(sc[j + 1])),
-                           acc[16 * h + j / 2]);
-        }
+        for (int c = 0; c < EC; c += 32) tmem_ld32(col0 + 2 * BN + c, sc + c);
       }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
       if (warp == 4 && lane == 0) GWB_TRACE_AT(6, gi);
+      if (lr) {
+        // f32 low-rank product la·proj_upᵀ seeds the accumulator
+#pragma unroll
+        for (int j = 0; j < EC; j += 2)
+          acc[j / 2] = make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+      } else if (dump) {
+        if (rv) {
+          const int g = gi - has_lr;
+          uint4* dp = reinterpret_cast<uint4*>(partials + ((size_t)g * M + row) * N + n0 + cb);
+#pragma unroll
+          for (int j = 0; j < EC / 4; ++j)
+            dp[j] = make_uint4((uint32_t)__float2int_rn(__uint_as_float(v[4 * j])),
+                               (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 1])),
+                               (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 2])),
+                               (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 3])));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < EC; j += 2)
+          acc[j / 2] = __ffma2_rn(make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])),
+                                  make_float2(__uint_as_float(sc[j]), __uint_as_float(sc[j + 1])),
+                                  acc[j / 2]);
+      }
     }
     if (ok && !dump && rv) {
 #pragma unroll
@@ -620,22 +497,33 @@ int launch_gemm_w8a8(const W8A8Args& a, cudaStream_t st) {
 int launch_gemm_w4a4(const W4A4Args& a, cudaStream_t st) {
   if (a.M <= 0 || a.K <= 0 || a.K % kBK || a.N % w4::BN) return GWB_E_SHAPE;
   if (a.rank_pad < 0 || a.rank_pad > 64 || a.rank_pad % 16) return GWB_E_SHAPE;
-  if (a.rank_pad > 0 && (!a.la || !a.up)) return GWB_E_SHAPE;
+  if (a.rank_pad > 0 && !a.partials && (!a.la || !a.up)) return GWB_E_SHAPE;
   if (!a.partials && !a.out) return GWB_E_SHAPE;
-  if (!al16(a.a_codes) || !al16(a.w_q8) || !al16(a.w_scale_gn) ||
-      (a.out && !al16(a.out)) || (a.bias && !al16(a.bias)) || (a.la && !al16(a.la)) ||
-      (a.up && !al16(a.up)) || (a.partials && !al16(a.partials)) ||
-      (reinterpret_cast<uintptr_t>(a.a_scale) & 3u))
+  const int G = a.K / 64;
+  if ((int64_t)G * a.M > 0x7fffffff || (int64_t)G * a.N > 0x7fffffff) return GWB_E_SHAPE;
+  if (!al16(a.a_q8) || !al16(a.w_q8) || (a.out && !al16(a.out)) || (a.bias && !al16(a.bias)) ||
+      (a.la && !al16(a.la)) || (a.up && !al16(a.up)) || (a.partials && !al16(a.partials)) ||
+      (!a.partials && (!al16(a.a_scale_k8) || !al16(a.w_scale_k8))))
     return GWB_E_ALIGN;
-  CUtensorMap tA, tB, tLA, tUP;
-  int rc = make_tmap(&tA, a.a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K / 2, a.M, kBK / 2,
-                     kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
+  CUtensorMap tA, tB, tAS, tBS, tLA, tUP;
+  int rc = make_tmap(&tA, a.a_q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.M, kBK, kBM,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = make_tmap(&tB, a.w_q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.N, kBK, w4::BN,
                  CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
+  tAS = tA;
+  tBS = tB;
   tLA = tA;
   tUP = tB;
+  if (!a.partials) {
+    rc = make_tmap(&tAS, a.a_scale_k8, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 8, (uint64_t)G * a.M,
+                   8, kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = make_tmap(&tBS, a.w_scale_k8, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 8, (uint64_t)G * a.N,
+                   8, w4::BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
   if (a.rank_pad > 0 && !a.partials) {
     rc = make_tmap(&tLA, a.la, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.rank_pad, a.M, 64, kBM,
                    CU_TENSOR_MAP_SWIZZLE_128B);
@@ -652,22 +540,9 @@ int launch_gemm_w4a4(const W4A4Args& a, cudaStream_t st) {
   }
   dim3 grid(a.N / w4::BN, (a.M + kBM - 1) / kBM);
   gemm_w4a4_kernel<<<grid, w4::THREADS, w4::SMEM_BYTES, st>>>(
-      tA, tB, tLA, tUP, static_cast<const __half*>(a.a_scale), a.w_scale_gn,
-      static_cast<const __nv_bfloat16*>(a.bias), static_cast<__nv_bfloat16*>(a.out), a.partials,
-      a.M, a.N, a.K, a.partials ? 0 : a.rank_pad, a.gelu);
-  return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
-}
-
-int launch_w4a4_weight_expand(const void* w_codes, void* w_q8, int64_t N, int64_t K,
-                              cudaStream_t st) {
-  if (N <= 0 || K <= 0 || K % 64) return GWB_E_SHAPE;
-  if ((reinterpret_cast<uintptr_t>(w_codes) & 3u) || (reinterpret_cast<uintptr_t>(w_q8) & 7u))
-    return GWB_E_ALIGN;
-  const int64_t nwords = N * K / 8;
-  int64_t blocks = (nwords + 255) / 256;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  w4a4_weight_expand_kernel<<<(int)blocks, 256, 0, st>>>(
-      static_cast<const uint32_t*>(w_codes), static_cast<uint2*>(w_q8), nwords);
+      tA, tB, tAS, tBS, tLA, tUP, static_cast<const __nv_bfloat16*>(a.bias),
+      static_cast<__nv_bfloat16*>(a.out), a.partials, a.M, a.N, a.K,
+      a.partials ? 0 : a.rank_pad, a.gelu);
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }
 

@@ -2,7 +2,8 @@
 // allocate device memory themselves.
 //
 // gwb_svdq_w4a4_linear needs three intermediate buffers between its two
-// kernels (INT4 codes, group scales, the low-rank activation la) and expects
+// kernels (the INT4 codes and group scales in GEMM operand form, and the
+// low-rank activation la) and expects
 // the caller to allocate them. Some callers cannot: a host runtime whose
 // device memory is owned by another framework's pool or by a fixed budget
 // set at start-up, or a serving loop that forbids cudaMalloc/cudaFree (and
@@ -13,7 +14,7 @@
 // Limits and sharing:
 //  * the array holds GWB_NOALLOC_SCRATCH_BYTES (32 MiB); every GPU on which
 //    the library's device code is loaded keeps it until the process exits;
-//  * a call needs M*(K/2) + M*(K/64)*2 + M*rank_pad*2 bytes (each part
+//  * a call needs M*K + M*(K/64)*16 + M*rank_pad*2 bytes (each part
 //    rounded up to 256); larger calls return GWB_E_CAPACITY and do nothing;
 //  * all calls on a device share the one array, and it keeps whatever the
 //    last call wrote. Both kernels overwrite every scratch byte they later
@@ -62,22 +63,22 @@ inline uint64_t round256(uint64_t v) { return (v + 255u) & ~uint64_t(255u); }
 
 extern "C" int gwb_svdq_w4a4_linear_noalloc(const void* x, const void* smooth,
                                             const void* proj_down_t, const void* w_q8,
-                                            const float* w_scale_gn, const void* proj_up,
+                                            const void* w_scale_k8, const void* proj_up,
                                             const void* bias, int64_t M, int64_t N, int64_t K,
                                             int rank_pad, int gelu, void* out, void* stream) {
   if (M == 0) return GWB_SUCCESS;
   int rc = check_w4a4_shape(M, N, K, rank_pad);
   if (rc) return rc;
-  const uint64_t codes_b = round256((uint64_t)M * (uint64_t)(K / 2));
-  const uint64_t scale_b = round256((uint64_t)M * (uint64_t)(K / 64) * 2u);
+  const uint64_t codes_b = round256((uint64_t)M * (uint64_t)K);
+  const uint64_t scale_b = round256((uint64_t)M * (uint64_t)(K / 64) * 16u);
   const uint64_t la_b = round256((uint64_t)M * (uint64_t)rank_pad * 2u);
   if (codes_b + scale_b + la_b > GWB_NOALLOC_SCRATCH_BYTES) return GWB_E_CAPACITY;
   unsigned char* base = nullptr;
   rc = noalloc_scratch(&base);
   if (rc) return rc;
-  void* codes = base;
-  void* ascale = base + codes_b;
+  void* a_q8 = base;
+  void* a_scale_k8 = base + codes_b;
   void* la = rank_pad ? static_cast<void*>(base + codes_b + scale_b) : nullptr;
-  return gwb_svdq_w4a4_linear(x, smooth, proj_down_t, w_q8, w_scale_gn, proj_up, bias, M, N,
-                              K, rank_pad, gelu, codes, ascale, la, out, stream);
+  return gwb_svdq_w4a4_linear(x, smooth, proj_down_t, w_q8, w_scale_k8, proj_up, bias, M, N,
+                              K, rank_pad, gelu, a_q8, a_scale_k8, la, out, stream);
 }

@@ -55,8 +55,8 @@ def rank_pad_of(rank: int) -> int:
 @torch.library.custom_op("gwb200::svdq_w4a4_quant", mutates_args=())
 def svdq_w4a4_quant(x2: torch.Tensor, smooth: Optional[torch.Tensor],
                     proj_down_t: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """x2 bf16 [M, K] -> (codes u8 [M, K/2], ascale f16 [M, K/64],
-    la bf16 [M, rank_pad]) with la = x2 · L1 (raw x)."""
+    """x2 bf16 [M, K] -> packed interchange form (codes u8 [M, K/2],
+    ascale f16 [M, K/64]) and la bf16 [M, rank_pad] = x2 · L1 (raw x)."""
     _need(x2, "x2", torch.bfloat16, 2)
     _need(smooth, "smooth", torch.bfloat16, 1)
     _need(proj_down_t, "proj_down_t", torch.bfloat16, 2)
@@ -82,32 +82,75 @@ def _(x2, smooth, proj_down_t):
             x2.new_empty(m, rp, dtype=torch.bfloat16))
 
 
-def expand_w4a4_weight(w_codes: torch.Tensor) -> torch.Tensor:
-    """Load-time repack of the packed INT4 weight u8 [N, K/2] into the GEMM's
-    operand form u8 [N, K] (each code an e4m3 integer, within-8 order of the
-    operand unpack), on the weight's CUDA device."""
-    _need(w_codes, "w_codes", torch.uint8, 2)
-    n, k = w_codes.shape[0], w_codes.shape[1] * 2
-    out = torch.empty(n, k, dtype=torch.uint8, device=w_codes.device)
+@torch.library.custom_op("gwb200::svdq_w4a4_quant_mma", mutates_args=())
+def svdq_w4a4_quant_mma(x2: torch.Tensor, smooth: Optional[torch.Tensor],
+                        proj_down_t: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """The same quantiser writing the GEMM operand form: a_q8 u8 [M, K]
+    (e4m3 integer codes), a_scale_k8 f16 [K/64, M, 8], la bf16 [M, rank_pad]."""
+    _need(x2, "x2", torch.bfloat16, 2)
+    _need(smooth, "smooth", torch.bfloat16, 1)
+    _need(proj_down_t, "proj_down_t", torch.bfloat16, 2)
+    m, k = x2.shape
+    rp = 0 if proj_down_t is None else int(proj_down_t.shape[0])
+    q8 = torch.empty(m, k, dtype=torch.uint8, device=x2.device)
+    sk8 = torch.empty(k // GROUP, m, 8, dtype=torch.float16, device=x2.device)
+    la = torch.empty(m, rp, dtype=torch.bfloat16, device=x2.device)
     lib = native.require()
-    native.check(lib.gwb_svdq_w4a4_weight_expand(w_codes.data_ptr(), n, k, out.data_ptr(),
-                                                 _stream()), "svdq_w4a4_weight_expand")
-    return out
+    native.check(lib.gwb_svdq_w4a4_quant_mma(x2.data_ptr(), _ptr(smooth), _ptr(proj_down_t), m, k,
+                                             rp, q8.data_ptr(), sk8.data_ptr(),
+                                             la.data_ptr() if rp else None, _stream()),
+                 "svdq_w4a4_quant_mma")
+    return q8, sk8, la
+
+
+@svdq_w4a4_quant_mma.register_fake
+def _(x2, smooth, proj_down_t):
+    m, k = x2.shape
+    rp = 0 if proj_down_t is None else int(proj_down_t.shape[0])
+    return (x2.new_empty(m, k, dtype=torch.uint8),
+            x2.new_empty(k // GROUP, m, 8, dtype=torch.float16),
+            x2.new_empty(m, rp, dtype=torch.bfloat16))
+
+
+@torch.library.custom_op("gwb200::svdq_w4a4_to_operand", mutates_args=())
+def svdq_w4a4_to_operand(codes: torch.Tensor, scale: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Packed interchange form (codes u8 [R, K/2], scale f16 [R, K/64]) ->
+    GEMM operand form (q8 u8 [R, K], scale_k8 f16 [K/64, R, 8]); weights at
+    load time or packed activations."""
+    _need(codes, "codes", torch.uint8, 2)
+    _need(scale, "scale", torch.float16, 2)
+    r, k = codes.shape[0], codes.shape[1] * 2
+    if tuple(scale.shape) != (r, k // GROUP):
+        raise SvdqB200Error(f"scale shape {tuple(scale.shape)} != {(r, k // GROUP)}")
+    q8 = torch.empty(r, k, dtype=torch.uint8, device=codes.device)
+    sk8 = torch.empty(k // GROUP, r, 8, dtype=torch.float16, device=codes.device)
+    lib = native.require()
+    native.check(lib.gwb_svdq_w4a4_to_operand(codes.data_ptr(), scale.data_ptr(), r, k,
+                                              q8.data_ptr(), sk8.data_ptr(), _stream()),
+                 "svdq_w4a4_to_operand")
+    return q8, sk8
+
+
+@svdq_w4a4_to_operand.register_fake
+def _(codes, scale):
+    r, k = codes.shape[0], codes.shape[1] * 2
+    return (codes.new_empty(r, k, dtype=torch.uint8),
+            codes.new_empty(k // GROUP, r, 8, dtype=torch.float16))
 
 
 @torch.library.custom_op("gwb200::svdq_w4a4_gemm", mutates_args=())
-def svdq_w4a4_gemm(codes: torch.Tensor, ascale: torch.Tensor, w_q8: torch.Tensor,
-                   w_scale_gn: torch.Tensor, la: Optional[torch.Tensor],
+def svdq_w4a4_gemm(a_q8: torch.Tensor, a_scale_k8: torch.Tensor, w_q8: torch.Tensor,
+                   w_scale_k8: torch.Tensor, la: Optional[torch.Tensor],
                    proj_up: Optional[torch.Tensor], bias: Optional[torch.Tensor],
                    gelu: bool) -> torch.Tensor:
-    """INT4 GEMM + group promotion + low-rank up-projection + bias
-    (+ GELU) -> bf16 [M, N]."""
-    _need(codes, "codes", torch.uint8, 2)
-    _need(ascale, "ascale", torch.float16, 2)
+    """INT4 group-64 GEMM (operand form) + promotion + low-rank up-projection
+    + bias (+ GELU) -> bf16 [M, N]."""
+    _need(a_q8, "a_q8", torch.uint8, 2)
+    _need(a_scale_k8, "a_scale_k8", torch.float16, 3)
     _need(w_q8, "w_q8", torch.uint8, 2)
-    _need(w_scale_gn, "w_scale_gn", torch.float32, 2)
+    _need(w_scale_k8, "w_scale_k8", torch.float16, 3)
     _need(bias, "bias", torch.bfloat16, 1)
-    m, k = codes.shape[0], codes.shape[1] * 2
+    m, k = a_q8.shape
     n = w_q8.shape[0]
     rp = 0
     if la is not None and proj_up is not None and la.shape[1] > 0:
@@ -116,10 +159,10 @@ def svdq_w4a4_gemm(codes: torch.Tensor, ascale: torch.Tensor, w_q8: torch.Tensor
         rp = int(la.shape[1])
         if int(proj_up.shape[1]) != rp:
             raise SvdqB200Error(f"la rank {rp} != proj_up rank {proj_up.shape[1]}")
-    out = torch.empty(m, n, dtype=torch.bfloat16, device=codes.device)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=a_q8.device)
     lib = native.require()
-    native.check(lib.gwb_svdq_w4a4_gemm(codes.data_ptr(), ascale.data_ptr(), w_q8.data_ptr(),
-                                        w_scale_gn.data_ptr(), _ptr(la) if rp else None,
+    native.check(lib.gwb_svdq_w4a4_gemm(a_q8.data_ptr(), a_scale_k8.data_ptr(), w_q8.data_ptr(),
+                                        w_scale_k8.data_ptr(), _ptr(la) if rp else None,
                                         _ptr(proj_up) if rp else None, _ptr(bias), m, n, k, rp,
                                         int(bool(gelu)), out.data_ptr(), _stream()),
                  "svdq_w4a4_gemm")
@@ -127,30 +170,29 @@ def svdq_w4a4_gemm(codes: torch.Tensor, ascale: torch.Tensor, w_q8: torch.Tensor
 
 
 @svdq_w4a4_gemm.register_fake
-def _(codes, ascale, w_q8, w_scale_gn, la, proj_up, bias, gelu):
-    return codes.new_empty(codes.shape[0], w_q8.shape[0], dtype=torch.bfloat16)
+def _(a_q8, a_scale_k8, w_q8, w_scale_k8, la, proj_up, bias, gelu):
+    return a_q8.new_empty(a_q8.shape[0], w_q8.shape[0], dtype=torch.bfloat16)
 
 
 @torch.library.custom_op("gwb200::svdq_w4a4_group_partials", mutates_args=())
-def svdq_w4a4_group_partials(codes: torch.Tensor, w_q8: torch.Tensor) -> torch.Tensor:
+def svdq_w4a4_group_partials(a_q8: torch.Tensor, w_q8: torch.Tensor) -> torch.Tensor:
     """Debug: every 64-group integer partial sum of the tcgen05 GEMM,
-    s32 [K/64, M, N] (w_q8 = expand_w4a4_weight(weight))."""
-    _need(codes, "codes", torch.uint8, 2)
+    s32 [K/64, M, N] (operand-form inputs)."""
+    _need(a_q8, "a_q8", torch.uint8, 2)
     _need(w_q8, "w_q8", torch.uint8, 2)
-    m, k = codes.shape[0], codes.shape[1] * 2
+    m, k = a_q8.shape
     n = w_q8.shape[0]
-    out = torch.empty(k // GROUP, m, n, dtype=torch.int32, device=codes.device)
+    out = torch.empty(k // GROUP, m, n, dtype=torch.int32, device=a_q8.device)
     lib = native.require()
-    native.check(lib.gwb_svdq_w4a4_group_partials(codes.data_ptr(), w_q8.data_ptr(), m, n, k,
+    native.check(lib.gwb_svdq_w4a4_group_partials(a_q8.data_ptr(), w_q8.data_ptr(), m, n, k,
                                                   out.data_ptr(), _stream()),
                  "svdq_w4a4_group_partials")
     return out
 
 
 @svdq_w4a4_group_partials.register_fake
-def _(codes, w_q8):
-    return codes.new_empty(codes.shape[1] * 2 // GROUP, codes.shape[0], w_q8.shape[0],
-                           dtype=torch.int32)
+def _(a_q8, w_q8):
+    return a_q8.new_empty(a_q8.shape[1] // GROUP, a_q8.shape[0], w_q8.shape[0], dtype=torch.int32)
 
 
 # ---------------------------------------------------------------- W8A8
@@ -196,18 +238,20 @@ def _(q, scale, w_q, w_scale, bias, gelu):
 
 
 # ---------------------------------------------------------------- load-time repacks
-def prepare_w4a4_weights(w_scale: torch.Tensor, proj_down: Optional[torch.Tensor],
+def prepare_w4a4_weights(weight: Optional[torch.Tensor], w_scale: torch.Tensor,
+                         proj_down: Optional[torch.Tensor],
                          proj_up: Optional[torch.Tensor]) -> dict:
     """Load-time repack of the module buffers into the kernel operand layouts
     (the reference repacks at load too: ``to_buffers``,
     ``svdq_layout.py:473-483``):
-      weight_scale f16 [N, K/64] -> w_scale_gn f32 [K/64, N] (|scale| <= 127)
+      weight u8 [N, K/2] + weight_scale f16 [N, K/64]
+                                 -> w_q8 u8 [N, K], w_scale_k8 f16 [K/64, N, 8]
+                                    (CUDA only; None when weight is None)
       proj_down bf16 [K, r]      -> proj_down_t bf16 [rank_pad, K] (zero rows)
       proj_up bf16 [N, r]        -> proj_up_pad bf16 [N, rank_pad] (zero cols)"""
-    if w_scale.numel() and float(w_scale.float().abs().max()) > 127.0:
-        raise SvdqB200Error("weight scales above 127 are not supported (the GEMM carries "
-                            "w_scale * 2^9 in fp16)")
-    out = {"w_scale_gn": w_scale.float().t().contiguous()}
+    out: dict = {"w_q8": None, "w_scale_k8": None}
+    if weight is not None:
+        out["w_q8"], out["w_scale_k8"] = svdq_w4a4_to_operand(weight, w_scale.to(torch.float16))
     if proj_down is not None and proj_up is not None and proj_down.shape[1] > 0:
         k, r = proj_down.shape
         n = proj_up.shape[0]

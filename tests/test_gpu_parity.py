@@ -23,8 +23,16 @@ def _layer_case(m, k, n, rank, seed, lora=0, bias=True, smooth=True):
     return x, L
 
 
+def _quant_gpu_down_t(L):
+    if L["proj_down"] is None:
+        return None
+    return ops.prepare_w4a4_weights(None, L["w_scale"], L["proj_down"].cuda(),
+                                    L["proj_up"].cuda())["proj_down_t"]
+
+
 def _quant_gpu(x, L):
-    p = ops.prepare_w4a4_weights(L["w_scale"].cuda(), None if L["proj_down"] is None else L["proj_down"].cuda(),
+    p = ops.prepare_w4a4_weights(L["w_packed"].cuda(), L["w_scale"].cuda(),
+                                 None if L["proj_down"] is None else L["proj_down"].cuda(),
                                  None if L["proj_up"] is None else L["proj_up"].cuda())
     sm = None if L["smooth"] is None else L["smooth"].cuda()
     codes, ascale, la = ops.svdq_w4a4_quant(x.cuda(), sm, p["proj_down_t"])
@@ -41,6 +49,11 @@ def test_int4_activation_codes_and_scales_bit_exact(cuda_ready, m, k):
     assert torch.equal(ascale.cpu().view(torch.int16), want_scale.view(torch.int16))
     la_ref = O.lowrank_down(x, L["proj_down"])
     assert O.rel_l2(la.cpu()[:, :32], la_ref) < 1e-2
+    # the operand-form quantiser writes the same codes and scales
+    q8, sk8, la2 = ops.svdq_w4a4_quant_mma(x.cuda(), L["smooth"].cuda(), _quant_gpu_down_t(L))
+    w8, wsk8 = ops.svdq_w4a4_to_operand(codes, ascale)
+    assert torch.equal(q8, w8) and torch.equal(sk8.view(torch.int16), wsk8.view(torch.int16))
+    assert torch.equal(la2, la)
 
 
 def test_int4_activation_without_smoothing(cuda_ready):
@@ -54,8 +67,9 @@ def test_int4_activation_without_smoothing(cuda_ready):
 @pytest.mark.parametrize("m,k,n", [(128, 128, 128), (200, 384, 256), (256, 3072, 384)])
 def test_int4_group_partials_bit_exact(cuda_ready, m, k, n):
     x, L = _layer_case(m, k, n, 0, seed=m + n)
-    _, codes, _, _ = _quant_gpu(x, L)
-    got = ops.svdq_w4a4_group_partials(codes, ops.expand_w4a4_weight(L["w_packed"].cuda()))
+    p, codes, ascale, _ = _quant_gpu(x, L)
+    a_q8, _ = ops.svdq_w4a4_to_operand(codes, ascale)
+    got = ops.svdq_w4a4_group_partials(a_q8, p["w_q8"])
     want = O.int4_group_partials(codes.cpu(), L["w_packed"])
     assert torch.equal(got.cpu(), want)
     assert native.device_error() == 0

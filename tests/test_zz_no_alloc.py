@@ -35,11 +35,11 @@ def test_noalloc_linear_matches_allocating_entry_point(cuda_ready, m, k, n, rank
     stream = torch.cuda.current_stream().cuda_stream
     x0 = O.synth_activation(m, k, seed=41)
     L = O.synth_svdq_layer(k, n, rank, seed=42, x_calib=x0)
-    p = ops.prepare_w4a4_weights(L["w_scale"].to(dev),
+    p = ops.prepare_w4a4_weights(L["w_packed"].to(dev), L["w_scale"].to(dev),
                                  None if rank == 0 else L["proj_down"].to(dev),
                                  None if rank == 0 else L["proj_up"].to(dev))
     rp = 0 if rank == 0 else int(p["proj_down_t"].shape[0])
-    w = ops.expand_w4a4_weight(L["w_packed"].to(dev))
+    w = p["w_q8"]
     smooth = L["smooth"].to(dev)
     bias = L["bias"].to(dev)
     down_t = p["proj_down_t"]
@@ -48,17 +48,17 @@ def test_noalloc_linear_matches_allocating_entry_point(cuda_ready, m, k, n, rank
 
     for seed in (43, 44):   # two calls in a row, different inputs
         x = O.synth_activation(m, k, seed=seed).to(dev)
-        codes = torch.empty(m, k // 2, dtype=torch.uint8, device=dev)
-        ascale = torch.empty(m, k // 64, dtype=torch.float16, device=dev)
+        codes = torch.empty(m, k, dtype=torch.uint8, device=dev)
+        ascale = torch.empty(k // 64, m, 8, dtype=torch.float16, device=dev)
         la = torch.empty(m, max(rp, 1), dtype=torch.bfloat16, device=dev)
         y_ref = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
         y_na = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=dev)
         _call(lib, "gwb_svdq_w4a4_linear", x.data_ptr(), smooth.data_ptr(), ptr(down_t),
-              w.data_ptr(), p["w_scale_gn"].data_ptr(), ptr(up), bias.data_ptr(), m, n, k, rp,
+              w.data_ptr(), p["w_scale_k8"].data_ptr(), ptr(up), bias.data_ptr(), m, n, k, rp,
               0, codes.data_ptr(), ascale.data_ptr(), la.data_ptr() if rp else None,
               y_ref.data_ptr(), stream)
         _call(lib, "gwb_svdq_w4a4_linear_noalloc", x.data_ptr(), smooth.data_ptr(),
-              ptr(down_t), w.data_ptr(), p["w_scale_gn"].data_ptr(), ptr(up), bias.data_ptr(),
+              ptr(down_t), w.data_ptr(), p["w_scale_k8"].data_ptr(), ptr(up), bias.data_ptr(),
               m, n, k, rp, 0, y_na.data_ptr(), stream)
         torch.cuda.synchronize()
         assert native.device_error() == 0
@@ -68,7 +68,7 @@ def test_noalloc_linear_matches_allocating_entry_point(cuda_ready, m, k, n, rank
 
 def test_noalloc_rejects_requests_beyond_its_capacity(cuda_ready):
     lib = native.require()
-    # 20000 x 3072 needs 20000*(1536+96+64) bytes > 32 MiB -> GWB_E_CAPACITY (8),
+    # 20000 x 3072 needs 20000*(3072+768+64) bytes > 32 MiB -> GWB_E_CAPACITY (8),
     # refused before any pointer is touched
     rc = lib.gwb_svdq_w4a4_linear_noalloc(None, None, None, None, None, None, None,
                                           20000, 3072, 3072, 32, 0, None, None)
