@@ -311,7 +311,7 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
                 tot += e[0].elapsed_time(e[2]) / steps
                 gemm += e[1].elapsed_time(e[2]) / steps
         ops_ = 2.0 * m * n * k
-        act_bytes = m * k * 2 + (m * k + m * k // 4 + m * r * 2 if kind == "w4a4"
+        act_bytes = m * k * 2 + (m * k // 2 + m * k // 4 + m * r * 2 if kind == "w4a4"
                                  else m * k + m * 4)
         rows.append({"kind": kind, "M": m, "K": k, "N": n, "rank": r, "gelu": gelu,
                      "ms": tot, "gemm_ms": gemm, "act_ms": tot - gemm,

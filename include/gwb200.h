@@ -6,14 +6,18 @@
  * (0 = success). Device buffers must be 16-byte aligned and row-major
  * contiguous. G = K/64 groups.
  *
- * Interchange (packed) form, as stored in checkpoints / module buffers:
- *   codes        u8   [R, K/2]   INT4 sign-magnitude nibbles (bit 3 = sign,
+ * INT4 codes (activations and weights alike):
+ *   codes        u8   [R, K/2]   sign-magnitude nibbles (bit 3 = sign,
  *                                bits 0-2 = |q|, q in -7..7), even k low
+ * Group scales, interchange form (checkpoints, module buffers, quant output):
  *   scale        f16  [R, G]     one scale per 64-group
- * GEMM operand form (what the tensor cores read; gwb_svdq_w4a4_to_operand
- * converts, gwb_svdq_w4a4_quant_mma produces it directly):
- *   q8           u8   [R, K]     each code as an e4m3 integer, elements of
- *                                every 8-block in the order 0 2 4 6 1 3 5 7
+ * INT4 codes, GEMM operand form (weights: gwb_svdq_w4a4_weight_expand at
+ * load time; activations: gwb_svdq_w4a4_quant_mma):
+ *   q8 (w_q8, a_q8) u8 [R, K]    each code as the e4m3 byte of q * 2^-9,
+ *                                elements of every 8-block in the order
+ *                                0 2 4 6 1 3 5 7
+ * Group scales, GEMM scale-operand rows (gwb_svdq_w4a4_scale_k8 converts,
+ * gwb_svdq_w4a4_quant_mma writes them directly):
  *   scale_k8     f16  [G, R, 8]  scale at k = 0, zeros at k = 1..7
  * Other tensors:
  *   x            bf16 [M, K];  smooth bf16 [K] (or NULL)
@@ -53,34 +57,51 @@ int gwb_svdq_w4a4_quant(const void* x, const void* smooth, const void* proj_down
                         void* codes, void* ascale, void* la, void* stream);
 
 /* The same quantiser (identical codes and scales) writing the GEMM operand
- * form instead (a_q8 [M, K], a_scale_k8 [G, M, 8]): the hot-path producer of
+ * form: a_q8 [M, K] and a_scale_k8 [G, M, 8]. The hot-path producer of
  * `SvdqLinear.forward` (svdq_native.py:145-147). */
 int gwb_svdq_w4a4_quant_mma(const void* x, const void* smooth, const void* proj_down_t,
                             int64_t M, int64_t K, int rank_pad,
                             void* a_q8, void* a_scale_k8, void* la, void* stream);
 
-/* Packed interchange form -> GEMM operand form for R rows (weights at load
- * time, or packed activations). Counterpart of the reference's load-time
- * repacks `to_buffers` / `to_blocked_scales` (svdq_layout.py:473-483,
- * nvfp4_quant.py:72-84). */
-int gwb_svdq_w4a4_to_operand(const void* codes, const void* scale, int64_t R, int64_t K,
-                             void* q8, void* scale_k8, void* stream);
+/* Group scales f16 [R, G] -> scale-operand rows f16 [G, R, 8] (weights at
+ * load time, or activation scales from gwb_svdq_w4a4_quant). Counterpart of
+ * the reference's load-time scale repack `to_blocked_scales`
+ * (nvfp4_quant.py:72-84). */
+int gwb_svdq_w4a4_scale_k8(const void* scale, int64_t R, int64_t K, void* scale_k8,
+                           void* stream);
+
+/* Load-time weight repack (counterpart of the reference's load-time
+ * `to_buffers` / `pack_e2m1` repacks, svdq_layout.py:473-483): packed INT4
+ * w_codes u8 [N, K/2] -> w_q8 u8 [N, K] in the GEMM operand form. */
+int gwb_svdq_w4a4_weight_expand(const void* w_codes, int64_t N, int64_t K, void* w_q8,
+                                void* stream);
 
 /* Replaces `cozy_gen_worker::svdq_gemm_w4a4_lora(qa, sa, wq_kn, ws, s2,
  * second, lora_act, up, bias)` (reference svdq_fused.py:379-383, kernel
  * :180-238) and the baseline chain `_gemm_w4a4` + scale + low-rank + bias of
- * `SvdqLinear.forward` (svdq_native.py:148-155). Operands in GEMM operand
- * form; gelu != 0 applies GELU(tanh) after the bias. */
+ * `SvdqLinear.forward` (svdq_native.py:148-155). Both operands in GEMM
+ * operand form, both scales as scale-operand rows; gelu != 0 applies
+ * GELU(tanh) after the bias. */
 int gwb_svdq_w4a4_gemm(const void* a_q8, const void* a_scale_k8, const void* w_q8,
                        const void* w_scale_k8, const void* la, const void* proj_up,
                        const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
                        int gelu, void* out, void* stream);
 
+/* The same GEMM taking the activations as packed INT4 codes [M, K/2] (the
+ * interchange form, e.g. from gwb_svdq_w4a4_quant): TMA loads the packed
+ * tiles and the kernel unpacks them to the operand layout in shared memory
+ * (the reference's `svdq_gemm_w4a4_lora` takes packed `qa`, svdq_fused.py:
+ * 379-383). */
+int gwb_svdq_w4a4_gemm_packed(const void* codes, const void* a_scale_k8, const void* w_q8,
+                              const void* w_scale_k8, const void* la, const void* proj_up,
+                              const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
+                              int gelu, void* out, void* stream);
+
 /* Debug/parity entry (no reference counterpart beyond the group sums the
  * reference's GEMM forms internally, svdq_fused.py:213-222): the same
  * tcgen05 GEMM with the epilogue replaced by a dump of every 64-group integer
  * partial sum, partials s32 [G, M, N]. */
-int gwb_svdq_w4a4_group_partials(const void* a_q8, const void* w_q8, int64_t M, int64_t N,
+int gwb_svdq_w4a4_group_partials(const void* codes, const void* w_q8, int64_t M, int64_t N,
                                  int64_t K, int32_t* partials, void* stream);
 
 /* Whole SvdqLinear forward (reference svdq_native.py:140-156): quantise to

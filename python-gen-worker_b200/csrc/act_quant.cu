@@ -73,10 +73,11 @@ __device__ __forceinline__ void quant_seg16(const uint32_t (&xw)[8], const uint3
 }
 
 // NB = padded rank / 8 (0 = no low-rank branch). MMA_FORM = false writes the
-// packed interchange form (codes u8 [M, K/2], ascale f16 [M, K/64]); true
-// writes the GEMM operand form instead: codes u8 [M, K] as e4m3 integers in
-// the within-8 operand order (expand_word_e4m3) and ascale f16 [K/64, M, 8]
-// with the scale at k = 0 and zeros at k = 1..7 (one 16-byte TMA row each).
+// interchange form: packed codes u8 [M, K/2] and ascale f16 [M, K/64].
+// MMA_FORM = true writes the GEMM operand form: codes u8 [M, K] as e4m3
+// bytes of q * 2^-9 in the within-8 operand order (unpack8_e4m3), and the
+// scales as scale-operand rows f16 [K/64, M, 8] (scale at k = 0, zeros at
+// k = 1..7: one 16-byte TMA row per matrix row).
 template <int NB, bool MMA_FORM>
 __global__ void __launch_bounds__(kActWarps * 32)
 act_int4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ smooth,
@@ -128,29 +129,38 @@ act_int4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
     __half s0, s1;
     quant_seg16(w0, sw, has_smooth, lo0, hi0, s0);
     quant_seg16(w1, sw, has_smooth, lo1, hi1, s1);
-    if constexpr (MMA_FORM) {
-      if (v0) {
-        const uint2 a = expand_word_e4m3(lo0), b = expand_word_e4m3(hi0);
-        *reinterpret_cast<uint4*>(codes + (size_t)row0 * K + k0) = make_uint4(a.x, a.y, b.x, b.y);
-        if (c == 0)
+    if (v0) {
+      if constexpr (MMA_FORM) {
+        uint4 o;
+        unpack8_e4m3(lo0, o.x, o.y);
+        unpack8_e4m3(hi0, o.z, o.w);
+        *reinterpret_cast<uint4*>(codes + (size_t)row0 * K + k0) = o;
+      } else {
+        *reinterpret_cast<uint2*>(codes + (size_t)row0 * (K / 2) + k0 / 2) = make_uint2(lo0, hi0);
+      }
+      if (c == 0) {
+        if constexpr (MMA_FORM)
           *reinterpret_cast<uint4*>(ascale + ((size_t)kc * M + row0) * 8) =
               make_uint4(__half_as_ushort(s0), 0u, 0u, 0u);
+        else
+          ascale[(size_t)row0 * G + kc] = s0;
       }
-      if (v1) {
-        const uint2 a = expand_word_e4m3(lo1), b = expand_word_e4m3(hi1);
-        *reinterpret_cast<uint4*>(codes + (size_t)row1 * K + k0) = make_uint4(a.x, a.y, b.x, b.y);
-        if (c == 0)
+    }
+    if (v1) {
+      if constexpr (MMA_FORM) {
+        uint4 o;
+        unpack8_e4m3(lo1, o.x, o.y);
+        unpack8_e4m3(hi1, o.z, o.w);
+        *reinterpret_cast<uint4*>(codes + (size_t)row1 * K + k0) = o;
+      } else {
+        *reinterpret_cast<uint2*>(codes + (size_t)row1 * (K / 2) + k0 / 2) = make_uint2(lo1, hi1);
+      }
+      if (c == 0) {
+        if constexpr (MMA_FORM)
           *reinterpret_cast<uint4*>(ascale + ((size_t)kc * M + row1) * 8) =
               make_uint4(__half_as_ushort(s1), 0u, 0u, 0u);
-      }
-    } else {
-      if (v0) {
-        *reinterpret_cast<uint2*>(codes + (size_t)row0 * (K / 2) + k0 / 2) = make_uint2(lo0, hi0);
-        if (c == 0) ascale[(size_t)row0 * G + kc] = s0;
-      }
-      if (v1) {
-        *reinterpret_cast<uint2*>(codes + (size_t)row1 * (K / 2) + k0 / 2) = make_uint2(lo1, hi1);
-        if (c == 0) ascale[(size_t)row1 * G + kc] = s1;
+        else
+          ascale[(size_t)row1 * G + kc] = s1;
       }
     }
     if constexpr (NB > 0) {
@@ -256,32 +266,25 @@ int launch_act_int4(const void* x, const void* smooth, const void* down_t, void*
                                              st);
 }
 
-// Packed interchange form -> GEMM operand form (rows R of a K-wide matrix):
-// codes u8 [R, K/2] -> e4m3 u8 [R, K]; scales f16 [R, K/64] -> f16 [K/64, R, 8].
-__global__ void int4_to_operand_kernel(const uint32_t* __restrict__ packed,
-                                       const __half* __restrict__ scale, uint2* __restrict__ q8,
-                                       uint4* __restrict__ scale_k8, int R, int K) {
-  const int64_t nwords = (int64_t)R * K / 8;
-  const int G = K / 64;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nwords; i += stride)
-    q8[i] = expand_word_e4m3(packed[i]);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)R * G;
-       i += stride) {
+// Scale interchange form f16 [R, K/64] -> GEMM scale operand rows
+// f16 [K/64, R, 8] (scale at k = 0, zeros at k = 1..7).
+__global__ void scale_k8_kernel(const __half* __restrict__ scale, uint4* __restrict__ scale_k8,
+                                int R, int G) {
+  const int64_t n = (int64_t)R * G;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / G, g = i % G;
     scale_k8[(size_t)g * R + r] = make_uint4(__half_as_ushort(scale[i]), 0u, 0u, 0u);
   }
 }
 
-int launch_int4_to_operand(const void* packed, const void* scale, void* q8, void* scale_k8,
-                           int R, int K, cudaStream_t st) {
+int launch_scale_k8(const void* scale, void* scale_k8, int R, int K, cudaStream_t st) {
   if (R <= 0 || K <= 0 || K % 64) return GWB_E_SHAPE;
-  const int64_t work = (int64_t)R * K / 8;
+  const int64_t work = (int64_t)R * (K / 64);
   int64_t blocks = (work + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  int4_to_operand_kernel<<<(int)blocks, 256, 0, st>>>(
-      static_cast<const uint32_t*>(packed), static_cast<const __half*>(scale),
-      static_cast<uint2*>(q8), static_cast<uint4*>(scale_k8), R, K);
+  scale_k8_kernel<<<(int)blocks, 256, 0, st>>>(static_cast<const __half*>(scale),
+                                               static_cast<uint4*>(scale_k8), R, K / 64);
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }
 

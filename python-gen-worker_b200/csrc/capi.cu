@@ -90,14 +90,19 @@ int gwb_svdq_w4a4_quant_mma(const void* x, const void* smooth, const void* proj_
                               rank_pad ? la : nullptr, (int)M, (int)K, rank_pad, true, S(stream));
 }
 
-int gwb_svdq_w4a4_to_operand(const void* codes, const void* scale, int64_t R, int64_t K,
-                             void* q8, void* scale_k8, void* stream) {
+int gwb_svdq_w4a4_scale_k8(const void* scale, int64_t R, int64_t K, void* scale_k8,
+                           void* stream) {
   if (R == 0) return GWB_SUCCESS;
   if (!fits_int(R) || !fits_int(K) || K % 64 || (K / 64) * R > 0x7fffffff) return GWB_E_SHAPE;
-  if ((reinterpret_cast<uintptr_t>(codes) & 3u) || (reinterpret_cast<uintptr_t>(q8) & 7u) ||
-      (reinterpret_cast<uintptr_t>(scale) & 1u) || !al16(scale_k8))
-    return GWB_E_ALIGN;
-  return gwb::launch_int4_to_operand(codes, scale, q8, scale_k8, (int)R, (int)K, S(stream));
+  if ((reinterpret_cast<uintptr_t>(scale) & 1u) || !al16(scale_k8)) return GWB_E_ALIGN;
+  return gwb::launch_scale_k8(scale, scale_k8, (int)R, (int)K, S(stream));
+}
+
+int gwb_svdq_w4a4_weight_expand(const void* w_codes, int64_t N, int64_t K, void* w_q8,
+                                void* stream) {
+  if (N == 0) return GWB_SUCCESS;
+  if (!fits_int(N) || !fits_int(K)) return GWB_E_SHAPE;
+  return gwb::launch_w4a4_weight_expand(w_codes, w_q8, N, K, S(stream));
 }
 
 int gwb_svdq_w4a4_gemm(const void* a_q8, const void* a_scale_k8, const void* w_q8,
@@ -109,18 +114,30 @@ int gwb_svdq_w4a4_gemm(const void* a_q8, const void* a_scale_k8, const void* w_q
   if (rc) return rc;
   gwb::W4A4Args a{a_q8, a_scale_k8, w_q8, w_scale_k8, la, proj_up, bias, out, nullptr,
                   (int)M, (int)N, (int)K, rank_pad, gelu ? 1 : 0};
-  return gwb::launch_gemm_w4a4(a, S(stream));
+  return gwb::launch_gemm_w4a4(a, false, S(stream));
 }
 
-int gwb_svdq_w4a4_group_partials(const void* a_q8, const void* w_q8, int64_t M, int64_t N,
+int gwb_svdq_w4a4_gemm_packed(const void* codes, const void* a_scale_k8, const void* w_q8,
+                              const void* w_scale_k8, const void* la, const void* proj_up,
+                              const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
+                              int gelu, void* out, void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  int rc = check_w4a4_shape(M, N, K, rank_pad);
+  if (rc) return rc;
+  gwb::W4A4Args a{codes, a_scale_k8, w_q8, w_scale_k8, la, proj_up, bias, out, nullptr,
+                  (int)M, (int)N, (int)K, rank_pad, gelu ? 1 : 0};
+  return gwb::launch_gemm_w4a4(a, true, S(stream));
+}
+
+int gwb_svdq_w4a4_group_partials(const void* codes, const void* w_q8, int64_t M, int64_t N,
                                  int64_t K, int32_t* partials, void* stream) {
   if (M == 0) return GWB_SUCCESS;
   int rc = check_w4a4_shape(M, N, K, 0);
   if (rc) return rc;
   if ((K / 64) * M * N > (int64_t)1 << 31) return GWB_E_CAPACITY;
-  gwb::W4A4Args a{a_q8, nullptr, w_q8, nullptr, nullptr, nullptr, nullptr, nullptr, partials,
-                  (int)M, (int)N, (int)K, 0, 0};
-  return gwb::launch_gemm_w4a4(a, S(stream));
+  gwb::W4A4Args a{codes, nullptr, w_q8, nullptr, nullptr, nullptr, nullptr, nullptr,
+                  partials, (int)M, (int)N, (int)K, 0, 0};
+  return gwb::launch_gemm_w4a4(a, true, S(stream));
 }
 
 int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_down_t,

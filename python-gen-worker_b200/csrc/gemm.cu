@@ -174,55 +174,122 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 // ======================================================================
 namespace w4 {
 constexpr int BN = 128;
-constexpr int STAGES = 4;                  // operand ring (all TMA-fed)
-constexpr int A_BYTES = kBM * kBK;         // 16 KB e4m3 A (activation operand form)
-constexpr int B_BYTES = BN * kBK;          // 16 KB e4m3 B (expanded weight)
+constexpr int PSTAGES = 4;                 // packed A staging ring (TMA)
+constexpr int USTAGES = 4;                 // operand ring read by the MMA
+constexpr int PA_BYTES = kBM * kBK / 2;    // 8 KB packed A per k-block
+constexpr int PSTAGE_BYTES = PA_BYTES;
+constexpr int UA_BYTES = kBM * kBK;        // 16 KB e4m3 A (unpacked here)
+constexpr int UB_BYTES = BN * kBK;         // 16 KB e4m3 B (TMA from the expanded weight)
 // Scale operand of one group and side: [128 rows x 16 k] f16, no-swizzle
 // K-major. TMA writes the k = 0..7 half (one 16-byte row per matrix row, only
-// k = 0 non-zero); the k = 8..15 half is a 2 KB zero block LBO = 2 KB away.
+// k = 0 non-zero); the k = 8..15 half is the shared 2 KB zero block.
 constexpr int SOP_DATA = 128 * 16;         // 2 KB
-constexpr int SOP_BYTES = 2 * SOP_DATA;    // 4 KB incl. the zero half
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES + 4 * SOP_BYTES;   // 48 KB
-constexpr int TX_BYTES = A_BYTES + B_BYTES + 4 * SOP_DATA;       // 40 KB by TMA
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int USTAGE_BYTES = UA_BYTES + UB_BYTES + 4 * SOP_DATA;    // 40 KB
+constexpr int ZERO_OFF = USTAGES * USTAGE_BYTES + PSTAGES * PSTAGE_BYTES;
+constexpr int SMEM_BYTES = ZERO_OFF + SOP_DATA + 1024 + 256;
 // TMEM: [0, 2*BN) f32 group sums V0/V1, [2*BN, 4*BN) f32 scale products S0/S1
 constexpr int TMEM_COLS = 512;
-constexpr int EPI_WARPS = 8;               // warps 4-11 (warpgroups 1-2)
+constexpr int UNPACK_WARPS = 6;            // warps 2-7 (packed activations only)
+constexpr int UNPACK_THREADS = 32 * UNPACK_WARPS;
+constexpr int EPI_WARPS = 8;               // the last two warpgroups
 constexpr int EC = BN / 2;                 // columns per epilogue warp
-constexpr int THREADS = 128 + 32 * EPI_WARPS;   // warps 2-3 idle: warpgroup 0 padding
+// packed activations: 16 warps (producer, MMA, 6 unpack, 8 epilogue);
+// operand-form activations: 12 warps (producer, MMA, 2 idle, 8 epilogue)
+template <bool A_PACKED> __host__ __device__ constexpr int threads() { return A_PACKED ? 512 : 384; }
+template <bool A_PACKED> __host__ __device__ constexpr int epi_warp0() { return A_PACKED ? 8 : 4; }
+// Both operands hold q * 2^-9 (e4m3 subnormals), so a group sum is
+// 2^-18 * v exactly; the accumulator is kept in that scale and multiplied by
+// 2^18 (exact) once at the end of the tile.
+constexpr float kUnscale = 262144.0f;      // 2^18
+constexpr float kRescale = 1.0f / 262144.0f;
 }  // namespace w4
 
 static_assert(w4::SMEM_BYTES <= 232448, "W4A4 shared memory exceeds 227 KB");
 
+// Unpack `chunks` 16-byte packed chunks (rows of 64 packed bytes, row-major,
+// no swizzle) into rows of 128 e4m3 bytes in the SWIZZLE_128B K-major layout.
+template <int kRows>
+__device__ __forceinline__ void unpack_tile(const uint8_t* __restrict__ src, uint8_t* dst,
+                                            int tid) {
+  constexpr int kChunks = kRows * 4;
+  constexpr int kPer = (kChunks + w4::UNPACK_THREADS - 1) / w4::UNPACK_THREADS;
+  uint4 p[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = tid + j * w4::UNPACK_THREADS;
+    if (i < kChunks) p[j] = *reinterpret_cast<const uint4*>(src + (i >> 2) * 64 + (i & 3) * 16);
+  }
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = tid + j * w4::UNPACK_THREADS;
+    if (i < kChunks) {
+      const int r = i >> 2, cj = i & 3;
+      uint4 o0, o1;
+      unpack8_e4m3(p[j].x, o0.x, o0.y);
+      unpack8_e4m3(p[j].y, o0.z, o0.w);
+      unpack8_e4m3(p[j].z, o1.x, o1.y);
+      unpack8_e4m3(p[j].w, o1.z, o1.w);
+      *reinterpret_cast<uint4*>(dst + swz128(r, cj * 32)) = o0;
+      *reinterpret_cast<uint4*>(dst + swz128(r, cj * 32 + 16)) = o1;
+    }
+  }
+}
+
+// Load-time weight expansion: packed sign-magnitude nibbles u8 [N, K/2] ->
+// e4m3 bytes q * 2^-9 u8 [N, K] in the operand order of unpack8_e4m3, so the
+// weight tile is TMA-loaded straight into the MMA operand layout.
+__global__ void w4a4_weight_expand_kernel(const uint32_t* __restrict__ packed,
+                                          uint2* __restrict__ out, int64_t nwords) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nwords;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    uint2 o;
+    unpack8_e4m3(packed[i], o.x, o.y);
+    out[i] = o;
+  }
+}
+
 // Shared-memory descriptor of a scale operand: K-major, no swizzle, 8-row x
 // 16-byte core matrices stored contiguously (SBO = 128 B between 8-row
-// blocks), the k = 8..15 half LBO = 2 KB away (layout type 0).
-__device__ __forceinline__ uint64_t sdesc_scale(uint32_t saddr) {
+// blocks); the k = 8..15 half is the shared zero block, `lbo` bytes away
+// (layout type 0).
+__device__ __forceinline__ uint64_t sdesc_scale(uint32_t saddr, uint32_t lbo) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)(w4::SOP_DATA >> 4) << 16;
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
   d |= (uint64_t)(128u >> 4) << 32;
   d |= (uint64_t)1 << 46;
   return d;
 }
 
-__global__ void __launch_bounds__(w4::THREADS, 1)
+// A_PACKED: activations arrive as packed INT4 codes (TMA into a staging ring,
+// expanded to the operand layout by the unpack warps); otherwise as the
+// operand form itself (u8 [M, K], TMA straight into the operand ring).
+template <bool A_PACKED>
+__global__ void __launch_bounds__(w4::threads<A_PACKED>(), 1)
 gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmAS, const __grid_constant__ CUtensorMap tmBS,
                  const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmUP,
                  const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out,
                  int32_t* __restrict__ partials, int M, int N, int K, int rank_pad, int gelu) {
   using namespace w4;
+  constexpr int THREADS = threads<A_PACKED>();
+  constexpr int EPI0 = epi_warp0<A_PACKED>();
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment by offsetting the __shared__ array itself, so the
   // compiler keeps emitting shared-space (not generic) loads and stores
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* full = bars;                    // [STAGES]
-  uint64_t* empty = full + STAGES;          // [STAGES]
-  uint64_t* acc_full = empty + STAGES;      // [2]
+  uint8_t* ustage = smem;
+  uint8_t* pstage = smem + USTAGES * USTAGE_BYTES;
+  uint8_t* zero = smem + ZERO_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(zero + SOP_DATA);
+  uint64_t* p_full = bars;                  // [PSTAGES] packed A landed (TMA)
+  uint64_t* p_empty = p_full + PSTAGES;     // [PSTAGES] unpack done reading
+  uint64_t* u_full = p_empty + PSTAGES;     // [USTAGES] unpack written + B/scales landed
+  uint64_t* u_empty = u_full + USTAGES;     // [USTAGES] MMA done reading
+  uint64_t* acc_full = u_empty + USTAGES;   // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint32_t* unpack_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
@@ -231,16 +298,15 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const bool dump = partials != nullptr;
   const int has_lr = (!dump && rank_pad > 0) ? 1 : 0;
 
-  // zero halves of the scale operands (never written by TMA)
-  for (int st = 0; st < STAGES; ++st)
-    for (int o = 0; o < 4; ++o) {
-      uint4* z = reinterpret_cast<uint4*>(smem + st * STAGE_BYTES + A_BYTES + B_BYTES +
-                                          o * SOP_BYTES + SOP_DATA);
-      for (int i = threadIdx.x; i < SOP_DATA / 16; i += THREADS) z[i] = make_uint4(0, 0, 0, 0);
-    }
+  for (int i = threadIdx.x; i < SOP_DATA / 16; i += THREADS)
+    reinterpret_cast<uint4*>(zero)[i] = make_uint4(0, 0, 0, 0);
   fence_proxy_async_smem();
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+    for (int i = 0; i < PSTAGES; ++i) { mbar_init(&p_full[i], 1); mbar_init(&p_empty[i], 1); }
+    for (int i = 0; i < USTAGES; ++i) {
+      mbar_init(&u_full[i], A_PACKED ? 2 : 1);
+      mbar_init(&u_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], EPI_WARPS); }
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -254,96 +320,142 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) GWB_TRACE_AT(7, 0);
-  // register hand-off: the launch gives 384 x 168 = 64512 registers;
-  // warpgroup 0 (producer, MMA, two idle warps) drops to 40 (5120) and the
-  // two epilogue warpgroups rise to 232 (59392): 64512 in total
-  if (warp < 4) {
-  regs_dec<40>();
-  if (warp == 0 && lane == 0) {
-    // ---------------------------------------------------------------- TMA
-    if (has_lr) {
-      // low-rank operands go straight into stage 0 (ring slot 0)
-      mbar_arrive_expect_tx(&full[0], kBM * 128 + BN * 128);
-      tma_load_2d(smem, &tmLA, &full[0], 0, m0);
-      tma_load_2d(smem + A_BYTES, &tmUP, &full[0], 0, n0);
-    }
-    for (int kb = 0; kb < nk; ++kb) {
-      const int ui = kb + has_lr, s = ui % STAGES;
-      if (!mbar_wait(&empty[s], ((ui / STAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
-      GWB_TRACE_AT(0, kb);
-      uint8_t* st = smem + s * STAGE_BYTES;
-      mbar_arrive_expect_tx(&full[s], dump ? A_BYTES + B_BYTES : TX_BYTES);
-      tma_load_2d(st, &tmA, &full[s], kb * kBK, m0);
-      tma_load_2d(st + A_BYTES, &tmB, &full[s], kb * kBK, n0);
-      if (!dump) {
-        uint8_t* so = st + A_BYTES + B_BYTES;
-#pragma unroll
-        for (int gs = 0; gs < 2; ++gs) {
-          const int g = 2 * kb + gs;
-          tma_load_2d(so + (2 * gs) * SOP_BYTES, &tmAS, &full[s], 0, g * M + m0);
-          tma_load_2d(so + (2 * gs + 1) * SOP_BYTES, &tmBS, &full[s], 0, g * N + n0);
+
+  // register hand-off. Packed activations: the launch gives 512 x 128 = 65536
+  // registers; warpgroups 0-1 (producer, MMA, unpack) drop to 56 (14336) and
+  // the two epilogue warpgroups rise to 200 (51200). Operand form: 384 x 168 =
+  // 64512; warpgroup 0 drops to 40 (5120), the epilogue rises to 232 (59392).
+  if (warp < EPI0) {
+    if constexpr (A_PACKED) regs_dec<56>();
+    else regs_dec<40>();
+    if (warp == 0 && lane == 0) {
+      // -------------------------------------------------------------- TMA
+      if (has_lr) {
+        // low-rank operands go straight into operand stage 0 (ring slot 0)
+        mbar_arrive_expect_tx(&u_full[0], kBM * 128 + BN * 128);
+        if (A_PACKED) mbar_arrive(&u_full[0]);
+        tma_load_2d(ustage, &tmLA, &u_full[0], 0, m0);
+        tma_load_2d(ustage + UA_BYTES, &tmUP, &u_full[0], 0, n0);
+      }
+      for (int kb = 0; kb < nk; ++kb) {
+        if (A_PACKED) {
+          const int s = kb % PSTAGES;
+          if (!mbar_wait(&p_empty[s], ((kb / PSTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
+          uint8_t* ps = pstage + s * PSTAGE_BYTES;
+          mbar_arrive_expect_tx(&p_full[s], PSTAGE_BYTES);
+          tma_load_2d(ps, &tmA, &p_full[s], kb * (kBK / 2), m0);
         }
-      }
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------------------------------------------------------- MMA
-    constexpr uint32_t idesc = idesc_fmt0_f32(kBM, BN);      // e4m3 x e4m3 -> f32
-    constexpr uint32_t idesc_lr = idesc_bf16(kBM, BN);
-    constexpr uint32_t idesc_s = idesc_fmt0_f32(kBM, BN);    // f16 x f16 -> f32
-    bool ok = true;
-    if (has_lr) {
-      // group slot 0 <- la · proj_upᵀ (f32), into accumulator buffer 0
-      if (!mbar_wait(&full[0], 0, GWB_ERR_TIMEOUT_MMA)) ok = false;
-      if (ok && !mbar_wait(&acc_empty[0], 1, GWB_ERR_TIMEOUT_MMA)) ok = false;
-      if (ok) {
-        tc_fence_after();
-        const uint32_t a_base = smem_u32(smem), b_base = a_base + A_BYTES;
-        for (int k = 0; k < rank_pad / 16; ++k)
-          mma_f16(tmem, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k), idesc_lr,
-                  k > 0 ? 1u : 0u);
-        mma_commit(&acc_full[0]);
-        mma_commit(&empty[0]);
-      }
-    }
-    for (int kb = 0; kb < nk && ok; ++kb) {
-      const int ui = kb + has_lr, s = ui % STAGES;
-      if (!mbar_wait(&full[s], (ui / STAGES) & 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
-      GWB_TRACE_AT(1, kb);
-      tc_fence_after();
-      const uint32_t a_base = smem_u32(smem + s * STAGE_BYTES);
-      const uint32_t b_base = a_base + A_BYTES;
-      const uint32_t s_base = b_base + B_BYTES;
-      for (int gs = 0; gs < 2 && ok; ++gs) {
-        const int gi = kb * 2 + gs + has_lr;
-        const int b = gi & 1;
-        if (!mbar_wait(&acc_empty[b], ((gi >> 1) & 1) ^ 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
-        GWB_TRACE_AT(2, gi);
-        tc_fence_after();
-        const uint32_t d = tmem + b * BN;
-        mma_f8(d, sdesc_k128(a_base + 64 * gs), sdesc_k128(b_base + 64 * gs), idesc, 0u);
-        mma_f8(d, sdesc_k128(a_base + 64 * gs + 32), sdesc_k128(b_base + 64 * gs + 32), idesc, 1u);
+        GWB_TRACE_AT(0, kb);
+        const int ui = kb + has_lr, u = ui % USTAGES;
+        if (!mbar_wait(&u_empty[u], ((ui / USTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
+        uint8_t* us = ustage + u * USTAGE_BYTES;
+        const uint32_t a_tx = A_PACKED ? 0u : (uint32_t)UA_BYTES;
+        mbar_arrive_expect_tx(&u_full[u], a_tx + (dump ? UB_BYTES : UB_BYTES + 4 * SOP_DATA));
+        if (!A_PACKED) tma_load_2d(us, &tmA, &u_full[u], kb * kBK, m0);
+        tma_load_2d(us + UA_BYTES, &tmB, &u_full[u], kb * kBK, n0);
         if (!dump) {
-          // S_b = a_scale[:, g] ⊗ w_scale[:, g], exact in f32 (11-bit x 11-bit)
-          const uint32_t so = s_base + 2 * gs * SOP_BYTES;
-          mma_f16(tmem + 2 * BN + b * BN, sdesc_scale(so), sdesc_scale(so + SOP_BYTES), idesc_s,
-                  0u);
+          uint8_t* so = us + UA_BYTES + UB_BYTES;
+#pragma unroll
+          for (int gs = 0; gs < 2; ++gs) {
+            const int g = 2 * kb + gs;
+            tma_load_2d(so + (2 * gs) * SOP_DATA, &tmAS, &u_full[u], 0, g * M + m0);
+            tma_load_2d(so + (2 * gs + 1) * SOP_DATA, &tmBS, &u_full[u], 0, g * N + n0);
+          }
         }
-        mma_commit(&acc_full[b]);
       }
-      mma_commit(&empty[s]);
+    } else if (warp == 1 && lane == 0) {
+      // -------------------------------------------------------------- MMA
+      constexpr uint32_t idesc = idesc_fmt0_f32(kBM, BN);      // e4m3 x e4m3 -> f32
+      constexpr uint32_t idesc_lr = idesc_bf16(kBM, BN);
+      constexpr uint32_t idesc_s = idesc_fmt0_f32(kBM, BN);    // f16 x f16 -> f32
+      const uint32_t zero_addr = smem_u32(zero);
+      bool ok = true;
+      if (has_lr) {
+        // group slot 0 <- la · proj_upᵀ (f32), into accumulator buffer 0
+        if (!mbar_wait(&u_full[0], 0, GWB_ERR_TIMEOUT_MMA)) ok = false;
+        if (ok && !mbar_wait(&acc_empty[0], 1, GWB_ERR_TIMEOUT_MMA)) ok = false;
+        if (ok) {
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(ustage), b_base = a_base + UA_BYTES;
+          for (int k = 0; k < rank_pad / 16; ++k)
+            mma_f16(tmem, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k), idesc_lr,
+                    k > 0 ? 1u : 0u);
+          mma_commit(&acc_full[0]);
+          mma_commit(&u_empty[0]);
+        }
+      }
+      for (int kb = 0; kb < nk && ok; ++kb) {
+        const int ui = kb + has_lr, u = ui % USTAGES;
+        if (!mbar_wait(&u_full[u], (ui / USTAGES) & 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
+        GWB_TRACE_AT(1, kb);
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(ustage + u * USTAGE_BYTES);
+        const uint32_t b_base = a_base + UA_BYTES;
+        const uint32_t s_base = b_base + UB_BYTES;
+        for (int gs = 0; gs < 2 && ok; ++gs) {
+          const int gi = kb * 2 + gs + has_lr;
+          const int b = gi & 1;
+          if (!mbar_wait(&acc_empty[b], ((gi >> 1) & 1) ^ 1, GWB_ERR_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          GWB_TRACE_AT(2, gi);
+          tc_fence_after();
+          const uint32_t d = tmem + b * BN;
+          mma_f8(d, sdesc_k128(a_base + 64 * gs), sdesc_k128(b_base + 64 * gs), idesc, 0u);
+          mma_f8(d, sdesc_k128(a_base + 64 * gs + 32), sdesc_k128(b_base + 64 * gs + 32), idesc,
+                 1u);
+          if (!dump) {
+            // S_b = a_scale[:, g] ⊗ w_scale[:, g], exact in f32 (11-bit x 11-bit)
+            const uint32_t sa = s_base + 2 * gs * SOP_DATA, sb = sa + SOP_DATA;
+            mma_f16(tmem + 2 * BN + b * BN, sdesc_scale(sa, zero_addr - sa),
+                    sdesc_scale(sb, zero_addr - sb), idesc_s, 0u);
+          }
+          mma_commit(&acc_full[b]);
+        }
+        mma_commit(&u_empty[u]);
+      }
+    } else if (A_PACKED && warp >= 2) {
+      // -------------------------------------------------------------- unpack
+      const int tid = threadIdx.x - 64;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % PSTAGES;
+        const int ui = kb + has_lr, u = ui % USTAGES;
+        // one thread waits, the named barrier broadcasts the outcome so all
+        // unpack warps always leave the loop together
+        if (tid == 0) {
+          bool ok = mbar_wait(&p_full[s], (kb / PSTAGES) & 1, GWB_ERR_TIMEOUT_UNPACK);
+          ok = ok && mbar_wait(&u_empty[u], ((ui / USTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_UNPACK);
+          *unpack_flag = ok ? 1u : 0u;
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(UNPACK_THREADS) : "memory");
+        if (*reinterpret_cast<volatile uint32_t*>(unpack_flag) == 0u) break;
+        if (tid == 0) GWB_TRACE_AT(3, kb);
+        const uint8_t* ps = pstage + s * PSTAGE_BYTES;
+        uint8_t* us = ustage + u * USTAGE_BYTES;
+        unpack_tile<kBM>(ps, us, tid);
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 1, %0;" ::"n"(UNPACK_THREADS) : "memory");
+        if (tid == 0) {
+          GWB_TRACE_AT(4, kb);
+          mbar_arrive(&p_empty[s]);
+          mbar_arrive(&u_full[u]);
+        }
+      }
     }
-  }
   } else {
-    regs_inc<232>();
+    if constexpr (A_PACKED) regs_inc<200>();
+    else regs_inc<232>();
     // ---------------------------------------------------------------- epilogue
-    // Per group: load the f32 group sum V (an exact integer: e4m3 operands
-    // hold the INT4 codes themselves) of this warp's 32 rows x EC columns and
-    // the scale product S = a_scale * w_scale the tensor core wrote beside it,
-    // wait once, hand the TMEM buffer straight back to the MMA warp, then
-    // acc += V * S (one FFMA per element). Warps 4..11: lane quarter warp % 4
-    // (tile rows 32*(warp%4)..), column slice ((warp-4)/4)*EC.
+    // Per group: load the f32 group sum V (= 2^-18 * v, exact) of this warp's
+    // 32 rows x EC columns and the scale product S = a_scale * w_scale the
+    // tensor core wrote beside it, wait once, hand the TMEM buffer straight
+    // back to the MMA warp, then acc += V * S (one FFMA per element; acc is
+    // 2^-18 times the result until the end of the tile). Epilogue warps
+    // EPI0..EPI0+7: lane quarter warp % 4 (tile rows 32*(warp%4)..), column
+    // slice ((warp-EPI0)/4)*EC.
     const int q = warp & 3;
-    const int cb = ((warp - 4) >> 2) * EC;
+    const int cb = ((warp - EPI0) >> 2) * EC;
     const int row = m0 + 32 * q + lane;
     const bool rv = row < M;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
@@ -355,7 +467,7 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     for (int gi = 0; gi < total; ++gi) {
       const int b = gi & 1;
       if (!mbar_wait(&acc_full[b], (gi >> 1) & 1, GWB_ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
-      if (warp == 4 && lane == 0) GWB_TRACE_AT(5, gi);
+      if (warp == EPI0 && lane == 0) GWB_TRACE_AT(5, gi);
       tc_fence_after();
       const uint32_t col0 = lane_base + b * BN + cb;
       const bool lr = has_lr && gi == 0;
@@ -370,22 +482,24 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
-      if (warp == 4 && lane == 0) GWB_TRACE_AT(6, gi);
+      if (warp == EPI0 && lane == 0) GWB_TRACE_AT(6, gi);
       if (lr) {
-        // f32 low-rank product la·proj_upᵀ seeds the accumulator
+        // f32 low-rank product la·proj_upᵀ seeds the accumulator (in its scale)
 #pragma unroll
         for (int j = 0; j < EC; j += 2)
-          acc[j / 2] = make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+          acc[j / 2] = make_float2(__uint_as_float(v[j]) * kRescale,
+                                   __uint_as_float(v[j + 1]) * kRescale);
       } else if (dump) {
         if (rv) {
           const int g = gi - has_lr;
           uint4* dp = reinterpret_cast<uint4*>(partials + ((size_t)g * M + row) * N + n0 + cb);
 #pragma unroll
           for (int j = 0; j < EC / 4; ++j)
-            dp[j] = make_uint4((uint32_t)__float2int_rn(__uint_as_float(v[4 * j])),
-                               (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 1])),
-                               (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 2])),
-                               (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 3])));
+            dp[j] = make_uint4(
+                (uint32_t)__float2int_rn(__uint_as_float(v[4 * j]) * kUnscale),
+                (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 1]) * kUnscale),
+                (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 2]) * kUnscale),
+                (uint32_t)__float2int_rn(__uint_as_float(v[4 * j + 3]) * kUnscale));
         }
       } else {
 #pragma unroll
@@ -401,8 +515,8 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         float f[8];
 #pragma unroll
         for (int j = 0; j < 8; j += 2) {
-          f[j] = acc[(c + j) / 2].x;
-          f[j + 1] = acc[(c + j) / 2].y;
+          f[j] = acc[(c + j) / 2].x * kUnscale;
+          f[j + 1] = acc[(c + j) / 2].y * kUnscale;
         }
         if (bias != nullptr) {
           const uint4 bw = __ldg(reinterpret_cast<const uint4*>(bias + n0 + cb + c));
@@ -494,20 +608,23 @@ int launch_gemm_w8a8(const W8A8Args& a, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }
 
-int launch_gemm_w4a4(const W4A4Args& a, cudaStream_t st) {
+int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, cudaStream_t st) {
   if (a.M <= 0 || a.K <= 0 || a.K % kBK || a.N % w4::BN) return GWB_E_SHAPE;
   if (a.rank_pad < 0 || a.rank_pad > 64 || a.rank_pad % 16) return GWB_E_SHAPE;
   if (a.rank_pad > 0 && !a.partials && (!a.la || !a.up)) return GWB_E_SHAPE;
   if (!a.partials && !a.out) return GWB_E_SHAPE;
   const int G = a.K / 64;
   if ((int64_t)G * a.M > 0x7fffffff || (int64_t)G * a.N > 0x7fffffff) return GWB_E_SHAPE;
-  if (!al16(a.a_q8) || !al16(a.w_q8) || (a.out && !al16(a.out)) || (a.bias && !al16(a.bias)) ||
+  if (!al16(a.a_codes) || !al16(a.w_q8) || (a.out && !al16(a.out)) ||
+      (a.bias && !al16(a.bias)) ||
       (a.la && !al16(a.la)) || (a.up && !al16(a.up)) || (a.partials && !al16(a.partials)) ||
       (!a.partials && (!al16(a.a_scale_k8) || !al16(a.w_scale_k8))))
     return GWB_E_ALIGN;
   CUtensorMap tA, tB, tAS, tBS, tLA, tUP;
-  int rc = make_tmap(&tA, a.a_q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.M, kBK, kBM,
-                     CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc = a_packed ? make_tmap(&tA, a.a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K / 2, a.M,
+                               kBK / 2, kBM, CU_TENSOR_MAP_SWIZZLE_NONE)
+                     : make_tmap(&tA, a.a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.M, kBK,
+                                 kBM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = make_tmap(&tB, a.w_q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.N, kBK, w4::BN,
                  CU_TENSOR_MAP_SWIZZLE_128B);
@@ -534,15 +651,31 @@ int launch_gemm_w4a4(const W4A4Args& a, cudaStream_t st) {
   }
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(gemm_w4a4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(gemm_w4a4_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         w4::SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_w4a4_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          w4::SMEM_BYTES);
     attr = true;
   }
   dim3 grid(a.N / w4::BN, (a.M + kBM - 1) / kBM);
-  gemm_w4a4_kernel<<<grid, w4::THREADS, w4::SMEM_BYTES, st>>>(
+  auto kern = a_packed ? gemm_w4a4_kernel<true> : gemm_w4a4_kernel<false>;
+  kern<<<grid, a_packed ? w4::threads<true>() : w4::threads<false>(), w4::SMEM_BYTES, st>>>(
       tA, tB, tAS, tBS, tLA, tUP, static_cast<const __nv_bfloat16*>(a.bias),
       static_cast<__nv_bfloat16*>(a.out), a.partials, a.M, a.N, a.K,
       a.partials ? 0 : a.rank_pad, a.gelu);
+  return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
+}
+
+int launch_w4a4_weight_expand(const void* w_codes, void* w_q8, int64_t N, int64_t K,
+                              cudaStream_t st) {
+  if (N <= 0 || K <= 0 || K % 64) return GWB_E_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(w_codes) & 3u) || (reinterpret_cast<uintptr_t>(w_q8) & 7u))
+    return GWB_E_ALIGN;
+  const int64_t nwords = N * K / 8;
+  int64_t blocks = (nwords + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  w4a4_weight_expand_kernel<<<(int)blocks, 256, 0, st>>>(
+      static_cast<const uint32_t*>(w_codes), static_cast<uint2*>(w_q8), nwords);
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }
 

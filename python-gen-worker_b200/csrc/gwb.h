@@ -20,14 +20,13 @@ namespace gwb {
 int launch_act_int4(const void* x, const void* smooth, const void* down_t, void* codes,
                     void* ascale, void* la, int M, int K, int rank_pad, bool mma_form,
                     cudaStream_t st);
-int launch_int4_to_operand(const void* packed, const void* scale, void* q8, void* scale_k8,
-                           int R, int K, cudaStream_t st);
+int launch_scale_k8(const void* scale, void* scale_k8, int R, int K, cudaStream_t st);
 int launch_act_int8(const void* x, void* q, void* scale, int M, int K, cudaStream_t st);
 
 struct W4A4Args {
-  const void* a_q8;        // e4m3 [M, K] activation operand form
+  const void* a_codes;     // u8 [M, K/2] packed INT4 (a_packed) or u8 [M, K] operand form
   const void* a_scale_k8;  // f16 [K/64, M, 8] (scale at k = 0)
-  const void* w_q8;        // e4m3 [N, K] expanded weight
+  const void* w_q8;        // u8 [N, K] expanded weight (launch_w4a4_weight_expand)
   const void* w_scale_k8;  // f16 [K/64, N, 8]
   const void* la;          // bf16 [M, rank_pad] or null
   const void* up;          // bf16 [N, rank_pad] or null
@@ -36,7 +35,9 @@ struct W4A4Args {
   int32_t* partials;       // optional debug: s32 [K/64, M, N]; disables the epilogue
   int M, N, K, rank_pad, gelu;
 };
-int launch_gemm_w4a4(const W4A4Args& a, cudaStream_t st);
+int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, cudaStream_t st);
+int launch_w4a4_weight_expand(const void* w_codes, void* w_q8, int64_t N, int64_t K,
+                              cudaStream_t st);
 
 
 struct W8A8Args {

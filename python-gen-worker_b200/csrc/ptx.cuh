@@ -212,30 +212,15 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// ------------------------------------------------ INT4 -> e4m3 operand form
-// e4m3 bytes of the integers 0..7 (normal numbers; 0 -> 0x00):
-// 0, 1.0, 2.0, 3.0 | 4.0, 5.0, 6.0, 7.0
-__device__ __forceinline__ uint32_t e4m3_int(uint32_t m) {
-  return __byte_perm(0x44403800u, 0x4E4C4A48u, m) & 0xFFu;
-}
-
-// One word of 8 packed sign-magnitude nibbles (element 0 in the low nibble of
-// byte 0) -> 8 e4m3 bytes holding the integers q exactly, in the GEMM operand
-// order (e0 e2 e4 e6)(e1 e3 e5 e7). The same order is used for activations
-// and weights, so every 64-group dot product is unchanged.
-__device__ __forceinline__ uint2 expand_word_e4m3(uint32_t w) {
-  uint32_t o[2];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    uint32_t r = 0;
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const uint32_t n = (w >> (8 * b + 4 * h)) & 0xFu;
-      r |= (e4m3_int(n & 7u) | ((n & 8u) << 4)) << (8 * b);
-    }
-    o[h] = r;
-  }
-  return make_uint2(o[0], o[1]);
+// ------------------------------------------------ INT4 -> e4m3 operand bytes
+// 8 sign-magnitude nibbles (element 0 in the low nibble of byte 0) -> 8 e4m3
+// bytes s000_0mmm = (-1)^s * |q| * 2^-9 (e4m3 subnormals; exact). Output
+// order (q0 q2 q4 q6)(q1 q3 q5 q7): the same permutation inside every
+// 8-element block of A and B, which leaves every 64-group dot product
+// unchanged.
+__device__ __forceinline__ void unpack8_e4m3(uint32_t w, uint32_t& o0, uint32_t& o1) {
+  o0 = (w & 0x07070707u) | ((w << 4) & 0x80808080u);
+  o1 = ((w >> 4) & 0x07070707u) | (w & 0x80808080u);
 }
 
 // ------------------------------------------------ UMMA descriptors (sm_100)

@@ -110,8 +110,8 @@ class SvdqInt4Linear(nn.Module):
         on the buffers' device)."""
         dev = self.weight.device
         if self._packed is None or self._packed["device"] != dev:
-            p = ops.prepare_w4a4_weights(self.weight, self.weight_scale, self.proj_down,
-                                         self.proj_up)
+            p = ops.prepare_w4a4_weights(self.weight_scale, self.proj_down, self.proj_up,
+                                         weight=self.weight)
             p["device"] = dev
             self._packed = p
         return self._packed
@@ -126,8 +126,8 @@ class SvdqInt4Linear(nn.Module):
         if not x2.is_contiguous():
             x2 = x2.contiguous()
         p = self.prepare()
-        a_q8, a_sk8, la = ops.svdq_w4a4_quant_mma(x2, self.smooth_factor, p["proj_down_t"])
-        y = ops.svdq_w4a4_gemm(a_q8, a_sk8, p["w_q8"], p["w_scale_k8"],
+        codes, a_sk8, la = ops.svdq_w4a4_quant_mma(x2, self.smooth_factor, p["proj_down_t"])
+        y = ops.svdq_w4a4_gemm(codes, a_sk8, p["w_q8"], p["w_scale_k8"],
                                la if p["proj_down_t"] is not None else None,
                                p["proj_up_pad"],
                                self.bias.detach() if self.bias is not None else None,

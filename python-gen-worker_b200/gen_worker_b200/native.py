@@ -32,10 +32,13 @@ _SIGNATURES = {
                             c_void_p, c_void_p, c_void_p, c_void_p],
     "gwb_svdq_w4a4_quant_mma": [c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_int,
                                 c_void_p, c_void_p, c_void_p, c_void_p],
-    "gwb_svdq_w4a4_to_operand": [c_void_p, c_void_p, c_i64, c_i64, c_void_p, c_void_p,
-                                 c_void_p],
+    "gwb_svdq_w4a4_scale_k8": [c_void_p, c_i64, c_i64, c_void_p, c_void_p],
+    "gwb_svdq_w4a4_weight_expand": [c_void_p, c_i64, c_i64, c_void_p, c_void_p],
     "gwb_svdq_w4a4_gemm": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                            c_void_p, c_i64, c_i64, c_i64, c_int, c_int, c_void_p, c_void_p],
+    "gwb_svdq_w4a4_gemm_packed": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                  c_void_p, c_i64, c_i64, c_i64, c_int, c_int, c_void_p,
+                                  c_void_p],
     "gwb_svdq_w4a4_group_partials": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_void_p,
                                      c_void_p],
     "gwb_svdq_w4a4_linear": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

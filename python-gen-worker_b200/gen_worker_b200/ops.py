@@ -85,22 +85,23 @@ def _(x2, smooth, proj_down_t):
 @torch.library.custom_op("gwb200::svdq_w4a4_quant_mma", mutates_args=())
 def svdq_w4a4_quant_mma(x2: torch.Tensor, smooth: Optional[torch.Tensor],
                         proj_down_t: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """The same quantiser writing the GEMM operand form: a_q8 u8 [M, K]
-    (e4m3 integer codes), a_scale_k8 f16 [K/64, M, 8], la bf16 [M, rank_pad]."""
+    """The same quantiser (identical codes and scales) writing the GEMM
+    operand form: a_q8 u8 [M, K] (e4m3 bytes of q * 2^-9, within-8 operand
+    order), a_scale_k8 f16 [K/64, M, 8], la bf16 [M, rank_pad]."""
     _need(x2, "x2", torch.bfloat16, 2)
     _need(smooth, "smooth", torch.bfloat16, 1)
     _need(proj_down_t, "proj_down_t", torch.bfloat16, 2)
     m, k = x2.shape
     rp = 0 if proj_down_t is None else int(proj_down_t.shape[0])
-    q8 = torch.empty(m, k, dtype=torch.uint8, device=x2.device)
+    codes = torch.empty(m, k, dtype=torch.uint8, device=x2.device)
     sk8 = torch.empty(k // GROUP, m, 8, dtype=torch.float16, device=x2.device)
     la = torch.empty(m, rp, dtype=torch.bfloat16, device=x2.device)
     lib = native.require()
     native.check(lib.gwb_svdq_w4a4_quant_mma(x2.data_ptr(), _ptr(smooth), _ptr(proj_down_t), m, k,
-                                             rp, q8.data_ptr(), sk8.data_ptr(),
+                                             rp, codes.data_ptr(), sk8.data_ptr(),
                                              la.data_ptr() if rp else None, _stream()),
                  "svdq_w4a4_quant_mma")
-    return q8, sk8, la
+    return codes, sk8, la
 
 
 @svdq_w4a4_quant_mma.register_fake
@@ -112,46 +113,47 @@ def _(x2, smooth, proj_down_t):
             x2.new_empty(m, rp, dtype=torch.bfloat16))
 
 
-@torch.library.custom_op("gwb200::svdq_w4a4_to_operand", mutates_args=())
-def svdq_w4a4_to_operand(codes: torch.Tensor, scale: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """Packed interchange form (codes u8 [R, K/2], scale f16 [R, K/64]) ->
-    GEMM operand form (q8 u8 [R, K], scale_k8 f16 [K/64, R, 8]); weights at
-    load time or packed activations."""
-    _need(codes, "codes", torch.uint8, 2)
+@torch.library.custom_op("gwb200::svdq_w4a4_scale_k8", mutates_args=())
+def svdq_w4a4_scale_k8(scale: torch.Tensor) -> torch.Tensor:
+    """Group scales f16 [R, K/64] -> GEMM scale-operand rows f16 [K/64, R, 8]
+    (weights at load time, or activation scales from ``svdq_w4a4_quant``)."""
     _need(scale, "scale", torch.float16, 2)
-    r, k = codes.shape[0], codes.shape[1] * 2
-    if tuple(scale.shape) != (r, k // GROUP):
-        raise SvdqB200Error(f"scale shape {tuple(scale.shape)} != {(r, k // GROUP)}")
-    q8 = torch.empty(r, k, dtype=torch.uint8, device=codes.device)
-    sk8 = torch.empty(k // GROUP, r, 8, dtype=torch.float16, device=codes.device)
+    r, g = scale.shape
+    out = torch.empty(g, r, 8, dtype=torch.float16, device=scale.device)
     lib = native.require()
-    native.check(lib.gwb_svdq_w4a4_to_operand(codes.data_ptr(), scale.data_ptr(), r, k,
-                                              q8.data_ptr(), sk8.data_ptr(), _stream()),
-                 "svdq_w4a4_to_operand")
-    return q8, sk8
+    native.check(lib.gwb_svdq_w4a4_scale_k8(scale.data_ptr(), r, g * GROUP, out.data_ptr(),
+                                            _stream()), "svdq_w4a4_scale_k8")
+    return out
 
 
-@svdq_w4a4_to_operand.register_fake
-def _(codes, scale):
-    r, k = codes.shape[0], codes.shape[1] * 2
-    return (codes.new_empty(r, k, dtype=torch.uint8),
-            codes.new_empty(k // GROUP, r, 8, dtype=torch.float16))
+@svdq_w4a4_scale_k8.register_fake
+def _(scale):
+    return scale.new_empty(scale.shape[1], scale.shape[0], 8, dtype=torch.float16)
 
 
-@torch.library.custom_op("gwb200::svdq_w4a4_gemm", mutates_args=())
-def svdq_w4a4_gemm(a_q8: torch.Tensor, a_scale_k8: torch.Tensor, w_q8: torch.Tensor,
-                   w_scale_k8: torch.Tensor, la: Optional[torch.Tensor],
-                   proj_up: Optional[torch.Tensor], bias: Optional[torch.Tensor],
-                   gelu: bool) -> torch.Tensor:
-    """INT4 group-64 GEMM (operand form) + promotion + low-rank up-projection
-    + bias (+ GELU) -> bf16 [M, N]."""
-    _need(a_q8, "a_q8", torch.uint8, 2)
+def expand_w4a4_weight(w_codes: torch.Tensor) -> torch.Tensor:
+    """Load-time repack of the packed INT4 weight u8 [N, K/2] into the GEMM
+    operand form u8 [N, K] (e4m3 bytes of q * 2^-9, within-8 operand order),
+    on the weight's CUDA device."""
+    _need(w_codes, "w_codes", torch.uint8, 2)
+    n, k = w_codes.shape[0], w_codes.shape[1] * 2
+    out = torch.empty(n, k, dtype=torch.uint8, device=w_codes.device)
+    lib = native.require()
+    native.check(lib.gwb_svdq_w4a4_weight_expand(w_codes.data_ptr(), n, k, out.data_ptr(),
+                                                 _stream()), "svdq_w4a4_weight_expand")
+    return out
+
+
+def _w4a4_gemm(fn: str, a: torch.Tensor, k: int, a_scale_k8, w_q8, w_scale_k8, la, proj_up,
+               bias, gelu) -> torch.Tensor:
     _need(a_scale_k8, "a_scale_k8", torch.float16, 3)
     _need(w_q8, "w_q8", torch.uint8, 2)
     _need(w_scale_k8, "w_scale_k8", torch.float16, 3)
     _need(bias, "bias", torch.bfloat16, 1)
-    m, k = a_q8.shape
+    m = a.shape[0]
     n = w_q8.shape[0]
+    if int(w_q8.shape[1]) != k:
+        raise SvdqB200Error(f"w_q8 K {w_q8.shape[1]} != activation K {k}")
     rp = 0
     if la is not None and proj_up is not None and la.shape[1] > 0:
         _need(la, "la", torch.bfloat16, 2)
@@ -159,14 +161,25 @@ def svdq_w4a4_gemm(a_q8: torch.Tensor, a_scale_k8: torch.Tensor, w_q8: torch.Ten
         rp = int(la.shape[1])
         if int(proj_up.shape[1]) != rp:
             raise SvdqB200Error(f"la rank {rp} != proj_up rank {proj_up.shape[1]}")
-    out = torch.empty(m, n, dtype=torch.bfloat16, device=a_q8.device)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=a.device)
     lib = native.require()
-    native.check(lib.gwb_svdq_w4a4_gemm(a_q8.data_ptr(), a_scale_k8.data_ptr(), w_q8.data_ptr(),
-                                        w_scale_k8.data_ptr(), _ptr(la) if rp else None,
-                                        _ptr(proj_up) if rp else None, _ptr(bias), m, n, k, rp,
-                                        int(bool(gelu)), out.data_ptr(), _stream()),
-                 "svdq_w4a4_gemm")
+    native.check(getattr(lib, fn)(a.data_ptr(), a_scale_k8.data_ptr(), w_q8.data_ptr(),
+                                  w_scale_k8.data_ptr(), _ptr(la) if rp else None,
+                                  _ptr(proj_up) if rp else None, _ptr(bias), m, n, k, rp,
+                                  int(bool(gelu)), out.data_ptr(), _stream()), fn)
     return out
+
+
+@torch.library.custom_op("gwb200::svdq_w4a4_gemm", mutates_args=())
+def svdq_w4a4_gemm(a_q8: torch.Tensor, a_scale_k8: torch.Tensor, w_q8: torch.Tensor,
+                   w_scale_k8: torch.Tensor, la: Optional[torch.Tensor],
+                   proj_up: Optional[torch.Tensor], bias: Optional[torch.Tensor],
+                   gelu: bool) -> torch.Tensor:
+    """INT4 group-64 GEMM on operand-form activations (``svdq_w4a4_quant_mma``)
+    + promotion + low-rank up-projection + bias (+ GELU) -> bf16 [M, N]."""
+    _need(a_q8, "a_q8", torch.uint8, 2)
+    return _w4a4_gemm("gwb_svdq_w4a4_gemm", a_q8, int(a_q8.shape[1]), a_scale_k8, w_q8,
+                      w_scale_k8, la, proj_up, bias, gelu)
 
 
 @svdq_w4a4_gemm.register_fake
@@ -174,25 +187,43 @@ def _(a_q8, a_scale_k8, w_q8, w_scale_k8, la, proj_up, bias, gelu):
     return a_q8.new_empty(a_q8.shape[0], w_q8.shape[0], dtype=torch.bfloat16)
 
 
+@torch.library.custom_op("gwb200::svdq_w4a4_gemm_packed", mutates_args=())
+def svdq_w4a4_gemm_packed(codes: torch.Tensor, a_scale_k8: torch.Tensor, w_q8: torch.Tensor,
+                          w_scale_k8: torch.Tensor, la: Optional[torch.Tensor],
+                          proj_up: Optional[torch.Tensor], bias: Optional[torch.Tensor],
+                          gelu: bool) -> torch.Tensor:
+    """The same GEMM on packed activation codes u8 [M, K/2] (unpacked to the
+    operand layout in shared memory)."""
+    _need(codes, "codes", torch.uint8, 2)
+    return _w4a4_gemm("gwb_svdq_w4a4_gemm_packed", codes, int(codes.shape[1]) * 2, a_scale_k8,
+                      w_q8, w_scale_k8, la, proj_up, bias, gelu)
+
+
+@svdq_w4a4_gemm_packed.register_fake
+def _(codes, a_scale_k8, w_q8, w_scale_k8, la, proj_up, bias, gelu):
+    return codes.new_empty(codes.shape[0], w_q8.shape[0], dtype=torch.bfloat16)
+
+
 @torch.library.custom_op("gwb200::svdq_w4a4_group_partials", mutates_args=())
-def svdq_w4a4_group_partials(a_q8: torch.Tensor, w_q8: torch.Tensor) -> torch.Tensor:
+def svdq_w4a4_group_partials(codes: torch.Tensor, w_q8: torch.Tensor) -> torch.Tensor:
     """Debug: every 64-group integer partial sum of the tcgen05 GEMM,
-    s32 [K/64, M, N] (operand-form inputs)."""
-    _need(a_q8, "a_q8", torch.uint8, 2)
+    s32 [K/64, M, N] (packed activation codes, expanded weight)."""
+    _need(codes, "codes", torch.uint8, 2)
     _need(w_q8, "w_q8", torch.uint8, 2)
-    m, k = a_q8.shape
+    m, k = codes.shape[0], codes.shape[1] * 2
     n = w_q8.shape[0]
-    out = torch.empty(k // GROUP, m, n, dtype=torch.int32, device=a_q8.device)
+    out = torch.empty(k // GROUP, m, n, dtype=torch.int32, device=codes.device)
     lib = native.require()
-    native.check(lib.gwb_svdq_w4a4_group_partials(a_q8.data_ptr(), w_q8.data_ptr(), m, n, k,
+    native.check(lib.gwb_svdq_w4a4_group_partials(codes.data_ptr(), w_q8.data_ptr(), m, n, k,
                                                   out.data_ptr(), _stream()),
                  "svdq_w4a4_group_partials")
     return out
 
 
 @svdq_w4a4_group_partials.register_fake
-def _(a_q8, w_q8):
-    return a_q8.new_empty(a_q8.shape[1] // GROUP, a_q8.shape[0], w_q8.shape[0], dtype=torch.int32)
+def _(codes, w_q8):
+    return codes.new_empty(codes.shape[1] * 2 // GROUP, codes.shape[0], w_q8.shape[0],
+                           dtype=torch.int32)
 
 
 # ---------------------------------------------------------------- W8A8
@@ -238,20 +269,22 @@ def _(q, scale, w_q, w_scale, bias, gelu):
 
 
 # ---------------------------------------------------------------- load-time repacks
-def prepare_w4a4_weights(weight: Optional[torch.Tensor], w_scale: torch.Tensor,
-                         proj_down: Optional[torch.Tensor],
-                         proj_up: Optional[torch.Tensor]) -> dict:
+def prepare_w4a4_weights(w_scale: Optional[torch.Tensor], proj_down: Optional[torch.Tensor],
+                         proj_up: Optional[torch.Tensor],
+                         weight: Optional[torch.Tensor] = None) -> dict:
     """Load-time repack of the module buffers into the kernel operand layouts
     (the reference repacks at load too: ``to_buffers``,
     ``svdq_layout.py:473-483``):
-      weight u8 [N, K/2] + weight_scale f16 [N, K/64]
-                                 -> w_q8 u8 [N, K], w_scale_k8 f16 [K/64, N, 8]
-                                    (CUDA only; None when weight is None)
+      weight u8 [N, K/2]         -> w_q8 u8 [N, K] (CUDA only; else None)
+      weight_scale f16 [N, K/64] -> w_scale_k8 f16 [K/64, N, 8] (CUDA only;
+                                    None when w_scale is None or on the CPU)
       proj_down bf16 [K, r]      -> proj_down_t bf16 [rank_pad, K] (zero rows)
       proj_up bf16 [N, r]        -> proj_up_pad bf16 [N, rank_pad] (zero cols)"""
-    out: dict = {"w_q8": None, "w_scale_k8": None}
-    if weight is not None:
-        out["w_q8"], out["w_scale_k8"] = svdq_w4a4_to_operand(weight, w_scale.to(torch.float16))
+    out: dict = {"w_scale_k8": None, "w_q8": None}
+    if weight is not None and weight.is_cuda:
+        out["w_q8"] = expand_w4a4_weight(weight.contiguous())
+    if w_scale is not None and w_scale.is_cuda:
+        out["w_scale_k8"] = svdq_w4a4_scale_k8(w_scale.to(torch.float16).contiguous())
     if proj_down is not None and proj_up is not None and proj_down.shape[1] > 0:
         k, r = proj_down.shape
         n = proj_up.shape[0]

@@ -26,12 +26,12 @@ def _layer_case(m, k, n, rank, seed, lora=0, bias=True, smooth=True):
 def _quant_gpu_down_t(L):
     if L["proj_down"] is None:
         return None
-    return ops.prepare_w4a4_weights(None, L["w_scale"], L["proj_down"].cuda(),
+    return ops.prepare_w4a4_weights(None, L["proj_down"].cuda(),
                                     L["proj_up"].cuda())["proj_down_t"]
 
 
 def _quant_gpu(x, L):
-    p = ops.prepare_w4a4_weights(L["w_packed"].cuda(), L["w_scale"].cuda(),
+    p = ops.prepare_w4a4_weights(L["w_scale"].cuda(),
                                  None if L["proj_down"] is None else L["proj_down"].cuda(),
                                  None if L["proj_up"] is None else L["proj_up"].cuda())
     sm = None if L["smooth"] is None else L["smooth"].cuda()
@@ -49,10 +49,16 @@ def test_int4_activation_codes_and_scales_bit_exact(cuda_ready, m, k):
     assert torch.equal(ascale.cpu().view(torch.int16), want_scale.view(torch.int16))
     la_ref = O.lowrank_down(x, L["proj_down"])
     assert O.rel_l2(la.cpu()[:, :32], la_ref) < 1e-2
-    # the operand-form quantiser writes the same codes and scales
-    q8, sk8, la2 = ops.svdq_w4a4_quant_mma(x.cuda(), L["smooth"].cuda(), _quant_gpu_down_t(L))
-    w8, wsk8 = ops.svdq_w4a4_to_operand(codes, ascale)
-    assert torch.equal(q8, w8) and torch.equal(sk8.view(torch.int16), wsk8.view(torch.int16))
+    # the hot-path quantiser writes the same codes in operand form (the
+    # load-time weight expansion applies the same map), and the same scales
+    # as scale-operand rows
+    c2, sk8, la2 = ops.svdq_w4a4_quant_mma(x.cuda(), L["smooth"].cuda(), _quant_gpu_down_t(L))
+    want_k8 = ops.svdq_w4a4_scale_k8(ascale)
+    assert torch.equal(c2, ops.expand_w4a4_weight(codes))
+    assert torch.equal(sk8.view(torch.int16), want_k8.view(torch.int16))
+    assert torch.all(sk8[:, :, 1:] == 0)
+    assert torch.equal(sk8[:, :, 0].t().contiguous().view(torch.int16),
+                       ascale.view(torch.int16))
     assert torch.equal(la2, la)
 
 
@@ -67,9 +73,8 @@ def test_int4_activation_without_smoothing(cuda_ready):
 @pytest.mark.parametrize("m,k,n", [(128, 128, 128), (200, 384, 256), (256, 3072, 384)])
 def test_int4_group_partials_bit_exact(cuda_ready, m, k, n):
     x, L = _layer_case(m, k, n, 0, seed=m + n)
-    p, codes, ascale, _ = _quant_gpu(x, L)
-    a_q8, _ = ops.svdq_w4a4_to_operand(codes, ascale)
-    got = ops.svdq_w4a4_group_partials(a_q8, p["w_q8"])
+    _, codes, _, _ = _quant_gpu(x, L)
+    got = ops.svdq_w4a4_group_partials(codes, ops.expand_w4a4_weight(L["w_packed"].cuda()))
     want = O.int4_group_partials(codes.cpu(), L["w_packed"])
     assert torch.equal(got.cpu(), want)
     assert native.device_error() == 0
@@ -93,6 +98,22 @@ def test_int4_linear_matches_oracle(cuda_ready, m, k, n, rank, lora, gelu):
     assert O.rel_l2(y, want["y"]) <= REL_TOL
     assert O.max_abs_beyond_bf16(y, want["y64"]) <= ABS_TOL
     assert native.device_error() == 0
+
+
+@pytest.mark.parametrize("m,k,n,rank", [(300, 1024, 256, 32), (128, 512, 128, 0)])
+def test_packed_activation_gemm_matches_operand_form(cuda_ready, m, k, n, rank):
+    """gwb_svdq_w4a4_gemm_packed (packed codes unpacked in shared memory)
+    gives the same output as the operand-form GEMM."""
+    x, L = _layer_case(m, k, n, rank, seed=17 * m)
+    p, codes, ascale, la = _quant_gpu(x, L)
+    sk8 = ops.svdq_w4a4_scale_k8(ascale)
+    w_q8 = ops.expand_w4a4_weight(L["w_packed"].cuda())
+    bias = L["bias"].cuda()
+    a = ops.svdq_w4a4_gemm_packed(codes, sk8, w_q8, p["w_scale_k8"], la if rank else None,
+                                  p["proj_up_pad"], bias, False)
+    b = ops.svdq_w4a4_gemm(ops.expand_w4a4_weight(codes), sk8, w_q8, p["w_scale_k8"],
+                           la if rank else None, p["proj_up_pad"], bias, False)
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
 
 
 @pytest.mark.parametrize("m,k", [(1, 128), (77, 3072), (256, 12288)])

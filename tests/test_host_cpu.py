@@ -53,7 +53,7 @@ def test_entry_points_reject_bad_shapes_before_touching_memory():
                                   None, None) == 1
     assert lib.gwb_svdq_w4a4_quant(None, None, None, 4, 128, 24, None, None, None, None) == 1
     assert lib.gwb_svdq_w4a4_quant_mma(None, None, None, 4, 100, 0, None, None, None, None) == 1
-    assert lib.gwb_svdq_w4a4_to_operand(None, None, 4, 100, None, None, None) == 1
+    assert lib.gwb_svdq_w4a4_scale_k8(None, 4, 100, None, None) == 1
     assert lib.gwb_w8a8_linear(None, None, None, None, 4, 128, 100, 0, None, None, None, None) == 1
     # M == 0 is a no-op success
     assert lib.gwb_svdq_w4a4_linear(*([None] * 7), 0, 128, 128, 0, 0, *([None] * 5)) == 0
@@ -73,13 +73,13 @@ def test_prepare_repacks_layouts():
     ws = torch.rand(256, 4).to(torch.float16)
     down = torch.randn(256, 20).to(torch.bfloat16)
     up = torch.randn(128, 20).to(torch.bfloat16)
-    p = ops.prepare_w4a4_weights(None, ws, down, up)
-    assert p["w_q8"] is None and p["w_scale_k8"] is None
+    p = ops.prepare_w4a4_weights(ws, down, up)
+    assert p["w_scale_k8"] is None      # CPU tensors: the scale rows are built on the GPU
     assert p["proj_down_t"].shape == (32, 256) and torch.all(p["proj_down_t"][20:] == 0)
     assert torch.equal(p["proj_down_t"][:20], down.t())
     assert p["proj_up_pad"].shape == (128, 32) and torch.all(p["proj_up_pad"][:, 20:] == 0)
     with pytest.raises(ops.SvdqB200Error):
-        ops.prepare_w4a4_weights(None, ws, torch.zeros(256, 80), torch.zeros(128, 80))
+        ops.prepare_w4a4_weights(ws, torch.zeros(256, 80), torch.zeros(128, 80))
 
 
 def test_module_surface_and_swap():

@@ -35,9 +35,10 @@ def test_noalloc_linear_matches_allocating_entry_point(cuda_ready, m, k, n, rank
     stream = torch.cuda.current_stream().cuda_stream
     x0 = O.synth_activation(m, k, seed=41)
     L = O.synth_svdq_layer(k, n, rank, seed=42, x_calib=x0)
-    p = ops.prepare_w4a4_weights(L["w_packed"].to(dev), L["w_scale"].to(dev),
+    p = ops.prepare_w4a4_weights(L["w_scale"].to(dev),
                                  None if rank == 0 else L["proj_down"].to(dev),
-                                 None if rank == 0 else L["proj_up"].to(dev))
+                                 None if rank == 0 else L["proj_up"].to(dev),
+                                 weight=L["w_packed"].to(dev))
     rp = 0 if rank == 0 else int(p["proj_down_t"].shape[0])
     w = p["w_q8"]
     smooth = L["smooth"].to(dev)
@@ -68,7 +69,7 @@ def test_noalloc_linear_matches_allocating_entry_point(cuda_ready, m, k, n, rank
 
 def test_noalloc_rejects_requests_beyond_its_capacity(cuda_ready):
     lib = native.require()
-    # 20000 x 3072 needs 20000*(3072+768+64) bytes > 32 MiB -> GWB_E_CAPACITY (8),
+    # 20000 x 3072 needs 20000*(1536+768+64) bytes > 32 MiB -> GWB_E_CAPACITY (8),
     # refused before any pointer is touched
     rc = lib.gwb_svdq_w4a4_linear_noalloc(None, None, None, None, None, None, None,
                                           20000, 3072, 3072, 32, 0, None, None)
