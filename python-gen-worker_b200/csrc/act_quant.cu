@@ -15,18 +15,33 @@
 
 namespace gwb {
 
-constexpr int kActRows = 16;    // rows per CTA (one m16 MMA tile)
-constexpr int kActWarps = 8;    // warps per CTA, splitting K round-robin
+// warps per CTA (splitting K round-robin in 64-wide chunks); with 128
+// registers per thread two CTAs share an SM
+template <int MT> __host__ __device__ constexpr int act_warps() { return 8; }
 
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-// sign-magnitude nibble of clamp(rint(v/s), -7, 7): bit 3 = sign, bits 0-2 = |q|
-__device__ __forceinline__ uint32_t q4(float v, float s) {
-  float q = rintf(__fdiv_rn(v, s));
-  q = fminf(fmaxf(q, -7.0f), 7.0f);
-  const int qi = static_cast<int>(q);
-  return qi < 0 ? (8u | static_cast<uint32_t>(-qi)) : static_cast<uint32_t>(qi);
+// a / b given rb = RN(1/b), correctly rounded whenever the quotient is a
+// normal number (Markstein's theorem: with q0 = RN(a * rb) and the exact
+// remainder r = a - b * q0 from an FMA, RN(q0 + r * rb) = RN(a / b)).
+// A quotient below 2^-126 cannot change any code or scale produced here:
+// group scales are at least 2^-24, so such values quantise to 0 and cannot
+// be a group's amax unless every value of the group is below 2^-126, in
+// which case the scale clamps to 2^-24 whatever their exact values.
+__device__ __forceinline__ float div_rn(float a, float b, float rb) {
+  const float q = a * rb;
+  const float r = fmaf(-q, b, a);
+  return fmaf(r, rb, q);
+}
+
+// sign-magnitude nibble of clamp(rint(v/s), -7, 7): bit 3 = sign, bits 0-2 = |q|.
+// |q| <= 7.5 here, so min(|q|, 7) + 2^23 rounds half-to-even to the integer
+// magnitude in the low mantissa bits (rint(|q|) = |rint(q)|).
+__device__ __forceinline__ uint32_t q4(float v, float s, float rs) {
+  const float q = div_rn(v, s, rs);
+  const uint32_t mag = __float_as_uint(fminf(fabsf(q), 7.0f) + 8388608.0f) & 7u;
+  return mag | ((q < 0.0f && mag != 0u) ? 8u : 0u);
 }
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
@@ -39,17 +54,18 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
 }
 
 // Quantise 16 consecutive raw elements (8 bf16x2 words) of one row-group
-// segment. The 4 lanes of a quad hold the 64 elements of one group.
-__device__ __forceinline__ void quant_seg16(const uint32_t (&xw)[8], const uint32_t (&sw)[8],
-                                            bool has_smooth, uint32_t& lo, uint32_t& hi,
-                                            __half& scale_out) {
+// segment: smoothing divide rounded to bf16, then the group's INT4 codes.
+// The 4 lanes of a quad hold the 64 elements of one group.
+__device__ __forceinline__ void quant_seg16(const uint32_t (&xw)[8], const float (&sm)[16],
+                                            const float (&rsm)[16], bool has_smooth,
+                                            uint32_t& lo, uint32_t& hi, __half& scale_out) {
   float v[16];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     float a = bf_lo(xw[j]), b = bf_hi(xw[j]);
     if (has_smooth) {
-      a = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(a, bf_lo(sw[j]))));
-      b = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(b, bf_hi(sw[j]))));
+      a = __bfloat162float(__float2bfloat16_rn(div_rn(a, sm[2 * j], rsm[2 * j])));
+      b = __bfloat162float(__float2bfloat16_rn(div_rn(b, sm[2 * j + 1], rsm[2 * j + 1])));
     }
     v[2 * j] = a;
     v[2 * j + 1] = b;
@@ -61,143 +77,237 @@ __device__ __forceinline__ void quant_seg16(const uint32_t (&xw)[8], const uint3
   amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
   float s32 = __fdiv_rn(amax, 7.0f);
   s32 = fminf(fmaxf(s32, 5.9604644775390625e-08f), 65504.0f);
-  __half sh = __float2half_rn(s32);
-  float s = __half2float(sh);
+  const __half sh = __float2half_rn(s32);
+  const float s = __half2float(sh);
+  const float rs = __frcp_rn(s);
   lo = 0;
   hi = 0;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) lo |= q4(v[j], s) << (4 * j);
+  for (int j = 0; j < 8; ++j) lo |= q4(v[j], s, rs) << (4 * j);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) hi |= q4(v[8 + j], s) << (4 * j);
+  for (int j = 0; j < 8; ++j) hi |= q4(v[8 + j], s, rs) << (4 * j);
   scale_out = sh;
 }
 
-// NB = padded rank / 8 (0 = no low-rank branch). MMA_FORM = false writes the
-// interchange form: packed codes u8 [M, K/2] and ascale f16 [M, K/64].
-// MMA_FORM = true writes the GEMM operand form: codes u8 [M, K] as e4m3
-// bytes of q * 2^-9 in the within-8 operand order (unpack8_e4m3), and the
-// scales as scale-operand rows f16 [K/64, M, 8] (scale at k = 0, zeros at
-// k = 1..7: one 16-byte TMA row per matrix row).
-template <int NB, bool MMA_FORM>
-__global__ void __launch_bounds__(kActWarps * 32)
+// NB = padded rank / 8 (0 = no low-rank branch); MT = m16 row tiles per CTA
+// (16 * MT rows); act_warps<MT>() warps split K round-robin in 64-wide chunks.
+// MMA_FORM = false writes the interchange form: packed codes u8 [M, K/2] and
+// ascale f16 [M, K/64]. MMA_FORM = true writes the GEMM operand form: codes
+// u8 [M, K] as e4m3 bytes of q * 2^-9 in the within-8 operand order
+// (unpack8_e4m3), and the scales as scale-operand rows f16 [K/64, M, 8]
+// (scale at k = 0, zeros at k = 1..7: one 16-byte TMA row per matrix row).
+// la = bf16(x · L1) on raw x: each warp accumulates its K chunks with
+// mma.sync; the per-warp partials are summed in a fixed order through
+// shared memory, so la is deterministic.
+template <int NB, bool MMA_FORM, int MT>
+__global__ void __launch_bounds__(act_warps<MT>() * 32, 2)
 act_int4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ smooth,
                 const __nv_bfloat16* __restrict__ down_t, uint8_t* __restrict__ codes,
                 __half* __restrict__ ascale, __nv_bfloat16* __restrict__ la, int M, int K) {
   constexpr int RP = NB * 8;
-  __shared__ float red[NB > 0 ? kActWarps : 1][kActRows][RP > 0 ? RP : 1];
+  constexpr int ROWS = 16 * MT;
+  constexpr int kActWarps = act_warps<MT>();
+  extern __shared__ float red[];   // [kActWarps][ROWS][RP]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int row0 = blockIdx.x * kActRows + g, row1 = row0 + 8;
-  const bool v0 = row0 < M, v1 = row1 < M;
   const int nchunks = K / 64;
   const int G = K / 64;
+  const bool has_smooth = smooth != nullptr;
 
-  float acc[NB > 0 ? NB : 1][4];
+  int rows[MT][2];
+  bool valid[MT][2];
+  const uint4* xr[MT][2];
 #pragma unroll
-  for (int j = 0; j < (NB > 0 ? NB : 1); ++j)
+  for (int t = 0; t < MT; ++t)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
+    for (int h = 0; h < 2; ++h) {
+      rows[t][h] = blockIdx.x * ROWS + 16 * t + 8 * h + g;
+      valid[t][h] = rows[t][h] < M;
+      xr[t][h] = reinterpret_cast<const uint4*>(x + (size_t)(valid[t][h] ? rows[t][h] : 0) * K);
+    }
 
-  const uint4* xr0 = reinterpret_cast<const uint4*>(x + (size_t)(v0 ? row0 : 0) * K);
-  const uint4* xr1 = reinterpret_cast<const uint4*>(x + (size_t)(v1 ? row1 : 0) * K);
+  float acc[MT][NB > 0 ? NB : 1][4];
+#pragma unroll
+  for (int t = 0; t < MT; ++t)
+#pragma unroll
+    for (int j = 0; j < (NB > 0 ? NB : 1); ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[t][j][e] = 0.f;
 
+  // x words of the current chunk; the next chunk's are loaded at the top of
+  // each iteration so their latency overlaps this chunk's work
+  uint4 nx[MT][2][2];
+  auto load_x = [&](int kc_) {
+    const int kk = kc_ * 64 + 16 * c;
+#pragma unroll
+    for (int t = 0; t < MT; ++t)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const bool ok = valid[t][h] && kc_ < nchunks;
+        nx[t][h][0] = ok ? __ldg(xr[t][h] + kk / 8) : make_uint4(0, 0, 0, 0);
+        nx[t][h][1] = ok ? __ldg(xr[t][h] + kk / 8 + 1) : make_uint4(0, 0, 0, 0);
+      }
+  };
+  load_x(warp);
   for (int kc = warp; kc < nchunks; kc += kActWarps) {
     const int k0 = kc * 64 + 16 * c;  // this lane's 16-element segment
-    uint32_t w0[8], w1[8];
-    {
-      uint4 p0 = v0 ? __ldg(xr0 + k0 / 8) : make_uint4(0, 0, 0, 0);
-      uint4 p1 = v0 ? __ldg(xr0 + k0 / 8 + 1) : make_uint4(0, 0, 0, 0);
-      uint4 q0 = v1 ? __ldg(xr1 + k0 / 8) : make_uint4(0, 0, 0, 0);
-      uint4 q1 = v1 ? __ldg(xr1 + k0 / 8 + 1) : make_uint4(0, 0, 0, 0);
-      w0[0] = p0.x; w0[1] = p0.y; w0[2] = p0.z; w0[3] = p0.w;
-      w0[4] = p1.x; w0[5] = p1.y; w0[6] = p1.z; w0[7] = p1.w;
-      w1[0] = q0.x; w1[1] = q0.y; w1[2] = q0.z; w1[3] = q0.w;
-      w1[4] = q1.x; w1[5] = q1.y; w1[6] = q1.z; w1[7] = q1.w;
-    }
-    uint32_t sw[8];
-    const bool has_smooth = smooth != nullptr;
+    uint32_t w[MT][2][8];
+#pragma unroll
+    for (int t = 0; t < MT; ++t)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint4 p0 = nx[t][h][0], p1 = nx[t][h][1];
+        w[t][h][0] = p0.x; w[t][h][1] = p0.y; w[t][h][2] = p0.z; w[t][h][3] = p0.w;
+        w[t][h][4] = p1.x; w[t][h][5] = p1.y; w[t][h][6] = p1.z; w[t][h][7] = p1.w;
+      }
+    load_x(kc + kActWarps);
+    float sm[16], rsm[16];
     if (has_smooth) {
       const uint4* sp = reinterpret_cast<const uint4*>(smooth + k0);
-      uint4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
-      sw[0] = s0.x; sw[1] = s0.y; sw[2] = s0.z; sw[3] = s0.w;
-      sw[4] = s1.x; sw[5] = s1.y; sw[6] = s1.z; sw[7] = s1.w;
+      const uint4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
+      const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sm[2 * j] = bf_lo(sw[j]);
+        sm[2 * j + 1] = bf_hi(sw[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) rsm[j] = __frcp_rn(sm[j]);
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) sw[j] = 0;
+      for (int j = 0; j < 16; ++j) { sm[j] = 1.f; rsm[j] = 1.f; }
     }
-    uint32_t lo0, hi0, lo1, hi1;
-    __half s0, s1;
-    quant_seg16(w0, sw, has_smooth, lo0, hi0, s0);
-    quant_seg16(w1, sw, has_smooth, lo1, hi1, s1);
-    if (v0) {
-      if constexpr (MMA_FORM) {
-        uint4 o;
-        unpack8_e4m3(lo0, o.x, o.y);
-        unpack8_e4m3(hi0, o.z, o.w);
-        *reinterpret_cast<uint4*>(codes + (size_t)row0 * K + k0) = o;
-      } else {
-        *reinterpret_cast<uint2*>(codes + (size_t)row0 * (K / 2) + k0 / 2) = make_uint2(lo0, hi0);
+#pragma unroll
+    for (int t = 0; t < MT; ++t)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t lo, hi;
+        __half sc;
+        quant_seg16(w[t][h], sm, rsm, has_smooth, lo, hi, sc);
+        if (valid[t][h]) {
+          const int row = rows[t][h];
+          if constexpr (MMA_FORM) {
+            uint4 o;
+            unpack8_e4m3(lo, o.x, o.y);
+            unpack8_e4m3(hi, o.z, o.w);
+            *reinterpret_cast<uint4*>(codes + (size_t)row * K + k0) = o;
+            if (c == 0)
+              *reinterpret_cast<uint4*>(ascale + ((size_t)kc * M + row) * 8) =
+                  make_uint4(__half_as_ushort(sc), 0u, 0u, 0u);
+          } else {
+            *reinterpret_cast<uint2*>(codes + (size_t)row * (K / 2) + k0 / 2) = make_uint2(lo, hi);
+            if (c == 0) ascale[(size_t)row * G + kc] = sc;
+          }
+        }
       }
-      if (c == 0) {
-        if constexpr (MMA_FORM)
-          *reinterpret_cast<uint4*>(ascale + ((size_t)kc * M + row0) * 8) =
-              make_uint4(__half_as_ushort(s0), 0u, 0u, 0u);
-        else
-          ascale[(size_t)row0 * G + kc] = s0;
-      }
-    }
-    if (v1) {
-      if constexpr (MMA_FORM) {
-        uint4 o;
-        unpack8_e4m3(lo1, o.x, o.y);
-        unpack8_e4m3(hi1, o.z, o.w);
-        *reinterpret_cast<uint4*>(codes + (size_t)row1 * K + k0) = o;
-      } else {
-        *reinterpret_cast<uint2*>(codes + (size_t)row1 * (K / 2) + k0 / 2) = make_uint2(lo1, hi1);
-      }
-      if (c == 0) {
-        if constexpr (MMA_FORM)
-          *reinterpret_cast<uint4*>(ascale + ((size_t)kc * M + row1) * 8) =
-              make_uint4(__half_as_ushort(s1), 0u, 0u, 0u);
-        else
-          ascale[(size_t)row1 * G + kc] = s1;
-      }
-    }
     if constexpr (NB > 0) {
       // k is permuted consistently in A and B: logical fragment positions
       // (2c,2c+1 | 2c+8,2c+9) of k16-step s map to physical 16c+4s+(0,1 | 2,3).
 #pragma unroll
       for (int j = 0; j < NB; ++j) {
         const uint4* dp = reinterpret_cast<const uint4*>(down_t + (size_t)(8 * j + g) * K + k0);
-        uint4 d0 = __ldg(dp), d1 = __ldg(dp + 1);
-        uint32_t dw[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+        const uint4 d0 = __ldg(dp), d1 = __ldg(dp + 1);
+        const uint32_t dw[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          uint32_t a[4] = {w0[2 * s], w1[2 * s], w0[2 * s + 1], w1[2 * s + 1]};
-          mma_bf16_16816(acc[j], a, dw[2 * s], dw[2 * s + 1]);
-        }
+        for (int t = 0; t < MT; ++t)
+#pragma unroll
+          for (int s = 0; s < 4; ++s) {
+            const uint32_t a[4] = {w[t][0][2 * s], w[t][1][2 * s], w[t][0][2 * s + 1],
+                                   w[t][1][2 * s + 1]};
+            mma_bf16_16816(acc[t][j], a, dw[2 * s], dw[2 * s + 1]);
+          }
       }
     }
   }
 
   if constexpr (NB > 0) {
 #pragma unroll
-    for (int j = 0; j < NB; ++j) {
-      red[warp][g][8 * j + 2 * c] = acc[j][0];
-      red[warp][g][8 * j + 2 * c + 1] = acc[j][1];
-      red[warp][g + 8][8 * j + 2 * c] = acc[j][2];
-      red[warp][g + 8][8 * j + 2 * c + 1] = acc[j][3];
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < kActRows * RP; i += blockDim.x) {
-      const int r = i / RP, col = i % RP;
-      float s = 0.f;
+    for (int t = 0; t < MT; ++t)
 #pragma unroll
-      for (int w = 0; w < kActWarps; ++w) s += red[w][r][col];
-      const int row = blockIdx.x * kActRows + r;
-      if (row < M) la[(size_t)row * RP + col] = __float2bfloat16_rn(s);
+      for (int j = 0; j < NB; ++j) {
+        float* r0 = red + ((size_t)warp * ROWS + 16 * t + g) * RP + 8 * j + 2 * c;
+        float* r1 = r0 + 8 * RP;
+        r0[0] = acc[t][j][0];
+        r0[1] = acc[t][j][1];
+        r1[0] = acc[t][j][2];
+        r1[1] = acc[t][j][3];
+      }
+    __syncthreads();
+    for (int i = threadIdx.x; i < ROWS * RP; i += blockDim.x) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w2 = 0; w2 < kActWarps; ++w2) sum += red[(size_t)w2 * ROWS * RP + i];
+      const int row = blockIdx.x * ROWS + i / RP;
+      if (row < M) la[(size_t)row * RP + i % RP] = __float2bfloat16_rn(sum);
     }
   }
+}
+
+template <bool MMA_FORM, int MT>
+static int launch_act_int4_mt(const void* x, const void* smooth, const void* down_t, void* codes,
+                              void* ascale, void* la, int M, int K, int rank_pad,
+                              cudaStream_t st) {
+  constexpr int kActWarps = act_warps<MT>();
+  dim3 grid((M + 16 * MT - 1) / (16 * MT)), block(kActWarps * 32);
+  auto X = static_cast<const __nv_bfloat16*>(x);
+  auto S = static_cast<const __nv_bfloat16*>(smooth);
+  auto D = static_cast<const __nv_bfloat16*>(down_t);
+  auto C = static_cast<uint8_t*>(codes);
+  auto A = static_cast<__half*>(ascale);
+  auto L = static_cast<__nv_bfloat16*>(la);
+  const size_t smem = (size_t)kActWarps * 16 * MT * rank_pad * sizeof(float);
+#define GWB_ACT_CASE(RPAD, NBV)                                                              \
+  case RPAD: {                                                                               \
+    auto k = act_int4_kernel<NBV, MMA_FORM, MT>;                                             \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                               (int)smem);                                   \
+    k<<<grid, block, smem, st>>>(X, S, D, C, A, L, M, K);                                    \
+    break;                                                                                   \
+  }
+  switch (rank_pad) {
+    GWB_ACT_CASE(0, 0)
+    GWB_ACT_CASE(16, 2)
+    GWB_ACT_CASE(32, 4)
+    GWB_ACT_CASE(48, 6)
+    GWB_ACT_CASE(64, 8)
+    default: return GWB_E_SHAPE;
+  }
+#undef GWB_ACT_CASE
+  return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
+}
+
+int launch_act_int4(const void* x, const void* smooth, const void* down_t, void* codes,
+                    void* ascale, void* la, int M, int K, int rank_pad, bool mma_form,
+                    cudaStream_t st) {
+  // two row tiles per CTA when that still gives every SM a CTA
+  const bool two = false;   // one m16 row tile per CTA measured fastest
+  if (mma_form)
+    return two ? launch_act_int4_mt<true, 2>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st)
+               : launch_act_int4_mt<true, 1>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st);
+  return two ? launch_act_int4_mt<false, 2>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st)
+             : launch_act_int4_mt<false, 1>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st);
+}
+
+// Scale interchange form f16 [R, K/64] -> GEMM scale-operand rows
+// f16 [K/64, R, 8] (scale at k = 0, zeros at k = 1..7).
+__global__ void scale_k8_kernel(const __half* __restrict__ scale, uint4* __restrict__ scale_k8,
+                                int R, int G) {
+  const int64_t n = (int64_t)R * G;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / G, g = i % G;
+    scale_k8[(size_t)g * R + r] = make_uint4(__half_as_ushort(scale[i]), 0u, 0u, 0u);
+  }
+}
+
+int launch_scale_k8(const void* scale, void* scale_k8, int R, int K, cudaStream_t st) {
+  if (R <= 0 || K <= 0 || K % 64) return GWB_E_SHAPE;
+  const int64_t work = (int64_t)R * (K / 64);
+  int64_t blocks = (work + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  scale_k8_kernel<<<(int)blocks, 256, 0, st>>>(static_cast<const __half*>(scale),
+                                               static_cast<uint4*>(scale_k8), R, K / 64);
+  return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }
 
 // One warp per row: pass 1 amax, pass 2 (L1/L2-resident re-read) quantise.
@@ -235,57 +345,6 @@ act_int8_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restrict__ q,
     }
     qr[i] = make_uint2(packed[0], packed[1]);
   }
-}
-
-template <bool MMA_FORM>
-static int launch_act_int4_t(const void* x, const void* smooth, const void* down_t, void* codes,
-                             void* ascale, void* la, int M, int K, int rank_pad, cudaStream_t st) {
-  dim3 grid((M + kActRows - 1) / kActRows), block(kActWarps * 32);
-  auto X = static_cast<const __nv_bfloat16*>(x);
-  auto S = static_cast<const __nv_bfloat16*>(smooth);
-  auto D = static_cast<const __nv_bfloat16*>(down_t);
-  auto C = static_cast<uint8_t*>(codes);
-  auto A = static_cast<__half*>(ascale);
-  auto L = static_cast<__nv_bfloat16*>(la);
-  switch (rank_pad) {
-    case 0: act_int4_kernel<0, MMA_FORM><<<grid, block, 0, st>>>(X, S, D, C, A, L, M, K); break;
-    case 16: act_int4_kernel<2, MMA_FORM><<<grid, block, 0, st>>>(X, S, D, C, A, L, M, K); break;
-    case 32: act_int4_kernel<4, MMA_FORM><<<grid, block, 0, st>>>(X, S, D, C, A, L, M, K); break;
-    case 48: act_int4_kernel<6, MMA_FORM><<<grid, block, 0, st>>>(X, S, D, C, A, L, M, K); break;
-    case 64: act_int4_kernel<8, MMA_FORM><<<grid, block, 0, st>>>(X, S, D, C, A, L, M, K); break;
-    default: return GWB_E_SHAPE;
-  }
-  return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
-}
-
-int launch_act_int4(const void* x, const void* smooth, const void* down_t, void* codes,
-                    void* ascale, void* la, int M, int K, int rank_pad, bool mma_form,
-                    cudaStream_t st) {
-  return mma_form ? launch_act_int4_t<true>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st)
-                  : launch_act_int4_t<false>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad,
-                                             st);
-}
-
-// Scale interchange form f16 [R, K/64] -> GEMM scale operand rows
-// f16 [K/64, R, 8] (scale at k = 0, zeros at k = 1..7).
-__global__ void scale_k8_kernel(const __half* __restrict__ scale, uint4* __restrict__ scale_k8,
-                                int R, int G) {
-  const int64_t n = (int64_t)R * G;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / G, g = i % G;
-    scale_k8[(size_t)g * R + r] = make_uint4(__half_as_ushort(scale[i]), 0u, 0u, 0u);
-  }
-}
-
-int launch_scale_k8(const void* scale, void* scale_k8, int R, int K, cudaStream_t st) {
-  if (R <= 0 || K <= 0 || K % 64) return GWB_E_SHAPE;
-  const int64_t work = (int64_t)R * (K / 64);
-  int64_t blocks = (work + 255) / 256;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  scale_k8_kernel<<<(int)blocks, 256, 0, st>>>(static_cast<const __half*>(scale),
-                                               static_cast<uint4*>(scale_k8), R, K / 64);
-  return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }
 
 int launch_act_int8(const void* x, void* q, void* scale, int M, int K, cudaStream_t st) {

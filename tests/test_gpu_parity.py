@@ -40,7 +40,8 @@ def _quant_gpu(x, L):
     return p, codes, ascale, la
 
 
-@pytest.mark.parametrize("m,k", [(1, 128), (16, 256), (77, 3072), (333, 3072), (128, 12288)])
+@pytest.mark.parametrize("m,k", [(1, 128), (16, 256), (77, 3072), (333, 3072), (128, 12288),
+                                 (4736, 1024)])
 def test_int4_activation_codes_and_scales_bit_exact(cuda_ready, m, k):
     x, L = _layer_case(m, k, 128, 32, seed=m + k)
     _, codes, ascale, la = _quant_gpu(x, L)
@@ -60,6 +61,23 @@ def test_int4_activation_codes_and_scales_bit_exact(cuda_ready, m, k):
     assert torch.equal(sk8[:, :, 0].t().contiguous().view(torch.int16),
                        ascale.view(torch.int16))
     assert torch.equal(la2, la)
+
+
+def test_int4_activation_bit_exact_over_wide_value_ranges(cuda_ready):
+    """25M elements spanning many binades and smoothing factors in [1e-3, 1e3]:
+    the kernel's divides (reciprocal + remainder correction) must round
+    exactly like the oracle's IEEE divides, codes and scales bit for bit."""
+    gen = torch.Generator().manual_seed(7)
+    m, k = 2048, 12288
+    mant = torch.rand(m, k, generator=gen) + 0.5
+    expo = torch.randint(-20, 12, (m, k), generator=gen).float()
+    sign = torch.where(torch.rand(m, k, generator=gen) < 0.5, -1.0, 1.0)
+    x = (sign * mant * torch.pow(2.0, expo)).to(torch.bfloat16)
+    smooth = torch.pow(10.0, torch.rand(k, generator=gen) * 6 - 3).to(torch.bfloat16)
+    codes, ascale, _ = ops.svdq_w4a4_quant(x.cuda(), smooth.cuda(), None)
+    want_codes, want_scale = O.quant_int4(O.smooth_bf16(x, smooth))
+    assert torch.equal(codes.cpu(), want_codes)
+    assert torch.equal(ascale.cpu().view(torch.int16), want_scale.view(torch.int16))
 
 
 def test_int4_activation_without_smoothing(cuda_ready):
