@@ -42,7 +42,23 @@ DUAL = [("qkv", HIDDEN, 9216, False), ("out", HIDDEN, HIDDEN, False),
         ("fc1", HIDDEN, 12288, True), ("fc2", 12288, HIDDEN, False)]
 SINGLE = [("qkv_mlp", HIDDEN, 21504, False), ("out", 15360, HIDDEN, False)]
 N_DUAL, N_SINGLE = 19, 38
-INT8_DENSE_PEAK_TOPS = 4500.0   # B200 datasheet dense INT8 (no measured INT8 peak exists)
+INT8_DENSE_PEAK_TOPS = 4500.0   # B200 datasheet dense INT8 / FP8, for context
+# DRAM bytes (read + write) of one gemm_w4a4_kernel launch on the cfg3 shape
+# (M 4608, K 3072, N 3072) from one ncu capture (profiles/gemm_w4a4_cfg3.md);
+# its algorithmic bytes are 29.5 MB (a_q8 + w_q8 + both scale-operand arrays).
+GEMM_TRAFFIC_CFG3_BYTES = 30.29e6 + 0.42e6
+
+
+def tensor_peak_tops() -> tuple[float, str]:
+    """The e4m3 MMA (tcgen05 kind::f8f6f4) issues at twice the bf16 rate, so
+    the roofline denominator is 2x the measured sustained bf16 cuBLAS figure
+    (the GEMM is timed inside a long step)."""
+    try:
+        mp = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return 2.0 * float(mp["bf16_tflops_sustained"]), \
+            "2 x measured sustained bf16 (MEASURED_PEAKS.json): e4m3 MMA rate"
+    except (OSError, KeyError, ValueError):
+        return 2.0 * 1400.0, "2 x fallback sustained bf16 1.4 PFLOP/s: e4m3 MMA rate"
 METRIC = "W4A4 DiT-stack tokens/s (cfg4 Flux linear stack, 16896 tokens)"
 
 
@@ -459,6 +475,7 @@ def main() -> int:
         tps = TOKENS / (ms_max / 1e3)
         gemm_avg_ops = gemm_ops / max(1, gemm_n)
         achieved = gemm_avg_ops / (gemm_avg_ms / 1e3) / 1e12
+        peak, peak_src = tensor_peak_tops()
         line = {
             "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
@@ -467,13 +484,17 @@ def main() -> int:
             "config": {"workload": "cfg4 Flux DiT W4A4 linear stack, 19 dual + 38 single blocks",
                        "tokens": TOKENS, "tokens_per_rank": m, "hidden": HIDDEN, "rank": RANK,
                        "group": 64, "parallelism": f"token-shard x{world}, weights replicated",
-                       "l2": "per-step working set 3.6 GB of distinct weights (>> 126 MB L2)"},
+                       "l2": "no flush: per-step working set 8.1 GB of distinct weight operands (>> 126 MB L2)"},
             "effective_tops": stack_ops() * TOKENS / (ms_max / 1e3) / 1e12,
             "lowrank_tops_excluded": lowrank_ops() * TOKENS / (ms_max / 1e3) / 1e12,
             "roofline": {"bound": "tensor", "kernel": "gemm_w4a4_kernel",
-                         "achieved": achieved, "peak": INT8_DENSE_PEAK_TOPS, "unit": "TOP/s",
-                         "peak_source": "B200 datasheet dense INT8 (no measured INT8 peak)",
-                         "frac": achieved / INT8_DENSE_PEAK_TOPS, "traffic": None,
+                         "achieved": achieved, "peak": peak, "unit": "TOP/s",
+                         "peak_source": peak_src, "frac": achieved / peak,
+                         "frac_of_datasheet_dense_int8_fp8": achieved / INT8_DENSE_PEAK_TOPS,
+                         "traffic": GEMM_TRAFFIC_CFG3_BYTES,
+                         "traffic_note": "DRAM read+write bytes of one launch, cfg3 shape "
+                                         "(4608x3072x3072), one ncu capture; algorithmic "
+                                         "29.5 MB",
                          "avg_launch_ms": gemm_avg_ms, "launches_timed": gemm_n},
             "e2e": {"value": TOKENS / (e2e_max / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": m * HIDDEN * 2, "d2h_bytes_per_step": m * HIDDEN * 2},

@@ -104,6 +104,7 @@ def test_int4_group_partials_bit_exact(cuda_ready, m, k, n):
     (77, 512, 256, 32, 0, True),
     (300, 1024, 128, 32, 16, False),   # rank 48 (LoRA folded)
     (64, 256, 128, 16, 0, False),
+    (264, 512, 256, 16, 0, False),     # M % 8 == 0 with a partial last row tile
 ])
 def test_int4_linear_matches_oracle(cuda_ready, m, k, n, rank, lora, gelu):
     x, L = _layer_case(m, k, n, rank, seed=3 * m + n, lora=lora)
@@ -132,6 +133,30 @@ def test_packed_activation_gemm_matches_operand_form(cuda_ready, m, k, n, rank):
     b = ops.svdq_w4a4_gemm(ops.expand_w4a4_weight(codes), sk8, w_q8, p["w_scale_k8"],
                            la if rank else None, p["proj_up_pad"], bias, False)
     assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+@pytest.mark.parametrize("m,k,n", [(77, 1024, 256), (1024, 3072, 640)])
+def test_int4_gemm_promotion_matches_exact_sum(cuda_ready, m, k, n):
+    """Without bias and low-rank branch the GEMM returns bf16(sum_g a_scale *
+    w_scale * V_g) with the sum kept in f32: compared with the same sum in
+    float64 from the bit-exact group partials, the error stays within the
+    bf16 output rounding plus a few f32 ulps of the sum of magnitudes."""
+    x, L = _layer_case(m, k, n, 0, seed=11 * m + n)
+    p, codes, ascale, _ = _quant_gpu(x, L)
+    w_q8 = ops.expand_w4a4_weight(L["w_packed"].cuda())
+    part = ops.svdq_w4a4_group_partials(codes, w_q8).double()           # [G, M, N]
+    sa = ascale.double().t()[:, :, None]                                    # [G, M, 1]
+    sw = L["w_scale"].cuda().double().t()[:, None, :]                       # [G, 1, N]
+    terms = part * sa * sw
+    exact = terms.sum(0)
+    mag = terms.abs().sum(0)
+    a_q8, a_sk8, _ = ops.svdq_w4a4_quant_mma(x.cuda(), L["smooth"].cuda(), None)
+    y = ops.svdq_w4a4_gemm(a_q8, a_sk8, w_q8, p["w_scale_k8"], None, None, None, False)
+    err = (y.double() - exact).abs()
+    # bf16 output rounding (2^-9 relative) plus f32 accumulation (G * 2^-24)
+    bound = exact.abs() * 2.0 ** -8 + mag * (k // 64) * 2.0 ** -23 + 1e-30
+    assert bool((err <= bound).all()), float((err / bound).max())
+    assert native.device_error() == 0
 
 
 @pytest.mark.parametrize("m,k", [(1, 128), (77, 3072), (256, 12288)])
