@@ -35,14 +35,19 @@ __device__ long long gwb_trace[8][512];
 
 namespace gwb {
 
-constexpr int kThreads = 256;
 constexpr int kBM = 128;
 constexpr int kBK = 128;  // int8 elements (= bytes) per k-block: one 128B swizzle row
 
+// GELU, tanh form: 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3))). tanh is
+// the hardware approximation (tanh.approx.f32, |error| < 2^-10.9), far below
+// the bf16 rounding of the output.
 __device__ __forceinline__ float gelu_tanh(float v) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
   const float k1 = 0.044715f;
-  return 0.5f * v * (1.0f + tanhf(k0 * (v + k1 * v * v * v)));
+  const float u = k0 * (v + k1 * v * v * v);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * v * (1.0f + t);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
@@ -53,17 +58,28 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 // ======================================================================
 // W8A8
 // ======================================================================
+// Persistent: each CTA walks tiles blockIdx.x, +gridDim.x, ... The two TMEM
+// accumulators (2 x 256 columns) let the MMA run tile i+1's k-loop while the
+// epilogue warps drain tile i, so the epilogue (scales, bias, GELU, store)
+// is hidden behind the tensor core instead of following it.
 namespace w8 {
 constexpr int BN = 256;
 constexpr int STAGES = 4;
 constexpr int A_BYTES = kBM * kBK;        // 16 KB
 constexpr int B_BYTES = BN * kBK;         // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int NACC = 2;                   // TMEM accumulators (tile ping-pong)
+constexpr int TMEM_COLS = NACC * BN;      // 512
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-constexpr int TMEM_COLS = 256;
+// 12 warps: 0 TMA, 1 MMA, 2-3 idle, 4-11 epilogue (lane quarter warp % 4,
+// column half ((warp - 4) / 4) * EC).
+constexpr int THREADS = 384;
+constexpr int EPI0 = 4;
+constexpr int EPI_WARPS = 8;
+constexpr int EC = BN / 2;
 }  // namespace w8
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(w8::THREADS, 1)
 gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const float* __restrict__ a_scale, const float* __restrict__ w_scale,
                  const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out,
@@ -75,16 +91,18 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* acc_full = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* acc_full = empty + STAGES;      // [NACC]
+  uint64_t* acc_empty = acc_full + NACC;    // [NACC]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + NACC);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
   const int nk = K / kBK;
+  const int tiles_n = N / BN;
+  const int ntiles = ((M + kBM - 1) / kBM) * tiles_n;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
-    mbar_init(acc_full, 1);
+    for (int i = 0; i < NACC; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], EPI_WARPS); }
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -95,72 +113,101 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % STAGES;
-      if (!mbar_wait(&empty[s], ((kb / STAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
-      uint8_t* sa = smem + s * STAGE_BYTES;
-      mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-      tma_load_2d(sa, &tmA, &full[s], kb * kBK, m0);
-      tma_load_2d(sa + A_BYTES, &tmB, &full[s], kb * kBK, n0);
-    }
-  } else if (warp == 1 && lane == 0) {
-    constexpr uint32_t idesc = idesc_i8(kBM, BN);
-    bool ok = true;
-    for (int kb = 0; kb < nk && ok; ++kb) {
-      const int s = kb % STAGES;
-      if (!mbar_wait(&full[s], (kb / STAGES) & 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t a_base = smem_u32(smem + s * STAGE_BYTES);
-      const uint32_t b_base = a_base + A_BYTES;
-#pragma unroll
-      for (int k = 0; k < kBK / 32; ++k) {
-        mma_i8(tmem, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k), idesc,
-               (kb > 0 || k > 0) ? 1u : 0u);
-      }
-      mma_commit(&empty[s]);
-    }
-    if (ok) mma_commit(acc_full);
-  } else if (warp >= 4) {
-    const int q = warp - 4;
-    const int row = m0 + 32 * q + lane;
-    if (mbar_wait(acc_full, 0, GWB_ERR_TIMEOUT_EPILOGUE)) {
-      tc_fence_after();
-      const float sa = row < M ? a_scale[row] : 0.f;
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + c, v);
-        tmem_wait_ld();
-        if (row < M) {
-          float f[16];
-#pragma unroll
-          for (int j = 0; j < 16; j += 4) {
-            const float4 ws = *reinterpret_cast<const float4*>(w_scale + n0 + c + j);
-            f[j + 0] = (float)(int)v[j + 0] * sa * ws.x;
-            f[j + 1] = (float)(int)v[j + 1] * sa * ws.y;
-            f[j + 2] = (float)(int)v[j + 2] * sa * ws.z;
-            f[j + 3] = (float)(int)v[j + 3] * sa * ws.w;
+  // register hand-off: 384 x 168 = 64512 at launch; warpgroup 0 drops to 40
+  // (5120), the two epilogue warpgroups rise to 232 (59392)
+  if (warp < EPI0) {
+    regs_dec<40>();
+    if (warp == 0 && lane == 0) {
+      // -------------------------------------------------------------- TMA
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+        const int m0 = (tile / tiles_n) * kBM, n0 = (tile % tiles_n) * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
           }
-          if (bias != nullptr) {
-            const uint4* bp = reinterpret_cast<const uint4*>(bias + n0 + c);
-            uint4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
-            uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              f[2 * j] += __uint_as_float(bw[j] << 16);
-              f[2 * j + 1] += __uint_as_float(bw[j] & 0xFFFF0000u);
-            }
-          }
-          if (gelu) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) f[j] = gelu_tanh(f[j]);
-          }
-          uint4* op = reinterpret_cast<uint4*>(out + (size_t)row * N + n0 + c);
-          op[0] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
-                             pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
-          op[1] = make_uint4(pack_bf16x2(f[8], f[9]), pack_bf16x2(f[10], f[11]),
-                             pack_bf16x2(f[12], f[13]), pack_bf16x2(f[14], f[15]));
+          uint8_t* sa = smem + s * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_2d(sa, &tmA, &full[s], kb * kBK, m0);
+          tma_load_2d(sa + A_BYTES, &tmB, &full[s], kb * kBK, n0);
         }
+      }
+    } else if (warp == 1 && lane == 0) {
+      // -------------------------------------------------------------- MMA
+      constexpr uint32_t idesc = idesc_i8(kBM, BN);
+      int it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++lt) {
+        const int b = lt & 1;
+        if (!mbar_wait(&acc_empty[b], ((lt >> 1) & 1) ^ 1, GWB_ERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + b * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&full[s], (it / STAGES) & 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t b_base = a_base + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < kBK / 32; ++k)
+            mma_i8(d, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k), idesc,
+                   (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit(&empty[s]);
+        }
+        if (ok) mma_commit(&acc_full[b]);
+      }
+    }
+  } else {
+    regs_inc<232>();
+    // ---------------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const int cb = ((warp - EPI0) >> 2) * EC;
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++lt) {
+      const int m0 = (tile / tiles_n) * kBM, n0 = (tile % tiles_n) * BN;
+      const int b = lt & 1;
+      if (!mbar_wait(&acc_full[b], (lt >> 1) & 1, GWB_ERR_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      // the whole 32-row x 128-column slice goes to registers, then the
+      // accumulator is handed back before any arithmetic
+      uint32_t v[EC];
+      const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) + b * BN + cb;
+#pragma unroll
+      for (int c = 0; c < EC; c += 32) tmem_ld32(base + c, v + c);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      const int row = m0 + 32 * q + lane;
+      if (row >= M) continue;
+      const float sa = a_scale[row];
+      uint4* op = reinterpret_cast<uint4*>(out + (size_t)row * N + n0 + cb);
+#pragma unroll
+      for (int c = 0; c < EC; c += 8) {
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(w_scale + n0 + cb + c));
+        const float4 w1 = __ldg(reinterpret_cast<const float4*>(w_scale + n0 + cb + c + 4));
+        const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float f[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = (float)(int)v[c + j] * sa * ws[j];
+        if (bias != nullptr) {
+          const uint4 bw = __ldg(reinterpret_cast<const uint4*>(bias + n0 + cb + c));
+          const uint32_t w[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            f[2 * j] += __uint_as_float(w[j] << 16);
+            f[2 * j + 1] += __uint_as_float(w[j] & 0xFFFF0000u);
+          }
+        }
+        if (gelu) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) f[j] = gelu_tanh(f[j]);
+        }
+        op[c / 8] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                               pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
       }
     }
   }
@@ -601,8 +648,16 @@ int launch_gemm_w8a8(const W8A8Args& a, cudaStream_t st) {
                          w8::SMEM_BYTES);
     attr = true;
   }
-  dim3 grid(a.N / w8::BN, (a.M + kBM - 1) / kBM);
-  gemm_w8a8_kernel<<<grid, kThreads, w8::SMEM_BYTES, st>>>(
+  static int n_sm = 0;
+  if (n_sm == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    if (n_sm <= 0) n_sm = 148;
+  }
+  const int ntiles = ((a.M + kBM - 1) / kBM) * (a.N / w8::BN);
+  const int grid = ntiles < n_sm ? ntiles : n_sm;
+  gemm_w8a8_kernel<<<grid, w8::THREADS, w8::SMEM_BYTES, st>>>(
       tA, tB, a.a_scale, a.w_scale, static_cast<const __nv_bfloat16*>(a.bias),
       static_cast<__nv_bfloat16*>(a.out), a.M, a.N, a.K, a.gelu);
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
