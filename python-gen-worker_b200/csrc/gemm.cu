@@ -339,11 +339,15 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   uint32_t* unpack_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
   const int nk = K / kBK;
   const int G = K / 64;
   const bool dump = partials != nullptr;
   const int has_lr = (!dump && rank_pad > 0) ? 1 : 0;
+  // Persistent: this CTA takes tiles blockIdx.x, +gridDim.x, ... (N-tile
+  // fastest). Ring slots and TMEM group buffers are counted across tiles, so
+  // the next tile's loads and MMAs start while this tile's epilogue finishes.
+  const int tiles_n = N / BN;
+  const int ntiles = ((M + kBM - 1) / kBM) * tiles_n;
 
   for (int i = threadIdx.x; i < SOP_DATA / 16; i += THREADS)
     reinterpret_cast<uint4*>(zero)[i] = make_uint4(0, 0, 0, 0);
@@ -371,30 +375,45 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   // register hand-off. Packed activations: the launch gives 512 x 128 = 65536
   // registers; warpgroups 0-1 (producer, MMA, unpack) drop to 56 (14336) and
   // the two epilogue warpgroups rise to 200 (51200). Operand form: 384 x 168 =
-  // 64512; warpgroup 0 drops to 40 (5120), the epilogue rises to 232 (59392).
+  // 64512; warpgroup 0 drops to 48 (6144), the epilogue rises to 224 (57344).
   if (warp < EPI0) {
     if constexpr (A_PACKED) regs_dec<56>();
-    else regs_dec<40>();
+    else regs_dec<48>();
     if (warp == 0 && lane == 0) {
       // -------------------------------------------------------------- TMA
+      int ui = 0, pk = 0;   // operand-ring and packed-ring slots used so far
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+      const int m0 = (tile / tiles_n) * kBM, n0 = (tile % tiles_n) * BN;
       if (has_lr) {
-        // low-rank operands go straight into operand stage 0 (ring slot 0)
-        mbar_arrive_expect_tx(&u_full[0], kBM * 128 + BN * 128);
-        if (A_PACKED) mbar_arrive(&u_full[0]);
-        tma_load_2d(ustage, &tmLA, &u_full[0], 0, m0);
-        tma_load_2d(ustage + UA_BYTES, &tmUP, &u_full[0], 0, n0);
+        // low-rank operands go straight into an operand ring slot
+        const int u = ui % USTAGES;
+        if (!mbar_wait(&u_empty[u], ((ui / USTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
+        mbar_arrive_expect_tx(&u_full[u], kBM * 128 + BN * 128);
+        if (A_PACKED) mbar_arrive(&u_full[u]);
+        uint8_t* us = ustage + u * USTAGE_BYTES;
+        tma_load_2d(us, &tmLA, &u_full[u], 0, m0);
+        tma_load_2d(us + UA_BYTES, &tmUP, &u_full[u], 0, n0);
+        ++ui;
       }
-      for (int kb = 0; kb < nk; ++kb) {
+      for (int kb = 0; kb < nk; ++kb, ++ui) {
         if (A_PACKED) {
-          const int s = kb % PSTAGES;
-          if (!mbar_wait(&p_empty[s], ((kb / PSTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
+          const int s = pk % PSTAGES;
+          if (!mbar_wait(&p_empty[s], ((pk / PSTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
           uint8_t* ps = pstage + s * PSTAGE_BYTES;
           mbar_arrive_expect_tx(&p_full[s], PSTAGE_BYTES);
           tma_load_2d(ps, &tmA, &p_full[s], kb * (kBK / 2), m0);
+          ++pk;
         }
-        GWB_TRACE_AT(0, kb);
-        const int ui = kb + has_lr, u = ui % USTAGES;
-        if (!mbar_wait(&u_empty[u], ((ui / USTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
+        GWB_TRACE_AT(0, ui);
+        const int u = ui % USTAGES;
+        if (!mbar_wait(&u_empty[u], ((ui / USTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
         uint8_t* us = ustage + u * USTAGE_BYTES;
         const uint32_t a_tx = A_PACKED ? 0u : (uint32_t)UA_BYTES;
         mbar_arrive_expect_tx(&u_full[u], a_tx + (dump ? UB_BYTES : UB_BYTES + 4 * SOP_DATA));
@@ -410,6 +429,7 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           }
         }
       }
+      }
     } else if (warp == 1 && lane == 0) {
       // -------------------------------------------------------------- MMA
       constexpr uint32_t idesc = idesc_fmt0_f32(kBM, BN);      // e4m3 x e4m3 -> f32
@@ -417,30 +437,33 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       constexpr uint32_t idesc_s = idesc_fmt0_f32(kBM, BN);    // f16 x f16 -> f32
       const uint32_t zero_addr = smem_u32(zero);
       bool ok = true;
+      int ui = 0, gi = 0;   // operand-ring slots and group buffers used so far
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
       if (has_lr) {
-        // group slot 0 <- la · proj_upᵀ (f32), into accumulator buffer 0
-        if (!mbar_wait(&u_full[0], 0, GWB_ERR_TIMEOUT_MMA)) ok = false;
-        if (ok && !mbar_wait(&acc_empty[0], 1, GWB_ERR_TIMEOUT_MMA)) ok = false;
-        if (ok) {
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(ustage), b_base = a_base + UA_BYTES;
-          for (int k = 0; k < rank_pad / 16; ++k)
-            mma_f16(tmem, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k), idesc_lr,
-                    k > 0 ? 1u : 0u);
-          mma_commit(&acc_full[0]);
-          mma_commit(&u_empty[0]);
-        }
+        // the tile's first group slot <- la · proj_upᵀ (f32)
+        const int u = ui % USTAGES, b = gi & 1;
+        ok = mbar_wait(&u_full[u], (ui / USTAGES) & 1, GWB_ERR_TIMEOUT_MMA) &&
+             mbar_wait(&acc_empty[b], ((gi >> 1) & 1) ^ 1, GWB_ERR_TIMEOUT_MMA);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(ustage + u * USTAGE_BYTES), b_base = a_base + UA_BYTES;
+        for (int k = 0; k < rank_pad / 16; ++k)
+          mma_f16(tmem + b * BN, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k),
+                  idesc_lr, k > 0 ? 1u : 0u);
+        mma_commit(&acc_full[b]);
+        mma_commit(&u_empty[u]);
+        ++ui;
+        ++gi;
       }
-      for (int kb = 0; kb < nk && ok; ++kb) {
-        const int ui = kb + has_lr, u = ui % USTAGES;
+      for (int kb = 0; kb < nk && ok; ++kb, ++ui) {
+        const int u = ui % USTAGES;
         if (!mbar_wait(&u_full[u], (ui / USTAGES) & 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
-        GWB_TRACE_AT(1, kb);
+        GWB_TRACE_AT(1, ui);
         tc_fence_after();
         const uint32_t a_base = smem_u32(ustage + u * USTAGE_BYTES);
         const uint32_t b_base = a_base + UA_BYTES;
         const uint32_t s_base = b_base + UB_BYTES;
-        for (int gs = 0; gs < 2 && ok; ++gs) {
-          const int gi = kb * 2 + gs + has_lr;
+        for (int gs = 0; gs < 2 && ok; ++gs, ++gi) {
           const int b = gi & 1;
           if (!mbar_wait(&acc_empty[b], ((gi >> 1) & 1) ^ 1, GWB_ERR_TIMEOUT_MMA)) {
             ok = false;
@@ -462,37 +485,43 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
         mma_commit(&u_empty[u]);
       }
+      }
     } else if (A_PACKED && warp >= 2) {
       // -------------------------------------------------------------- unpack
       const int tid = threadIdx.x - 64;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % PSTAGES;
-        const int ui = kb + has_lr, u = ui % USTAGES;
+      int ui = 0, pk = 0;
+      bool live = true;
+      for (int tile = blockIdx.x; live && tile < ntiles; tile += gridDim.x) {
+      ui += has_lr;   // the low-rank slot is filled by the TMA thread alone
+      for (int kb = 0; kb < nk; ++kb, ++ui, ++pk) {
+        const int s = pk % PSTAGES;
+        const int u = ui % USTAGES;
         // one thread waits, the named barrier broadcasts the outcome so all
         // unpack warps always leave the loop together
         if (tid == 0) {
-          bool ok = mbar_wait(&p_full[s], (kb / PSTAGES) & 1, GWB_ERR_TIMEOUT_UNPACK);
+          bool ok = mbar_wait(&p_full[s], (pk / PSTAGES) & 1, GWB_ERR_TIMEOUT_UNPACK);
           ok = ok && mbar_wait(&u_empty[u], ((ui / USTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_UNPACK);
           *unpack_flag = ok ? 1u : 0u;
         }
         asm volatile("bar.sync 1, %0;" ::"n"(UNPACK_THREADS) : "memory");
-        if (*reinterpret_cast<volatile uint32_t*>(unpack_flag) == 0u) break;
-        if (tid == 0) GWB_TRACE_AT(3, kb);
+        if (*reinterpret_cast<volatile uint32_t*>(unpack_flag) == 0u) { live = false; break; }
+        if (tid == 0) GWB_TRACE_AT(3, ui);
         const uint8_t* ps = pstage + s * PSTAGE_BYTES;
         uint8_t* us = ustage + u * USTAGE_BYTES;
         unpack_tile<kBM>(ps, us, tid);
         fence_proxy_async_smem();
         asm volatile("bar.sync 1, %0;" ::"n"(UNPACK_THREADS) : "memory");
         if (tid == 0) {
-          GWB_TRACE_AT(4, kb);
+          GWB_TRACE_AT(4, ui);
           mbar_arrive(&p_empty[s]);
           mbar_arrive(&u_full[u]);
         }
       }
+      }
     }
   } else {
     if constexpr (A_PACKED) regs_inc<200>();
-    else regs_inc<232>();
+    else regs_inc<224>();
     // ---------------------------------------------------------------- epilogue
     // Per group: load the f32 group sum V (= 2^-18 * v, exact) of this warp's
     // 32 rows x EC columns and the scale product S = a_scale * w_scale the
@@ -503,21 +532,24 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     // slice ((warp-EPI0)/4)*EC.
     const int q = warp & 3;
     const int cb = ((warp - EPI0) >> 2) * EC;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+    const int total = G + has_lr;
+    bool ok = true;
+    int gi = 0;   // group buffers consumed so far (counted across tiles)
+    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+    const int m0 = (tile / tiles_n) * kBM, n0 = (tile % tiles_n) * BN;
     const int row = m0 + 32 * q + lane;
     const bool rv = row < M;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
     float2 acc[EC / 2];
 #pragma unroll
     for (int j = 0; j < EC / 2; ++j) acc[j] = make_float2(0.f, 0.f);
-    const int total = G + has_lr;
-    bool ok = true;
-    for (int gi = 0; gi < total; ++gi) {
+    for (int gt = 0; gt < total; ++gt, ++gi) {
       const int b = gi & 1;
       if (!mbar_wait(&acc_full[b], (gi >> 1) & 1, GWB_ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
       if (warp == EPI0 && lane == 0) GWB_TRACE_AT(5, gi);
       tc_fence_after();
       const uint32_t col0 = lane_base + b * BN + cb;
-      const bool lr = has_lr && gi == 0;
+      const bool lr = has_lr && gt == 0;
       uint32_t v[EC], sc[EC];
 #pragma unroll
       for (int c = 0; c < EC; c += 32) tmem_ld32(col0 + c, v + c);
@@ -538,7 +570,7 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                                    __uint_as_float(v[j + 1]) * kRescale);
       } else if (dump) {
         if (rv) {
-          const int g = gi - has_lr;
+          const int g = gt - has_lr;
           uint4* dp = reinterpret_cast<uint4*>(partials + ((size_t)g * M + row) * N + n0 + cb);
 #pragma unroll
           for (int j = 0; j < EC / 4; ++j)
@@ -582,6 +614,7 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
                        pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
       }
+    }
     }
   }
   tc_fence_before();
@@ -628,6 +661,15 @@ static int make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, i
   return r == CUDA_SUCCESS ? GWB_SUCCESS : GWB_E_TMAP;
 }
 
+// Streaming multiprocessors of the current device (persistent grids).
+static int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    n = 148;
+  return n;
+}
+
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int launch_gemm_w8a8(const W8A8Args& a, cudaStream_t st) {
@@ -648,13 +690,7 @@ int launch_gemm_w8a8(const W8A8Args& a, cudaStream_t st) {
                          w8::SMEM_BYTES);
     attr = true;
   }
-  static int n_sm = 0;
-  if (n_sm == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
-    if (n_sm <= 0) n_sm = 148;
-  }
+  const int n_sm = sm_count();
   const int ntiles = ((a.M + kBM - 1) / kBM) * (a.N / w8::BN);
   const int grid = ntiles < n_sm ? ntiles : n_sm;
   gemm_w8a8_kernel<<<grid, w8::THREADS, w8::SMEM_BYTES, st>>>(
@@ -712,7 +748,9 @@ int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, cudaStream_t st) {
                          w4::SMEM_BYTES);
     attr = true;
   }
-  dim3 grid(a.N / w4::BN, (a.M + kBM - 1) / kBM);
+  const int ntiles = ((a.M + kBM - 1) / kBM) * (a.N / w4::BN);
+  const int n_sm = sm_count();
+  const int grid = ntiles < n_sm ? ntiles : n_sm;
   auto kern = a_packed ? gemm_w4a4_kernel<true> : gemm_w4a4_kernel<false>;
   kern<<<grid, a_packed ? w4::threads<true>() : w4::threads<false>(), w4::SMEM_BYTES, st>>>(
       tA, tB, tAS, tBS, tLA, tUP, static_cast<const __nv_bfloat16*>(a.bias),
