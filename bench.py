@@ -268,6 +268,8 @@ CASES = {
     # name: list of (kind, M, K, N, rank, gelu)
     "cfg0": [("w4a4", 256, 3072, 3072, 32, False)],
     "cfg1": [("w8a8", 4096, 3072, 12288, 0, True)],
+    # cfg1 shape in the reference's own W8A8 number format (FP8 e4m3 rowwise)
+    "cfg1fp8": [("fp8", 4096, 3072, 12288, 0, True)],
     "cfg2": [("w4a4", 4608, 3072, 9216, 32, False), ("w4a4", 4608, 3072, 3072, 32, False),
              ("w4a4", 4608, 3072, 12288, 32, True), ("w4a4", 4608, 12288, 3072, 32, False)],
     "cfg3": [("w4a4", 4608, 3072, 3072, 48, False)],
@@ -278,7 +280,8 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
     """Time one BASELINE config's linears (quantiser + GEMM, the module's two
     launches) with CUDA events on the current stream; inputs are resident in
     HBM and a 256 MB buffer is overwritten between iterations to flush L2."""
-    from gen_worker_b200.modules import (build_svdq_int4_linear, build_w8a8_int8_linear,
+    from gen_worker_b200.modules import (build_fp8_rowwise_linear, build_svdq_int4_linear,
+                                         build_w8a8_int8_linear, quantize_fp8_rows,
                                          quantize_int4_rows, quantize_int8_rows)
     from gen_worker_b200 import ops
     dev = torch.device("cuda", 0)
@@ -299,6 +302,10 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
                  "proj_down": (torch.randn(k, r, generator=g, device=dev) * 0.02).to(torch.bfloat16),
                  "proj_up": (torch.randn(n, r, generator=g, device=dev) * 0.02).to(torch.bfloat16),
                  "bias": b}, gelu=gelu, device=dev)
+        elif kind == "fp8":
+            q, s_ = quantize_fp8_rows(w)
+            mod = build_fp8_rowwise_linear({"weight": q, "weight_scale": s_, "bias": b},
+                                           gelu=gelu, device=dev)
         else:
             q, s_ = quantize_int8_rows(w)
             mod = build_w8a8_int8_linear({"weight": q, "weight_scale": s_, "bias": b},
@@ -316,6 +323,11 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
                 e[1].record()
                 ops.svdq_w4a4_gemm(c, a, p["w_q8"], p["w_scale_k8"], la, p["proj_up_pad"],
                                    mod.bias.detach(), gelu)
+            elif kind == "fp8":
+                q, s_ = ops.fp8_quant(xb)
+                e[1].record()
+                ops.fp8_gemm(q, s_, mod.weight, mod.weight_scale.reshape(-1),
+                             mod.bias.detach(), gelu)
             else:
                 q, s_ = ops.w8a8_quant(xb)
                 e[1].record()

@@ -146,6 +146,27 @@ int gwb_w8a8_linear(const void* x, const void* w_q, const float* w_scale, const 
                     int64_t M, int64_t N, int64_t K, int gelu, void* q, void* scale,
                     void* out, void* stream);
 
+/* The reference's own W8A8 number format, FP8 e4m3 rowwise. Replaces the
+ * dynamic rowwise branch of `_quant_src` (reference w8a8.py:261-273):
+ * scale f32 [M] = max(amax_row / 448, 1e-12); q = e4m3 bytes [M, K] of
+ * clamp(bf16(x * bf16(1 / scale)), +-448), nearest-even. */
+int gwb_fp8_quant(const void* x, int64_t M, int64_t K, void* q, void* scale, void* stream);
+
+/* Replaces `torch._scaled_mm(xq, w.t(), scale_a, scale_b, bias)` rowwise in
+ * `Fp8ScaledLinear.forward` (reference w8a8.py:374-378): w_q e4m3 bytes
+ * [N, K] and w_scale f32 [N] as the reference's producer writes them
+ * (`quantize_tree_w8a8`, w8a8.py:774-779); f32 accumulation; gelu != 0
+ * fuses GELU(tanh). */
+int gwb_fp8_gemm(const void* q, const float* scale, const void* w_q, const float* w_scale,
+                 const void* bias, int64_t M, int64_t N, int64_t K, int gelu, void* out,
+                 void* stream);
+
+/* Whole `Fp8ScaledLinear.forward` rowwise (reference w8a8.py:359-381):
+ * quantise into the caller's scratch q [M, K] / scale [M], then GEMM. */
+int gwb_fp8_linear(const void* x, const void* w_q, const float* w_scale, const void* bias,
+                   int64_t M, int64_t N, int64_t K, int gelu, void* q, void* scale,
+                   void* out, void* stream);
+
 /* Reads and clears the device-side error flag set by a bounded wait that
  * expired (0 = none). Synchronises the device. */
 int gwb_device_error(int* code);

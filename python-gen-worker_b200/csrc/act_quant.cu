@@ -9,6 +9,7 @@
 // half-to-even, clamp.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cstdint>
 #include "gwb.h"
 #include "ptx.cuh"
@@ -353,6 +354,58 @@ int launch_act_int8(const void* x, void* q, void* scale, int M, int K, cudaStrea
   act_int8_kernel<<<grid, block, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
                                           static_cast<int8_t*>(q), static_cast<float*>(scale),
                                           M, K);
+  return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
+}
+
+// FP8 (e4m3) rowwise, one warp per row as act_int8_kernel: the dynamic
+// rowwise branch of the reference's _quant_src
+// (src/gen_worker/models/w8a8.py:261-273): sa = max(amax / 448, 1e-12) in
+// f32; the reciprocal 1/sa (f32) rounded to bf16; q = e4m3(clamp(bf16(x *
+// inv), +-448)), round-to-nearest-even with subnormals. x * inv is exact in
+// f32 (two 8-bit significands), so its bf16 rounding matches a bf16 multiply.
+__global__ void __launch_bounds__(256)
+act_fp8_kernel(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q,
+               float* __restrict__ scale, int M, int K) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= M) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)warp * K);
+  const int nvec = K / 8;
+  float amax = 0.f;
+  for (int i = lane; i < nvec; i += 32) {
+    uint4 p = __ldg(xr + i);
+    uint32_t w[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) amax = fmaxf(amax, fmaxf(fabsf(bf_lo(w[j])), fabsf(bf_hi(w[j]))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float s = fmaxf(__fdiv_rn(amax, 448.0f), 1e-12f);
+  if (lane == 0) scale[warp] = s;
+  const float inv = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(1.0f, s)));
+  uint2* qr = reinterpret_cast<uint2*>(q + (size_t)warp * K);
+  for (int i = lane; i < nvec; i += 32) {
+    uint4 p = __ldg(xr + i);
+    uint32_t w[4] = {p.x, p.y, p.z, p.w};
+    uint32_t packed[2] = {0, 0};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 v;
+      v.x = fminf(fmaxf(__bfloat162float(__float2bfloat16_rn(bf_lo(w[j]) * inv)), -448.f), 448.f);
+      v.y = fminf(fmaxf(__bfloat162float(__float2bfloat16_rn(bf_hi(w[j]) * inv)), -448.f), 448.f);
+      const uint32_t pair = __nv_cvt_float2_to_fp8x2(v, __NV_SATFINITE, __NV_E4M3);
+      packed[j >> 1] |= (pair & 0xFFFFu) << (16 * (j & 1));
+    }
+    qr[i] = make_uint2(packed[0], packed[1]);
+  }
+}
+
+int launch_act_fp8(const void* x, void* q, void* scale, int M, int K, cudaStream_t st) {
+  const int warps_per_block = 8;
+  dim3 grid((M + warps_per_block - 1) / warps_per_block), block(warps_per_block * 32);
+  act_fp8_kernel<<<grid, block, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                         static_cast<uint8_t*>(q), static_cast<float*>(scale),
+                                         M, K);
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }
 

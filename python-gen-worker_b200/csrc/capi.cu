@@ -168,7 +168,7 @@ int gwb_w8a8_gemm(const void* q, const float* scale, const void* w_q, const floa
   if (M == 0) return GWB_SUCCESS;
   if (!fits_int(M) || !fits_int(N) || !fits_int(K)) return GWB_E_SHAPE;
   gwb::W8A8Args a{q, scale, w_q, w_scale, bias, out, (int)M, (int)N, (int)K, gelu ? 1 : 0};
-  return gwb::launch_gemm_w8a8(a, S(stream));
+  return gwb::launch_gemm_w8a8(a, false, S(stream));
 }
 
 int gwb_w8a8_linear(const void* x, const void* w_q, const float* w_scale, const void* bias,
@@ -180,6 +180,33 @@ int gwb_w8a8_linear(const void* x, const void* w_q, const float* w_scale, const 
   if (rc) return rc;
   return gwb_w8a8_gemm(q, static_cast<const float*>(scale), w_q, w_scale, bias, M, N, K, gelu,
                        out, stream);
+}
+
+int gwb_fp8_quant(const void* x, int64_t M, int64_t K, void* q, void* scale, void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  if (!fits_int(M) || !fits_int(K) || K % 8 || K == 0) return GWB_E_SHAPE;
+  if (!al16(x) || !al16(q) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return GWB_E_ALIGN;
+  return gwb::launch_act_fp8(x, q, scale, (int)M, (int)K, S(stream));
+}
+
+int gwb_fp8_gemm(const void* q, const float* scale, const void* w_q, const float* w_scale,
+                 const void* bias, int64_t M, int64_t N, int64_t K, int gelu, void* out,
+                 void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  if (!fits_int(M) || !fits_int(N) || !fits_int(K)) return GWB_E_SHAPE;
+  gwb::W8A8Args a{q, scale, w_q, w_scale, bias, out, (int)M, (int)N, (int)K, gelu ? 1 : 0};
+  return gwb::launch_gemm_w8a8(a, true, S(stream));
+}
+
+int gwb_fp8_linear(const void* x, const void* w_q, const float* w_scale, const void* bias,
+                   int64_t M, int64_t N, int64_t K, int gelu, void* q, void* scale, void* out,
+                   void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  if (!fits_int(N) || K % 128 || N % 256) return GWB_E_SHAPE;
+  int rc = gwb_fp8_quant(x, M, K, q, scale, stream);
+  if (rc) return rc;
+  return gwb_fp8_gemm(q, static_cast<const float*>(scale), w_q, w_scale, bias, M, N, K, gelu,
+                      out, stream);
 }
 
 int gwb_device_error(int* code) {

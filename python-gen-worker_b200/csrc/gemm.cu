@@ -1,20 +1,17 @@
-// TMA-fed tcgen05 kind::i8 GEMMs for the SVDQuant hot path.
+// TMA-fed tcgen05 GEMMs for the SVDQuant hot path (persistent tiles).
 //
-//  * gemm_w8a8_kernel: INT8 per-token x INT8 per-output-channel, one s32
-//    accumulation over all of K in TMEM, epilogue = s32 -> f32 * a_scale[m] *
-//    w_scale[n] + bias[n] (+ GELU tanh) -> bf16.  Tile 128 x 256 x 128.
-//  * gemm_w4a4_kernel: packed INT4 (group 64) operands arrive by TMA into a
-//    staging ring, unpack warps sign-extend nibbles to int8 in the 128B-swizzled
-//    UMMA layout, each 64-wide K group accumulates in its own TMEM s32 buffer
-//    (ping-pong), and the epilogue warps promote it into an f32 register
-//    accumulator with a_scale[m,g] * w_scale[n,g]. The low-rank branch
-//    la·proj_upᵀ is one kind::f16 MMA chain whose f32 result seeds the
-//    accumulator; bias / GELU / bf16 conversion happen before the store.
-//    Tile 128 x 128 x 128.
-//
-// Warp roles (both kernels): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
-// issuer, warps 2-3 = INT4 unpack (W4A4 only), warps 4-7 = epilogue
-// (warp 4+q reads TMEM lanes 32q..32q+31, i.e. tile rows 32q..32q+31).
+//  * gemm_w8a8_kernel: W8A8 per-token x per-output-channel, INT8 (kind::i8,
+//    s32 accumulator) or FP8 e4m3 (kind::f8f6f4, f32 accumulator); one
+//    accumulation over all of K in TMEM (two accumulators, so one tile's
+//    epilogue overlaps the next tile's k-loop); epilogue = acc * a_scale[m] *
+//    w_scale[n] + bias[n] (+ GELU tanh) -> bf16. Tile 128 x 256 x 128.
+//  * gemm_w4a4_kernel: INT4 group-64 codes as e4m3 operands (q * 2^-9): per
+//    64-group the tensor core forms the exact group sum V (f32, TMEM) and the
+//    scale product S = a_scale ⊗ w_scale (kind::f16, TMEM); the epilogue
+//    promotes acc += V * S in registers. The low-rank branch la·proj_upᵀ is
+//    one kind::f16 MMA chain whose f32 result seeds the accumulator; bias /
+//    GELU / bf16 conversion happen before the store. Activations arrive in
+//    the operand form or as packed codes expanded in shared memory.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -79,6 +76,9 @@ constexpr int EPI_WARPS = 8;
 constexpr int EC = BN / 2;
 }  // namespace w8
 
+// FP8 = false: s8 x s8 -> s32 (kind::i8); FP8 = true: e4m3 x e4m3 -> f32
+// (kind::f8f6f4), the reference's own W8A8 number format.
+template <bool FP8>
 __global__ void __launch_bounds__(w8::THREADS, 1)
 gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const float* __restrict__ a_scale, const float* __restrict__ w_scale,
@@ -137,7 +137,7 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       }
     } else if (warp == 1 && lane == 0) {
       // -------------------------------------------------------------- MMA
-      constexpr uint32_t idesc = idesc_i8(kBM, BN);
+      constexpr uint32_t idesc = FP8 ? idesc_fmt0_f32(kBM, BN) : idesc_i8(kBM, BN);
       int it = 0, lt = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++lt) {
@@ -152,9 +152,14 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           const uint32_t a_base = smem_u32(smem + s * STAGE_BYTES);
           const uint32_t b_base = a_base + A_BYTES;
 #pragma unroll
-          for (int k = 0; k < kBK / 32; ++k)
-            mma_i8(d, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k), idesc,
-                   (kb > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < kBK / 32; ++k) {
+            if constexpr (FP8)
+              mma_f8(d, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k), idesc,
+                     (kb > 0 || k > 0) ? 1u : 0u);
+            else
+              mma_i8(d, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k), idesc,
+                     (kb > 0 || k > 0) ? 1u : 0u);
+          }
           mma_commit(&empty[s]);
         }
         if (ok) mma_commit(&acc_full[b]);
@@ -192,7 +197,8 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         float f[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) f[j] = (float)(int)v[c + j] * sa * ws[j];
+        for (int j = 0; j < 8; ++j)
+          f[j] = (FP8 ? __uint_as_float(v[c + j]) : (float)(int)v[c + j]) * sa * ws[j];
         if (bias != nullptr) {
           const uint4 bw = __ldg(reinterpret_cast<const uint4*>(bias + n0 + cb + c));
           const uint32_t w[4] = {bw.x, bw.y, bw.z, bw.w};
@@ -672,7 +678,7 @@ static int sm_count() {
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int launch_gemm_w8a8(const W8A8Args& a, cudaStream_t st) {
+int launch_gemm_w8a8(const W8A8Args& a, bool fp8, cudaStream_t st) {
   if (a.M <= 0 || a.K <= 0 || a.K % kBK || a.N % w8::BN) return GWB_E_SHAPE;
   if (!al16(a.a_q) || !al16(a.w_q) || !al16(a.out) || !al16(a.w_scale) ||
       (a.bias && !al16(a.bias)))
@@ -686,14 +692,17 @@ int launch_gemm_w8a8(const W8A8Args& a, cudaStream_t st) {
   if (rc) return rc;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(gemm_w8a8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(gemm_w8a8_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         w8::SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_w8a8_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          w8::SMEM_BYTES);
     attr = true;
   }
   const int n_sm = sm_count();
   const int ntiles = ((a.M + kBM - 1) / kBM) * (a.N / w8::BN);
   const int grid = ntiles < n_sm ? ntiles : n_sm;
-  gemm_w8a8_kernel<<<grid, w8::THREADS, w8::SMEM_BYTES, st>>>(
+  auto kern = fp8 ? gemm_w8a8_kernel<true> : gemm_w8a8_kernel<false>;
+  kern<<<grid, w8::THREADS, w8::SMEM_BYTES, st>>>(
       tA, tB, a.a_scale, a.w_scale, static_cast<const __nv_bfloat16*>(a.bias),
       static_cast<__nv_bfloat16*>(a.out), a.M, a.N, a.K, a.gelu);
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;

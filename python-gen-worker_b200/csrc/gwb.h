@@ -22,6 +22,7 @@ int launch_act_int4(const void* x, const void* smooth, const void* down_t, void*
                     cudaStream_t st);
 int launch_scale_k8(const void* scale, void* scale_k8, int R, int K, cudaStream_t st);
 int launch_act_int8(const void* x, void* q, void* scale, int M, int K, cudaStream_t st);
+int launch_act_fp8(const void* x, void* q, void* scale, int M, int K, cudaStream_t st);
 
 struct W4A4Args {
   const void* a_codes;     // u8 [M, K/2] packed INT4 (a_packed) or u8 [M, K] operand form
@@ -41,7 +42,7 @@ int launch_w4a4_weight_expand(const void* w_codes, void* w_q8, int64_t N, int64_
 
 
 struct W8A8Args {
-  const void* a_q;        // s8 [M, K]
+  const void* a_q;        // s8 [M, K] (INT8) or e4m3 bytes [M, K] (FP8)
   const float* a_scale;   // f32 [M]
   const void* w_q;        // s8 [N, K]
   const float* w_scale;   // f32 [N]
@@ -49,7 +50,7 @@ struct W8A8Args {
   void* out;              // bf16 [M, N]
   int M, N, K, gelu;
 };
-int launch_gemm_w8a8(const W8A8Args& a, cudaStream_t st);
+int launch_gemm_w8a8(const W8A8Args& a, bool fp8, cudaStream_t st);
 
 int device_error_read_and_clear(int* code);
 }  // namespace gwb

@@ -182,6 +182,52 @@ class W8A8Int8Linear(nn.Module):
                 f"bias={self.bias is not None}, gelu={self.gelu}, mode=int8-rowwise")
 
 
+class Fp8RowwiseLinear(nn.Module):
+    """Drop-in for the reference's ``Fp8ScaledLinear`` in rowwise mode
+    (``src/gen_worker/models/w8a8.py:359-381``): buffers ``weight``
+    float8_e4m3fn [N, K], ``weight_scale`` f32 [N, 1], ``bias``; per-token
+    dynamic FP8 activations; one tcgen05 kind::f8f6f4 GEMM with the scales,
+    bias and (optionally) GELU(tanh) fused."""
+    _cozy_w8a8_linear = True
+
+    def __init__(self, in_features: int, out_features: int, *, bias: bool,
+                 compute_dtype: Any = torch.bfloat16, gelu: bool = False,
+                 device: Any = None) -> None:
+        super().__init__()
+        if in_features % 128 or out_features % 256:
+            raise SvdqB200LayoutError(
+                f"Fp8RowwiseLinear dims [{out_features}, {in_features}] break the tile "
+                f"alignment (in%128, out%256)")
+        self.in_features = int(in_features)
+        self.out_features = int(out_features)
+        self.gelu = bool(gelu)
+        self.compute_dtype = compute_dtype
+        dev = device or torch.device("meta")
+        self.register_buffer("weight", torch.empty(out_features, in_features,
+                                                   dtype=torch.float8_e4m3fn, device=dev))
+        self.register_buffer("weight_scale", torch.empty(out_features, 1, dtype=torch.float32,
+                                                         device=dev))
+        if bias:
+            self.bias: Optional[nn.Parameter] = nn.Parameter(
+                torch.empty(out_features, dtype=compute_dtype, device=dev), requires_grad=False)
+        else:
+            self.bias = None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        x2 = x.reshape(-1, self.in_features)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        q, s = ops.fp8_quant(x2)
+        y = ops.fp8_gemm(q, s, self.weight, self.weight_scale.reshape(-1),
+                         self.bias.detach() if self.bias is not None else None, self.gelu)
+        return y.reshape(*shape[:-1], self.out_features)
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, "
+                f"bias={self.bias is not None}, gelu={self.gelu}, mode=fp8-rowwise")
+
+
 # ---------------------------------------------------------------- builders / swap
 def build_svdq_int4_linear(buf: Dict[str, Any], *, gelu: bool = False,
                            device: Any = None) -> SvdqInt4Linear:
@@ -225,6 +271,44 @@ def build_w8a8_int8_linear(buf: Dict[str, Any], *, gelu: bool = False,
         mod.bias = nn.Parameter(buf["bias"].detach().to(torch.bfloat16).reshape(-1).to(dev),
                                 requires_grad=False)
     return mod
+
+
+def build_fp8_rowwise_linear(buf: Dict[str, Any], *, gelu: bool = False,
+                             device: Any = None) -> Fp8RowwiseLinear:
+    """From the reference's W8A8 checkpoint tensors: ``weight``
+    float8_e4m3fn (or its bytes) [N, K], ``weight_scale`` f32 [N] or [N, 1],
+    optional ``bias``."""
+    w = buf["weight"]
+    n, k = w.shape
+    mod = Fp8RowwiseLinear(k, n, bias=buf.get("bias") is not None, gelu=gelu,
+                           device=torch.device("cpu"))
+    dev = device or w.device
+    if w.dtype == torch.uint8:
+        w = w.view(torch.float8_e4m3fn)
+    if w.dtype != torch.float8_e4m3fn:
+        raise SvdqB200LayoutError(f"Fp8RowwiseLinear weight dtype {w.dtype} is not e4m3")
+    mod.weight = w.contiguous().to(dev)
+    mod.weight_scale = buf["weight_scale"].float().reshape(n, 1).contiguous().to(dev)
+    if mod.bias is not None:
+        mod.bias = nn.Parameter(buf["bias"].detach().to(torch.bfloat16).reshape(-1).to(dev),
+                                requires_grad=False)
+    return mod
+
+
+def quantize_fp8_rows(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """The reference's data-free W8A8 producer (``quantize_tree_w8a8``,
+    ``w8a8.py:774-779``): per output row ``scale = max(amax/448, 1e-12)``,
+    ``e4m3(clamp(w/scale, ±448))`` -> (float8_e4m3fn [N, K], f32 [N])."""
+    wf = w.float()
+    scale = (wf.abs().amax(dim=1, keepdim=True) / 448.0).clamp(min=1e-12)
+    return (wf / scale).clamp(-448.0, 448.0).to(torch.float8_e4m3fn), scale.reshape(-1)
+
+
+def fp8_rowwise_from_linear(lin: nn.Linear, gelu: bool = False) -> Fp8RowwiseLinear:
+    q, s = quantize_fp8_rows(lin.weight.detach())
+    buf = {"weight": q, "weight_scale": s,
+           "bias": lin.bias.detach() if lin.bias is not None else None}
+    return build_fp8_rowwise_linear(buf, gelu=gelu, device=lin.weight.device)
 
 
 def svdq_int4_from_linear(lin: nn.Linear, smooth: Optional[torch.Tensor] = None,

@@ -268,6 +268,60 @@ def _(q, scale, w_q, w_scale, bias, gelu):
     return q.new_empty(q.shape[0], w_q.shape[0], dtype=torch.bfloat16)
 
 
+# ---------------------------------------------------------------- FP8 rowwise
+def _as_fp8_bytes(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype == torch.float8_e4m3fn:
+        t = t.view(torch.uint8)
+    _need(t, name, torch.uint8, 2)
+    return t
+
+
+@torch.library.custom_op("gwb200::fp8_quant", mutates_args=())
+def fp8_quant(x2: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-token FP8 e4m3 (the reference's dynamic rowwise ``_quant_src``,
+    ``w8a8.py:261-273``): x2 bf16 [M, K] -> (q e4m3 bytes u8 [M, K],
+    scale f32 [M])."""
+    _need(x2, "x2", torch.bfloat16, 2)
+    m, k = x2.shape
+    q = torch.empty(m, k, dtype=torch.uint8, device=x2.device)
+    s = torch.empty(m, dtype=torch.float32, device=x2.device)
+    lib = native.require()
+    native.check(lib.gwb_fp8_quant(x2.data_ptr(), m, k, q.data_ptr(), s.data_ptr(), _stream()),
+                 "fp8_quant")
+    return q, s
+
+
+@fp8_quant.register_fake
+def _(x2):
+    return x2.new_empty(x2.shape, dtype=torch.uint8), x2.new_empty(x2.shape[0], dtype=torch.float32)
+
+
+@torch.library.custom_op("gwb200::fp8_gemm", mutates_args=())
+def fp8_gemm(q: torch.Tensor, scale: torch.Tensor, w_q: torch.Tensor, w_scale: torch.Tensor,
+             bias: Optional[torch.Tensor], gelu: bool) -> torch.Tensor:
+    """``_scaled_mm`` rowwise on e4m3 operands (``Fp8ScaledLinear.forward``,
+    ``w8a8.py:374-378``): q / w_q e4m3 bytes (u8 or float8_e4m3fn) [M, K] /
+    [N, K], scale f32 [M], w_scale f32 [N] -> bf16 [M, N] (+ GELU)."""
+    q = _as_fp8_bytes(q, "q")
+    w_q = _as_fp8_bytes(w_q, "w_q")
+    _need(scale, "scale", torch.float32, 1)
+    _need(w_scale, "w_scale", torch.float32, 1)
+    _need(bias, "bias", torch.bfloat16, 1)
+    m, k = q.shape
+    n = w_q.shape[0]
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=q.device)
+    lib = native.require()
+    native.check(lib.gwb_fp8_gemm(q.data_ptr(), scale.data_ptr(), w_q.data_ptr(),
+                                  w_scale.data_ptr(), _ptr(bias), m, n, k, int(bool(gelu)),
+                                  out.data_ptr(), _stream()), "fp8_gemm")
+    return out
+
+
+@fp8_gemm.register_fake
+def _(q, scale, w_q, w_scale, bias, gelu):
+    return q.new_empty(q.shape[0], w_q.shape[0], dtype=torch.bfloat16)
+
+
 # ---------------------------------------------------------------- load-time repacks
 def prepare_w4a4_weights(w_scale: Optional[torch.Tensor], proj_down: Optional[torch.Tensor],
                          proj_up: Optional[torch.Tensor],

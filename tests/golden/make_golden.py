@@ -19,7 +19,12 @@ Everything is produced by CALLING the reference's own functions:
   arithmetic -> xs bf16;
 * ``quantize_activation_torch`` (``nvfp4_quant.py:92-103``) -> the
   amax -> rounded-scale -> divide -> code structure the INT4 quantiser
-  follows (kept for the NVFP4 follow-on lane).
+  follows (kept for the NVFP4 follow-on lane);
+* the FP8 rowwise activation quantiser ``_quant_src`` (dynamic, rowwise;
+  ``src/gen_worker/models/w8a8.py:261-273``, reached through
+  ``_build_quantizer(torch).eager_source``) -> e4m3 codes and f32 row scales
+  over rows spanning many binades, an all-zero row and a row whose values
+  fall into the e4m3 subnormal range after scaling.
 """
 from __future__ import annotations
 
@@ -53,6 +58,7 @@ def main(ref_root: str = "/root/reference") -> None:
     from gen_worker.models import nvfp4_quant as nq
     from gen_worker.models import svdq_layout as sl
     from gen_worker.models import svdq_native as sn
+    from gen_worker.models import w8a8
 
     gen = torch.Generator().manual_seed(1234)
     out = {}
@@ -100,6 +106,17 @@ def main(ref_root: str = "/root/reference") -> None:
     s2 = (xa.abs().amax().float() / (6.0 * 448.0)).clamp(min=1e-12)
     qa, sa = nq.quantize_activation_torch(xa, s2)
     out["nvfp4_x"], out["nvfp4_s2"], out["nvfp4_q"], out["nvfp4_sa"] = xa, s2, qa, sa
+
+    # 6. FP8 rowwise activation quantiser (the reference's own eager source)
+    quant_src = w8a8._build_quantizer(torch).eager_source
+    xf = torch.randn(48, 512, generator=gen)
+    xf = xf * torch.pow(2.0, torch.randint(-12, 10, (48, 1), generator=gen).float())
+    xf[7] = 0.0                                      # all-zero row -> clamp path
+    xf[11, :] *= 1e-3
+    xf[11, 0] = 1000.0                               # most of the row lands in e4m3 subnormals
+    xf = xf.to(torch.bfloat16)
+    fq, fs = quant_src(xf, False, None)
+    out["fp8_x"], out["fp8_q"], out["fp8_scale"] = xf, fq.view(torch.uint8), fs
 
     path = HERE / "reference_golden.pt"
     torch.save(out, path)

@@ -1,15 +1,18 @@
 """GPU parity of the CUDA path against the CPU oracle.
 
-Bit-exact: INT4/INT8 activation codes and scales, int32 group partials.
+Bit-exact: INT4/INT8/FP8 activation codes and scales, int32 group partials.
 bf16 outputs: rel-L2 <= 1e-3 against the oracle's bf16 output (the
 correctly rounded bf16 of its float64 result), and max-abs <= 2e-2 beyond
 the bf16 rounding of the float64 result itself."""
+from pathlib import Path
+
 import pytest
 import torch
 
 from oracle import svdq_oracle as O
 from gen_worker_b200 import ops, native
-from gen_worker_b200.modules import build_svdq_int4_linear, build_w8a8_int8_linear
+from gen_worker_b200.modules import (build_fp8_rowwise_linear, build_svdq_int4_linear,
+                                     build_w8a8_int8_linear)
 
 pytestmark = pytest.mark.gpu
 
@@ -180,3 +183,37 @@ def test_w8a8_linear_matches_oracle(cuda_ready, m, k, n, gelu):
     assert O.rel_l2(y, want["y"]) <= REL_TOL
     assert O.max_abs_beyond_bf16(y, want["y64"]) <= ABS_TOL
     assert native.device_error() == 0
+
+
+# ---------------------------------------------------------------- FP8 rowwise
+@pytest.mark.parametrize("m,k", [(1, 128), (77, 3072), (256, 12288), (48, 512)])
+def test_fp8_activation_bit_exact(cuda_ready, m, k):
+    """e4m3 codes and f32 row scales bit-identical to the oracle's
+    restatement of the reference's _quant_src (pinned by the golden
+    fixture); the (48, 512) case is the fixture's own input."""
+    if (m, k) == (48, 512):
+        x = torch.load(Path(__file__).parent / "golden" / "reference_golden.pt")["fp8_x"]
+    else:
+        x = O.synth_activation(m, k, seed=m + 3) * torch.pow(
+            2.0, torch.randint(-10, 10, (m, 1), generator=torch.Generator().manual_seed(m))
+        ).to(torch.bfloat16)
+        x = x.to(torch.bfloat16)
+    q, s = ops.fp8_quant(x.cuda())
+    want_q, want_s = O.quant_fp8_rows(x)
+    assert torch.equal(q.cpu(), want_q)
+    assert torch.equal(s.cpu(), want_s)
+
+
+@pytest.mark.parametrize("m,k,n,gelu", [(128, 128, 256, False), (333, 3072, 512, True),
+                                        (1024, 3072, 1024, False)])
+def test_fp8_linear_matches_oracle(cuda_ready, m, k, n, gelu):
+    x = O.synth_activation(m, k, seed=5 * m)
+    L = O.synth_fp8_layer(k, n, seed=m + n)
+    mod = build_fp8_rowwise_linear({"weight": L["w_q"], "weight_scale": L["w_scale"],
+                                    "bias": L["bias"]}, gelu=gelu, device="cuda")
+    y = mod(x.cuda()).cpu()
+    want = O.fp8_rowwise_linear(x, L["w_q"], L["w_scale"], L["bias"], gelu=gelu)
+    assert O.rel_l2(y, want["y"]) <= REL_TOL
+    assert O.max_abs_beyond_bf16(y, want["y64"]) <= ABS_TOL
+    assert native.device_error() == 0
+

@@ -9,9 +9,9 @@ import torch
 
 from oracle import svdq_oracle as O
 from gen_worker_b200 import native, ops
-from gen_worker_b200.modules import (SvdqInt4Linear, W8A8Int8Linear, SvdqB200LayoutError,
-                                     quantize_int4_rows, quantize_int8_rows, swap_linears,
-                                     build_svdq_int4_linear)
+from gen_worker_b200.modules import (Fp8RowwiseLinear, SvdqInt4Linear, W8A8Int8Linear,
+                                     SvdqB200LayoutError, quantize_fp8_rows, quantize_int4_rows,
+                                     quantize_int8_rows, swap_linears, build_svdq_int4_linear)
 
 ROOT = Path(__file__).resolve().parent.parent
 
@@ -67,6 +67,9 @@ def test_producer_matches_oracle_rules():
     q8, s8 = quantize_int8_rows(w)
     oq, osc = O.quant_int8_rows(w)
     assert torch.equal(q8, oq) and torch.equal(s8, osc)
+    f8, fs = quantize_fp8_rows(w)
+    ofq, ofs = O.quant_fp8_weight(w)
+    assert torch.equal(f8.view(torch.uint8), ofq) and torch.equal(fs, ofs)
 
 
 def test_prepare_repacks_layouts():
@@ -87,6 +90,10 @@ def test_module_surface_and_swap():
         SvdqInt4Linear(100, 128, rank=0, bias=False)
     with pytest.raises(SvdqB200LayoutError):
         W8A8Int8Linear(128, 128, bias=False)
+    with pytest.raises(SvdqB200LayoutError):
+        Fp8RowwiseLinear(128, 128, bias=False)
+    f = Fp8RowwiseLinear(256, 256, bias=True)
+    assert f.weight.dtype == torch.float8_e4m3fn and tuple(f.weight_scale.shape) == (256, 1)
     m = SvdqInt4Linear(256, 128, rank=32, bias=True)
     names = {n for n, _ in m.named_buffers()} | {n for n, _ in m.named_parameters()}
     assert {"weight", "weight_scale", "smooth_factor", "proj_down", "proj_up", "bias"} <= names

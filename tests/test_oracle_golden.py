@@ -42,6 +42,16 @@ def test_smoothing_divide_matches_reference_bf16_semantics():
     assert torch.equal(xs.view(torch.int16), GOLD["smooth_xs"].view(torch.int16))
 
 
+def test_fp8_rowwise_quantiser_matches_reference_quant_src():
+    """quant_fp8_rows restates the reference's dynamic rowwise _quant_src
+    (w8a8.py:261-273): e4m3 codes and f32 row scales bit for bit, including
+    an all-zero row (scale clamp) and a row mostly in e4m3 subnormals."""
+    q, s = O.quant_fp8_rows(GOLD["fp8_x"])
+    assert torch.equal(q, GOLD["fp8_q"])
+    assert torch.equal(s, GOLD["fp8_scale"].reshape(-1))
+    assert int((GOLD["fp8_q"][11] & 0x78 == 0).sum()) > 100   # subnormal codes exercised
+
+
 def test_quantiser_structure_reproduces_reference_nvfp4():
     """Restating quantize_activation_torch (nvfp4_quant.py:92-103) with the
     oracle's ordering (amax -> scale rounded to storage dtype -> divide by the
