@@ -167,6 +167,31 @@ int gwb_fp8_linear(const void* x, const void* w_q, const float* w_scale, const v
                    int64_t M, int64_t N, int64_t K, int gelu, void* q, void* scale,
                    void* out, void* stream);
 
+/* The reference's own SVDQuant format, NVFP4 (e2m1 codes, e4m3 scales per
+ * 16-element block in the cuBLAS blocked layout, fp32 second-level scale).
+ * Replaces `quantize_activation` / `quantize_activation_torch` (reference
+ * src/gen_worker/models/nvfp4_quant.py:92-103, 272-280) preceded by the
+ * smoothing divide and the per-tensor `s2` of `SvdqLinear.forward`
+ * (svdq_native.py:144-146): codes u8 [M, K/2] (element 2j in the low
+ * nibble), sblk = blocked e4m3 scales (ceil(M/128)*128 * K/16 bytes; the
+ * caller zero-fills it so the row padding matches the reference), work f32
+ * [2] (work[1] = s2 on return). Bit-identical to the reference. K % 64 == 0. */
+int gwb_nvfp4_quant(const void* x, const void* smooth, int64_t M, int64_t K, void* codes,
+                    void* sblk, float* work, void* stream);
+
+/* Replaces `_gemm_w4a4` (`torch._scaled_mm` on float4_e2m1fn_x2 with blocked
+ * scales, reference w4a4.py:173-180) and the rest of the NVFP4
+ * `SvdqLinear.forward` (svdq_native.py:148-155): y = (A·B^T with block scales)
+ * * s2 * w_scale_2[n] + la·proj_up^T + bias -> bf16 [M, N]. w_codes / w_sblk
+ * / w_scale_2 are the reference module's `weight` / `weight_scale` /
+ * `weight_scale_2` buffers as stored (w_scale_2 per channel [N] when
+ * ws2_per_channel, else [1]); la = bf16(x · proj_down) [M, rank_pad] on raw
+ * x. K % 256 == 0, N % 128 == 0. */
+int gwb_nvfp4_gemm(const void* a_codes, const void* a_sblk, const float* a_work,
+                   const void* w_codes, const void* w_sblk, const float* w_scale_2,
+                   int ws2_per_channel, const void* la, const void* proj_up, const void* bias,
+                   int64_t M, int64_t N, int64_t K, int rank_pad, void* out, void* stream);
+
 /* Reads and clears the device-side error flag set by a bounded wait that
  * expired (0 = none). Synchronises the device. */
 int gwb_device_error(int* code);

@@ -400,6 +400,146 @@ act_fp8_kernel(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q,
   }
 }
 
+// ------------------------------------------------------------------ NVFP4
+// The reference's NVFP4 activation quantiser (quantize_activation_torch,
+// src/gen_worker/models/nvfp4_quant.py:92-103), after the smoothing divide
+// and the per-tensor second-level scale of SvdqLinear.forward
+// (svdq_native.py:144-146).
+//   nvfp4_amax_kernel: amax |bf16(x / smooth)| over the whole tensor (fp32
+//     bits, atomicMax; the values are non-negative) into work[0].
+//   act_nvfp4_kernel: s2 = max(amax / 2688, 1e-12) (written to work[1]);
+//     per 16-block: sa = e4m3(clamp(bmax / (6 s2), 2^-9, 448)) (nearest-
+//     even), q = xs / (sa * s2) (fp32, correctly rounded), e2m1 code with the
+//     reference's tie rule (cast_e2m1, nvfp4_quant.py:41-51); codes packed
+//     with element 2j in the low nibble, scales written at their cuBLAS
+//     blocked-layout address (to_blocked_scales, nvfp4_quant.py:72-84).
+
+// bf16(x / smooth) for 8 packed bf16 (smooth reciprocals precomputed)
+__device__ __forceinline__ void smooth8(const uint4& xv, const uint4& sv, float (&o)[8]) {
+  const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+  const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float s0 = bf_lo(sw[j]), s1 = bf_hi(sw[j]);
+    o[2 * j] = __bfloat162float(__float2bfloat16_rn(div_rn(bf_lo(xw[j]), s0, __frcp_rn(s0))));
+    o[2 * j + 1] = __bfloat162float(__float2bfloat16_rn(div_rn(bf_hi(xw[j]), s1, __frcp_rn(s1))));
+  }
+}
+
+__device__ __forceinline__ void raw8(const uint4& xv, float (&o)[8]) {
+  const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) { o[2 * j] = bf_lo(xw[j]); o[2 * j + 1] = bf_hi(xw[j]); }
+}
+
+__global__ void __launch_bounds__(256)
+nvfp4_amax_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ smooth,
+                  unsigned int* __restrict__ amax_bits, int M, int K) {
+  const int64_t nvec = (int64_t)M * K / 8;
+  const int kv = K / 8;
+  float m = 0.f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x) + i);
+    float v[8];
+    if (smooth) smooth8(xv, __ldg(reinterpret_cast<const uint4*>(smooth) + (i % kv)), v);
+    else raw8(xv, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) b = fmaxf(b, red[w]);
+    atomicMax(amax_bits, __float_as_uint(b));
+  }
+}
+
+// e2m1 magnitude code of |q| with the reference's rounding: the number of the
+// bounds 0.25 0.75 1.25 1.75 2.5 3.5 5.0 strictly below |q|, plus one when
+// |q| is exactly 0.75, 1.75 or 2.5.
+__device__ __forceinline__ uint32_t e2m1_code(float q) {
+  const float a = fabsf(q);
+  uint32_t c = (a > 0.25f) + (a > 0.75f) + (a > 1.25f) + (a > 1.75f) + (a > 2.5f) +
+               (a > 3.5f) + (a > 5.0f);
+  c += (a == 0.75f) | (a == 1.75f) | (a == 2.5f);
+  return c | (q < 0.0f ? 8u : 0u);
+}
+
+__global__ void __launch_bounds__(256)
+act_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ smooth,
+                 float* __restrict__ work, uint8_t* __restrict__ codes,
+                 uint8_t* __restrict__ sblk, int M, int K) {
+  const float amax = __uint_as_float(*reinterpret_cast<const volatile unsigned int*>(work));
+  const float s2 = fmaxf(__fdiv_rn(amax, 6.0f * 448.0f), 1e-12f);
+  if (blockIdx.x == 0 && threadIdx.x == 0) work[1] = s2;
+  const float d6 = 6.0f * s2;
+  const int kb16 = K / 16;
+  const int ncb = (kb16 + 3) / 4;
+  const int64_t nblk = (int64_t)M * kb16;
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nblk;
+       b += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(b / kb16), c = (int)(b % kb16);
+    const uint4* xp = reinterpret_cast<const uint4*>(x + (size_t)row * K + c * 16);
+    float v[16];
+    float lo[8], hi[8];
+    if (smooth) {
+      const uint4* sp = reinterpret_cast<const uint4*>(smooth + c * 16);
+      smooth8(__ldg(xp), __ldg(sp), lo);
+      smooth8(__ldg(xp + 1), __ldg(sp + 1), hi);
+    } else {
+      raw8(__ldg(xp), lo);
+      raw8(__ldg(xp + 1), hi);
+    }
+    float bmax = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[j] = lo[j];
+      v[8 + j] = hi[j];
+      bmax = fmaxf(bmax, fmaxf(fabsf(lo[j]), fabsf(hi[j])));
+    }
+    const float t = fminf(fmaxf(__fdiv_rn(bmax, d6), 0.001953125f), 448.0f);
+    const uint32_t sbyte = __nv_cvt_float_to_fp8(t, __NV_SATFINITE, __NV_E4M3) & 0xFFu;
+    const __half_raw hr = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)sbyte, __NV_E4M3);
+    const float sa = __half2float(__half(hr));
+    const float den = sa * s2;
+    const float rden = __frcp_rn(den);
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      w0 |= e2m1_code(div_rn(v[j], den, rden)) << (4 * j);
+      w1 |= e2m1_code(div_rn(v[8 + j], den, rden)) << (4 * j);
+    }
+    *reinterpret_cast<uint2*>(codes + (size_t)row * (K / 2) + c * 8) = make_uint2(w0, w1);
+    const size_t off = ((size_t)(row >> 7) * ncb + (c >> 2)) * 512 + (row & 31) * 16 +
+                       ((row & 127) >> 5) * 4 + (c & 3);
+    sblk[off] = (uint8_t)sbyte;
+  }
+}
+
+int launch_act_nvfp4(const void* x, const void* smooth, float* work, void* codes, void* sblk,
+                     int M, int K, cudaStream_t st) {
+  if (cudaMemsetAsync(work, 0, sizeof(float), st) != cudaSuccess) return GWB_E_LAUNCH;
+  const int64_t nvec = (int64_t)M * K / 8;
+  int64_t blocks = (nvec + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  nvfp4_amax_kernel<<<(int)blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                                  static_cast<const __nv_bfloat16*>(smooth),
+                                                  reinterpret_cast<unsigned int*>(work), M, K);
+  const int64_t nblk = (int64_t)M * (K / 16);
+  blocks = (nblk + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  act_nvfp4_kernel<<<(int)blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                                 static_cast<const __nv_bfloat16*>(smooth), work,
+                                                 static_cast<uint8_t*>(codes),
+                                                 static_cast<uint8_t*>(sblk), M, K);
+  return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
+}
+
 int launch_act_fp8(const void* x, void* q, void* scale, int M, int K, cudaStream_t st) {
   const int warps_per_block = 8;
   dim3 grid((M + warps_per_block - 1) / warps_per_block), block(warps_per_block * 32);

@@ -209,6 +209,27 @@ int gwb_fp8_linear(const void* x, const void* w_q, const float* w_scale, const v
                       out, stream);
 }
 
+int gwb_nvfp4_quant(const void* x, const void* smooth, int64_t M, int64_t K, void* codes,
+                    void* sblk, float* work, void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  if (!fits_int(M) || !fits_int(K) || K % 64 || K == 0) return GWB_E_SHAPE;
+  if (!al16(x) || !al16(codes) || (smooth && !al16(smooth)) || !sblk || !work ||
+      (reinterpret_cast<uintptr_t>(work) & 7u))
+    return GWB_E_ALIGN;
+  return gwb::launch_act_nvfp4(x, smooth, work, codes, sblk, (int)M, (int)K, S(stream));
+}
+
+int gwb_nvfp4_gemm(const void* a_codes, const void* a_sblk, const float* a_work,
+                   const void* w_codes, const void* w_sblk, const float* w_scale_2,
+                   int ws2_per_channel, const void* la, const void* proj_up, const void* bias,
+                   int64_t M, int64_t N, int64_t K, int rank_pad, void* out, void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  if (!fits_int(M) || !fits_int(N) || !fits_int(K)) return GWB_E_SHAPE;
+  gwb::NvFp4Args a{a_codes, a_sblk, a_work, w_codes, w_sblk, w_scale_2, ws2_per_channel ? 1 : 0,
+                   la, proj_up, bias, out, (int)M, (int)N, (int)K, rank_pad};
+  return gwb::launch_gemm_nvfp4(a, S(stream));
+}
+
 int gwb_device_error(int* code) {
   if (!code) return GWB_E_SHAPE;
   if (cudaDeviceSynchronize() != cudaSuccess) return GWB_E_LAUNCH;

@@ -629,6 +629,212 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 }
 
 // ======================================================================
+// NVFP4 (the reference's SVDQuant format): kind::mxf4nvf4 block-scaled MMA
+// ======================================================================
+// Activations and weights are packed e2m1 codes with e4m3 scales per
+// 16-element block in the cuBLAS blocked layout (exactly the reference's
+// `weight` / `weight_scale` buffers and its quantiser output); the tensor
+// core applies the block scales itself. Per k-block of 256 elements: TMA
+// brings the 128 x 128-byte A and B tiles (SWIZZLE_128B) and two 2 KB
+// bulk copies bring the four 128 x 4 scale tiles of A and of B; the MMA
+// thread copies each scale tile into TMEM (tcgen05.cp) and issues four
+// K = 64 MMAs. Epilogue: y = acc * s2 * weight_scale_2[n] + la·proj_upᵀ +
+// bias (the low-rank product accumulates in its own TMEM columns).
+namespace nv4 {
+constexpr int BN = 128;
+constexpr int KB_BYTES = 128;                 // packed bytes of one k-block row (256 codes)
+constexpr int STAGES = 5;
+constexpr int A_BYTES = kBM * KB_BYTES;       // 16 KB
+constexpr int B_BYTES = BN * KB_BYTES;        // 16 KB
+constexpr int SF_BYTES = 4 * 512;             // four 128 x 4 blocked scale tiles
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + 2 * SF_BYTES;    // 36 KB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int TMEM_COLS = 512;
+constexpr int ACC_COL = 0, LR_COL = 128, SF_COL = 256;
+constexpr int SF_SLOTS = 4;                   // 32 columns each: SFA 16, SFB 16
+constexpr int THREADS = 384;                  // warp 0 TMA, 1 MMA, 4-11 epilogue
+constexpr int EPI0 = 4;
+constexpr int EPI_WARPS = 8;
+constexpr int EC = BN / 2;
+}  // namespace nv4
+
+static_assert(nv4::SMEM_BYTES <= 232448, "NVFP4 shared memory exceeds 227 KB");
+
+__global__ void __launch_bounds__(nv4::THREADS, 1)
+gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                  const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmUP,
+                  const uint8_t* __restrict__ a_sblk, const uint8_t* __restrict__ w_sblk,
+                  const float* __restrict__ a_work, const float* __restrict__ w_scale_2,
+                  int ws2_per_channel, const __nv_bfloat16* __restrict__ bias,
+                  __nv_bfloat16* __restrict__ out, int M, int N, int K, int rank_pad) {
+  using namespace nv4;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = K / 256;
+  const int ncb = K / 64;                     // blocked-layout tile columns per 128 rows
+  const int has_lr = rank_pad > 0 ? 1 : 0;
+  const int tiles_n = N / BN;
+  const int ntiles = ((M + kBM - 1) / kBM) * tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, EPI_WARPS);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) { tmem_alloc(tmem_slot, TMEM_COLS); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < EPI0) {
+    regs_dec<48>();
+    if (warp == 0 && lane < 4) {
+      // -------------------------------------------------------------- TMA
+      // lane 0 A (and the low-rank operands), lane 1 B, lane 2 A scales,
+      // lane 3 B scales
+      const int pl = lane;
+      int ui = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+        const int mt = tile / tiles_n, m0 = mt * kBM, n0 = (tile % tiles_n) * BN;
+        if (has_lr) {
+          const int u = ui % STAGES;
+          ok = mbar_wait(&empty[u], ((ui / STAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER);
+          if (!__all_sync(0xFu, ok)) break;
+          if (pl == 0) {
+            uint8_t* us = smem + u * STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[u], kBM * 128 + BN * 128);
+            tma_load_2d(us, &tmLA, &full[u], 0, m0);
+            tma_load_2d(us + A_BYTES, &tmUP, &full[u], 0, n0);
+          }
+          __syncwarp(0xFu);
+          ++ui;
+        }
+        for (int kb = 0; kb < nk; ++kb, ++ui) {
+          const int u = ui % STAGES;
+          ok = mbar_wait(&empty[u], ((ui / STAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER);
+          if (!__all_sync(0xFu, ok)) break;
+          if (pl == 0) mbar_arrive_expect_tx(&full[u], STAGE_BYTES);
+          __syncwarp(0xFu);
+          uint8_t* us = smem + u * STAGE_BYTES;
+          if (pl == 0) tma_load_2d(us, &tmA, &full[u], kb * KB_BYTES, m0);
+          else if (pl == 1) tma_load_2d(us + A_BYTES, &tmB, &full[u], kb * KB_BYTES, n0);
+          else if (pl == 2)
+            bulk_load(us + A_BYTES + B_BYTES, a_sblk + ((size_t)mt * ncb + 4 * kb) * 512,
+                      SF_BYTES, &full[u]);
+          else
+            bulk_load(us + A_BYTES + B_BYTES + SF_BYTES,
+                      w_sblk + ((size_t)(n0 / 128) * ncb + 4 * kb) * 512, SF_BYTES, &full[u]);
+        }
+      }
+    } else if (warp == 1 && lane == 0) {
+      // -------------------------------------------------------------- MMA
+      constexpr uint32_t idesc = idesc_mxf4(kBM, BN);
+      constexpr uint32_t idesc_lr = idesc_bf16(kBM, BN);
+      int ui = 0, lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++lt) {
+        if (!mbar_wait(acc_empty, (lt & 1) ^ 1, GWB_ERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        if (has_lr) {
+          const int u = ui % STAGES;
+          if (!mbar_wait(&full[u], (ui / STAGES) & 1, GWB_ERR_TIMEOUT_MMA)) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + u * STAGE_BYTES), b_base = a_base + A_BYTES;
+          for (int k = 0; k < rank_pad / 16; ++k)
+            mma_f16(tmem + LR_COL, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k),
+                    idesc_lr, k > 0 ? 1u : 0u);
+          mma_commit(&empty[u]);
+          ++ui;
+        }
+        for (int kb = 0; kb < nk; ++kb, ++ui) {
+          const int u = ui % STAGES;
+          if (!mbar_wait(&full[u], (ui / STAGES) & 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + u * STAGE_BYTES);
+          const uint32_t b_base = a_base + A_BYTES;
+          const uint32_t sfa_s = b_base + B_BYTES, sfb_s = sfa_s + SF_BYTES;
+          const uint32_t sfa_t = tmem + SF_COL + (ui % SF_SLOTS) * 32, sfb_t = sfa_t + 16;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            tmem_cp_32x128b_x4(sfa_t + 4 * ks, sdesc_noswz(sfa_s + 512 * ks, 0));
+            tmem_cp_32x128b_x4(sfb_t + 4 * ks, sdesc_noswz(sfb_s + 512 * ks, 0));
+          }
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            mma_mxf4(tmem + ACC_COL, sdesc_k128(a_base + 32 * ks), sdesc_k128(b_base + 32 * ks),
+                     idesc, sfa_t + 4 * ks, sfb_t + 4 * ks, (kb > 0 || ks > 0) ? 1u : 0u);
+          mma_commit(&empty[u]);
+        }
+        if (ok) mma_commit(acc_full);
+      }
+    }
+  } else {
+    regs_inc<224>();
+    // ---------------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const int cb = ((warp - EPI0) >> 2) * EC;
+    const float s2 = a_work[1];
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++lt) {
+      const int m0 = (tile / tiles_n) * kBM, n0 = (tile % tiles_n) * BN;
+      if (!mbar_wait(acc_full, lt & 1, GWB_ERR_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      uint32_t v[EC], lr[EC];
+      const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) + cb;
+#pragma unroll
+      for (int c = 0; c < EC; c += 32) tmem_ld32(base + ACC_COL + c, v + c);
+      if (has_lr) {
+#pragma unroll
+        for (int c = 0; c < EC; c += 32) tmem_ld32(base + LR_COL + c, lr + c);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+      const int row = m0 + 32 * q + lane;
+      if (row >= M) continue;
+      uint4* op = reinterpret_cast<uint4*>(out + (size_t)row * N + n0 + cb);
+#pragma unroll
+      for (int c = 0; c < EC; c += 8) {
+        float f[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float w2 = ws2_per_channel ? __ldg(w_scale_2 + n0 + cb + c + j) : __ldg(w_scale_2);
+          f[j] = __uint_as_float(v[c + j]) * (s2 * w2);
+          if (has_lr) f[j] += __uint_as_float(lr[c + j]);
+        }
+        if (bias != nullptr) {
+          const uint4 bw = __ldg(reinterpret_cast<const uint4*>(bias + n0 + cb + c));
+          const uint32_t w[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            f[2 * j] += __uint_as_float(w[j] << 16);
+            f[2 * j + 1] += __uint_as_float(w[j] & 0xFFFF0000u);
+          }
+        }
+        op[c / 8] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                               pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ======================================================================
 // host side: tensor maps + launches
 // ======================================================================
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -765,6 +971,50 @@ int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, cudaStream_t st) {
       tA, tB, tAS, tBS, tLA, tUP, static_cast<const __nv_bfloat16*>(a.bias),
       static_cast<__nv_bfloat16*>(a.out), a.partials, a.M, a.N, a.K,
       a.partials ? 0 : a.rank_pad, a.gelu);
+  return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
+}
+
+int launch_gemm_nvfp4(const NvFp4Args& a, cudaStream_t st) {
+  if (a.M <= 0 || a.K <= 0 || a.K % 256 || a.N % nv4::BN) return GWB_E_SHAPE;
+  if (a.rank_pad < 0 || a.rank_pad > 64 || a.rank_pad % 16) return GWB_E_SHAPE;
+  if (a.rank_pad > 0 && (!a.la || !a.up)) return GWB_E_SHAPE;
+  if (!a.a_codes || !a.w_codes || !a.a_sblk || !a.w_sblk || !a.a_work || !a.w_scale_2 || !a.out)
+    return GWB_E_SHAPE;
+  if (!al16(a.a_codes) || !al16(a.w_codes) || !al16(a.a_sblk) || !al16(a.w_sblk) ||
+      !al16(a.out) || (a.bias && !al16(a.bias)) || (a.la && !al16(a.la)) ||
+      (a.up && !al16(a.up)) || (reinterpret_cast<uintptr_t>(a.a_work) & 7u) ||
+      (reinterpret_cast<uintptr_t>(a.w_scale_2) & 3u))
+    return GWB_E_ALIGN;
+  CUtensorMap tA, tB, tLA, tUP;
+  int rc = make_tmap(&tA, a.a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K / 2, a.M,
+                     nv4::KB_BYTES, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tmap(&tB, a.w_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K / 2, a.N, nv4::KB_BYTES,
+                 nv4::BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  tLA = tA;
+  tUP = tB;
+  if (a.rank_pad > 0) {
+    rc = make_tmap(&tLA, a.la, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.rank_pad, a.M, 64, kBM,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_tmap(&tUP, a.up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.rank_pad, a.N, 64, nv4::BN,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(gemm_nvfp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         nv4::SMEM_BYTES);
+    attr = true;
+  }
+  const int ntiles = ((a.M + kBM - 1) / kBM) * (a.N / nv4::BN);
+  const int n_sm = sm_count();
+  gemm_nvfp4_kernel<<<ntiles < n_sm ? ntiles : n_sm, nv4::THREADS, nv4::SMEM_BYTES, st>>>(
+      tA, tB, tLA, tUP, static_cast<const uint8_t*>(a.a_sblk),
+      static_cast<const uint8_t*>(a.w_sblk), a.a_work, a.w_scale_2, a.ws2_per_channel,
+      static_cast<const __nv_bfloat16*>(a.bias), static_cast<__nv_bfloat16*>(a.out), a.M, a.N,
+      a.K, a.rank_pad);
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }
 

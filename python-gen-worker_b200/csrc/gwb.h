@@ -23,6 +23,26 @@ int launch_act_int4(const void* x, const void* smooth, const void* down_t, void*
 int launch_scale_k8(const void* scale, void* scale_k8, int R, int K, cudaStream_t st);
 int launch_act_int8(const void* x, void* q, void* scale, int M, int K, cudaStream_t st);
 int launch_act_fp8(const void* x, void* q, void* scale, int M, int K, cudaStream_t st);
+// NVFP4 activations: work f32 [2] (work[0] amax scratch, work[1] = s2 out);
+// codes u8 [M, K/2]; sblk = blocked e4m3 scales (caller zero-fills the padding).
+int launch_act_nvfp4(const void* x, const void* smooth, float* work, void* codes, void* sblk,
+                     int M, int K, cudaStream_t st);
+
+struct NvFp4Args {
+  const void* a_codes;     // u8 [M, K/2] packed e2m1 (element 2j low nibble)
+  const void* a_sblk;      // e4m3 block scales, cuBLAS blocked layout
+  const float* a_work;     // f32 [2]; [1] = activation second-level scale s2
+  const void* w_codes;     // u8 [N, K/2]
+  const void* w_sblk;      // e4m3 block scales, blocked layout
+  const float* w_scale_2;  // f32 [1] or [N]
+  int ws2_per_channel;
+  const void* la;          // bf16 [M, rank_pad] or null
+  const void* up;          // bf16 [N, rank_pad] or null
+  const void* bias;        // bf16 [N] or null
+  void* out;               // bf16 [M, N]
+  int M, N, K, rank_pad;
+};
+int launch_gemm_nvfp4(const NvFp4Args& a, cudaStream_t st);
 
 struct W4A4Args {
   const void* a_codes;     // u8 [M, K/2] packed INT4 (a_packed) or u8 [M, K] operand form

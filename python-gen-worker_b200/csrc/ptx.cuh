@@ -101,6 +101,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uin
         "r"(x), "r"(y) : "memory");
 }
 
+// Untiled bulk copy global -> shared (both 16-byte aligned, bytes % 16 == 0).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Generic-proxy smem writes -> visible to the async proxy (tcgen05 / TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -150,6 +159,26 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+// D[tmem] (+)= (A · SFA) (B · SFB)^T, kind::mxf4nvf4 with 16-element blocks:
+// A and B packed e2m1 in shared memory, e4m3 block scales in TMEM.
+__device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem),
+        "r"(sfb_tmem) : "memory");
+}
+
+// Shared memory (32 rows x 16 bytes, no swizzle) -> TMEM, replicated into
+// all four 32-lane quarters: one 128 x 4 tile of block scales in the cuBLAS
+// blocked layout lands as lane r % 32 (every quarter), column r / 32, byte c.
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
 }
 
 // Arrive on `bar` once all previously issued tcgen05.mma of this thread finish.
@@ -235,6 +264,25 @@ __device__ __forceinline__ uint64_t sdesc_k128(uint32_t saddr) {
   d |= (uint64_t)(1024u >> 4) << 32;
   d |= (uint64_t)1 << 46;
   d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Block-scaled instruction descriptor for kind::mxf4nvf4: A/B format E2M1
+// (1) at [7,10) / [10,13), N>>3 at [17,23), scale format UE4M3 (0) at [23],
+// M>>4 at [24,29), scale-factor byte ids 0, dense K = 64.
+__host__ __device__ constexpr uint32_t idesc_mxf4(int M, int N) {
+  return (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Descriptor of a no-swizzle K-major operand whose 8-row x 16-byte core
+// matrices are stored contiguously (SBO = 128 B); `lbo` = byte distance to
+// the next 16-byte K slice.
+__device__ __forceinline__ uint64_t sdesc_noswz(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)(128u >> 4) << 32;
+  d |= (uint64_t)1 << 46;
   return d;
 }
 

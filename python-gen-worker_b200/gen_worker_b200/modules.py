@@ -182,6 +182,125 @@ class W8A8Int8Linear(nn.Module):
                 f"bias={self.bias is not None}, gelu={self.gelu}, mode=int8-rowwise")
 
 
+LAYOUT_NVFP4 = "nvfp4-blocked"
+
+
+class SvdqNvfp4Linear(nn.Module):
+    """Drop-in for the reference's NVFP4 ``SvdqLinear`` (``src/gen_worker/
+    models/svdq_native.py:94-156``) with its buffer set as stored: ``weight``
+    u8 [N, K/2] (packed e2m1), ``weight_scale`` e4m3 [blocked numel] (cuBLAS
+    blocked layout), ``weight_scale_2`` f32 [1, N] or [1, 1], optional
+    ``smooth_factor`` [K], ``proj_down`` [K, r], ``proj_up`` [N, r], ``bias``.
+    Forward: the smoothing divide, per-tensor ``s2`` and NVFP4 activation
+    codes in two native launches, ``la = x · proj_down`` (bf16 on raw x), then
+    one block-scaled tcgen05 GEMM with ``s2 · weight_scale_2``, the low-rank
+    up-projection and the bias fused."""
+    _cozy_svdq_linear = True
+    layout = LAYOUT_NVFP4
+
+    def __init__(self, in_features: int, out_features: int, *, rank: int, bias: bool,
+                 per_channel_scale: bool = False, smooth: bool = True,
+                 compute_dtype: Any = torch.bfloat16, device: Any = None) -> None:
+        super().__init__()
+        if in_features % 256 or out_features % 128:
+            raise SvdqB200LayoutError(
+                f"SvdqNvfp4Linear dims [{out_features}, {in_features}] break the tile "
+                f"alignment (in%256, out%128)")
+        if rank > 64:
+            raise SvdqB200LayoutError(f"low-rank rank {rank} > 64 is not supported")
+        self.in_features = int(in_features)
+        self.out_features = int(out_features)
+        self.rank = int(rank)
+        self.compute_dtype = compute_dtype
+        dev = device or torch.device("meta")
+        self.register_buffer("weight", torch.empty(out_features, in_features // 2,
+                                                   dtype=torch.uint8, device=dev))
+        self.register_buffer("weight_scale", torch.empty(
+            ops.nvfp4_blocked_numel(out_features, in_features), dtype=torch.float8_e4m3fn,
+            device=dev))
+        self.register_buffer("weight_scale_2", torch.empty(
+            1, out_features if per_channel_scale else 1, dtype=torch.float32, device=dev))
+        if smooth:
+            self.register_buffer("smooth_factor", torch.empty(in_features, dtype=compute_dtype,
+                                                              device=dev))
+        else:
+            self.smooth_factor = None
+        if self.rank:
+            self.register_buffer("proj_down", torch.empty(in_features, self.rank,
+                                                          dtype=compute_dtype, device=dev))
+            self.register_buffer("proj_up", torch.empty(out_features, self.rank,
+                                                        dtype=compute_dtype, device=dev))
+        else:
+            self.proj_down = None
+            self.proj_up = None
+        if bias:
+            self.bias: Optional[nn.Parameter] = nn.Parameter(
+                torch.empty(out_features, dtype=compute_dtype, device=dev), requires_grad=False)
+        else:
+            self.bias = None
+        self._up_pad: Optional[torch.Tensor] = None
+
+    def _apply(self, fn, recurse=True):
+        self._up_pad = None
+        return super()._apply(fn, recurse)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        x2 = x.reshape(-1, self.in_features)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        codes, sblk, work = ops.nvfp4_quant(x2, self.smooth_factor)
+        la = up = None
+        if self.rank:
+            rp = ops.rank_pad_of(self.rank)
+            if self._up_pad is None:
+                up_pad = torch.zeros(self.out_features, rp, dtype=torch.bfloat16,
+                                     device=self.proj_up.device)
+                up_pad[:, :self.rank] = self.proj_up.to(torch.bfloat16)
+                self._up_pad = up_pad
+            up = self._up_pad
+            la = torch.zeros(x2.shape[0], rp, dtype=torch.bfloat16, device=x2.device)
+            la[:, :self.rank] = x2 @ self.proj_down.to(x2.dtype)
+        y = ops.nvfp4_gemm(codes, sblk, work, self.weight, self.weight_scale,
+                           self.weight_scale_2, la, up,
+                           self.bias.detach() if self.bias is not None else None)
+        return y.reshape(*shape[:-1], self.out_features)
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, "
+                f"rank={self.rank}, bias={self.bias is not None}, "
+                f"smooth={self.smooth_factor is not None}, layout={self.layout}")
+
+
+def build_svdq_nvfp4_linear(buf: Dict[str, Any], *, device: Any = None) -> SvdqNvfp4Linear:
+    """From the reference's NVFP4 ``SvdqBuffers`` (``svdq_layout.py:66-84``)."""
+    w = buf["weight"]
+    n, k2 = w.shape
+    down = buf.get("proj_down")
+    rank = 0 if down is None else int(down.shape[1])
+    ws2 = buf["weight_scale_2"].float().reshape(1, -1)
+    mod = SvdqNvfp4Linear(k2 * 2, n, rank=rank, bias=buf.get("bias") is not None,
+                          per_channel_scale=ws2.shape[1] > 1,
+                          smooth=buf.get("smooth_factor") is not None,
+                          device=torch.device("cpu"))
+    dev = device or w.device
+    mod.weight = w.contiguous().to(dev)
+    wsc = buf["weight_scale"]
+    if wsc.dtype == torch.uint8:
+        wsc = wsc.view(torch.float8_e4m3fn)
+    mod.weight_scale = wsc.reshape(-1).contiguous().to(dev)
+    mod.weight_scale_2 = ws2.contiguous().to(dev)
+    if mod.smooth_factor is not None:
+        mod.smooth_factor = buf["smooth_factor"].to(torch.bfloat16).reshape(-1).contiguous().to(dev)
+    if rank:
+        mod.proj_down = down.to(torch.bfloat16).contiguous().to(dev)
+        mod.proj_up = buf["proj_up"].to(torch.bfloat16).contiguous().to(dev)
+    if mod.bias is not None:
+        mod.bias = nn.Parameter(buf["bias"].detach().to(torch.bfloat16).reshape(-1).to(dev),
+                                requires_grad=False)
+    return mod
+
+
 class Fp8RowwiseLinear(nn.Module):
     """Drop-in for the reference's ``Fp8ScaledLinear`` in rowwise mode
     (``src/gen_worker/models/w8a8.py:359-381``): buffers ``weight``

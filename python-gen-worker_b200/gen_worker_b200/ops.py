@@ -322,6 +322,83 @@ def _(q, scale, w_q, w_scale, bias, gelu):
     return q.new_empty(q.shape[0], w_q.shape[0], dtype=torch.bfloat16)
 
 
+# ---------------------------------------------------------------- NVFP4
+def nvfp4_blocked_numel(rows: int, k: int) -> int:
+    """Bytes of the cuBLAS blocked e4m3 scale layout for [rows, k/16] scales
+    (``blocked_scale_numel``, ``nvfp4_quant.py:87-89``)."""
+    return ((rows + 127) // 128) * 128 * ((k // 16 + 3) // 4) * 4
+
+
+@torch.library.custom_op("gwb200::nvfp4_quant", mutates_args=())
+def nvfp4_quant(x2: torch.Tensor, smooth: Optional[torch.Tensor]
+                ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """The reference's NVFP4 activation chain (smoothing divide, per-tensor
+    ``s2``, ``quantize_activation``): x2 bf16 [M, K] -> (codes u8 [M, K/2],
+    blocked e4m3 scale bytes u8, work f32 [2] with ``work[1] = s2``)."""
+    _need(x2, "x2", torch.bfloat16, 2)
+    _need(smooth, "smooth", torch.bfloat16, 1)
+    m, k = x2.shape
+    codes = torch.empty(m, k // 2, dtype=torch.uint8, device=x2.device)
+    sblk = torch.zeros(nvfp4_blocked_numel(m, k), dtype=torch.uint8, device=x2.device)
+    work = torch.empty(2, dtype=torch.float32, device=x2.device)
+    lib = native.require()
+    native.check(lib.gwb_nvfp4_quant(x2.data_ptr(), _ptr(smooth), m, k, codes.data_ptr(),
+                                     sblk.data_ptr(), work.data_ptr(), _stream()), "nvfp4_quant")
+    return codes, sblk, work
+
+
+@nvfp4_quant.register_fake
+def _(x2, smooth):
+    m, k = x2.shape
+    return (x2.new_empty(m, k // 2, dtype=torch.uint8),
+            x2.new_empty(nvfp4_blocked_numel(m, k), dtype=torch.uint8),
+            x2.new_empty(2, dtype=torch.float32))
+
+
+@torch.library.custom_op("gwb200::nvfp4_gemm", mutates_args=())
+def nvfp4_gemm(codes: torch.Tensor, sblk: torch.Tensor, work: torch.Tensor, w_codes: torch.Tensor,
+               w_sblk: torch.Tensor, w_scale_2: torch.Tensor, la: Optional[torch.Tensor],
+               proj_up: Optional[torch.Tensor], bias: Optional[torch.Tensor]) -> torch.Tensor:
+    """Block-scaled NVFP4 GEMM + ``s2 · weight_scale_2`` + low-rank + bias
+    -> bf16 [M, N] (``_gemm_w4a4`` and the rest of the NVFP4
+    ``SvdqLinear.forward``, ``svdq_native.py:148-155``)."""
+    _need(codes, "codes", torch.uint8, 2)
+    _need(w_codes, "w_codes", torch.uint8, 2)
+    _need(work, "work", torch.float32, 1)
+    _need(bias, "bias", torch.bfloat16, 1)
+    if sblk.dtype == torch.float8_e4m3fn:
+        sblk = sblk.view(torch.uint8)
+    if w_sblk.dtype == torch.float8_e4m3fn:
+        w_sblk = w_sblk.view(torch.uint8)
+    m, k = codes.shape[0], codes.shape[1] * 2
+    n = w_codes.shape[0]
+    if int(w_codes.shape[1]) * 2 != k:
+        raise SvdqB200Error(f"w_codes K {w_codes.shape[1] * 2} != activation K {k}")
+    if w_sblk.numel() != nvfp4_blocked_numel(n, k) or sblk.numel() != nvfp4_blocked_numel(m, k):
+        raise SvdqB200Error("blocked scale buffers do not match the operand shapes")
+    ws2 = w_scale_2.float().reshape(-1).contiguous()
+    if ws2.numel() not in (1, n):
+        raise SvdqB200Error(f"weight_scale_2 has {ws2.numel()} entries (want 1 or {n})")
+    rp = 0
+    if la is not None and proj_up is not None and la.shape[1] > 0:
+        _need(la, "la", torch.bfloat16, 2)
+        _need(proj_up, "proj_up", torch.bfloat16, 2)
+        rp = int(la.shape[1])
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=codes.device)
+    lib = native.require()
+    native.check(lib.gwb_nvfp4_gemm(codes.data_ptr(), sblk.data_ptr(), work.data_ptr(),
+                                    w_codes.data_ptr(), w_sblk.data_ptr(), ws2.data_ptr(),
+                                    int(ws2.numel() == n and n > 1), _ptr(la) if rp else None,
+                                    _ptr(proj_up) if rp else None, _ptr(bias), m, n, k, rp,
+                                    out.data_ptr(), _stream()), "nvfp4_gemm")
+    return out
+
+
+@nvfp4_gemm.register_fake
+def _(codes, sblk, work, w_codes, w_sblk, w_scale_2, la, proj_up, bias):
+    return codes.new_empty(codes.shape[0], w_codes.shape[0], dtype=torch.bfloat16)
+
+
 # ---------------------------------------------------------------- load-time repacks
 def prepare_w4a4_weights(w_scale: Optional[torch.Tensor], proj_down: Optional[torch.Tensor],
                          proj_up: Optional[torch.Tensor],

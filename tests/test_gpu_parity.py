@@ -12,7 +12,7 @@ import torch
 from oracle import svdq_oracle as O
 from gen_worker_b200 import ops, native
 from gen_worker_b200.modules import (build_fp8_rowwise_linear, build_svdq_int4_linear,
-                                     build_w8a8_int8_linear)
+                                     build_svdq_nvfp4_linear, build_w8a8_int8_linear)
 
 pytestmark = pytest.mark.gpu
 
@@ -213,6 +213,53 @@ def test_fp8_linear_matches_oracle(cuda_ready, m, k, n, gelu):
                                     "bias": L["bias"]}, gelu=gelu, device="cuda")
     y = mod(x.cuda()).cpu()
     want = O.fp8_rowwise_linear(x, L["w_q"], L["w_scale"], L["bias"], gelu=gelu)
+    assert O.rel_l2(y, want["y"]) <= REL_TOL
+    assert O.max_abs_beyond_bf16(y, want["y64"]) <= ABS_TOL
+    assert native.device_error() == 0
+
+
+# ---------------------------------------------------------------- NVFP4
+@pytest.mark.parametrize("m,k,smooth", [(128, 512, False), (333, 3072, True),
+                                        (1024, 12288, False), (64, 256, False)])
+def test_nvfp4_quant_bit_exact(cuda_ready, m, k, smooth):
+    """Codes, blocked e4m3 scales and s2 bit-identical to the oracle's
+    restatement of quantize_activation_torch (pinned to the reference by the
+    golden fixture); the shapes are the reference's own identity probes
+    (nvfp4_quant.py:21) plus the fixture's."""
+    if (m, k) == (64, 256):
+        x = torch.load(Path(__file__).parent / "golden" / "reference_golden.pt")["nvfp4_x"]
+    else:
+        x = O.synth_activation(m, k, seed=m + k)
+    sm = (torch.rand(k, generator=torch.Generator().manual_seed(k)) + 0.5).to(torch.bfloat16) \
+        if smooth else None
+    codes, sblk, work = ops.nvfp4_quant(x.cuda(), None if sm is None else sm.cuda())
+    xs = O.smooth_bf16(x, sm)
+    s2 = O.nvfp4_s2(xs)
+    want_codes, want_blk = O.quant_nvfp4(xs, s2)
+    assert torch.equal(work.cpu()[1:2], s2.reshape(1))
+    assert torch.equal(codes.cpu(), want_codes)
+    assert torch.equal(sblk.cpu(), want_blk)
+
+
+@pytest.mark.parametrize("m,k,n,rank,per_channel", [(128, 256, 128, 0, False),
+                                                    (300, 3072, 256, 32, False),
+                                                    (512, 1024, 384, 32, True)])
+def test_nvfp4_linear_matches_oracle(cuda_ready, m, k, n, rank, per_channel):
+    gen = torch.Generator().manual_seed(m + n)
+    x = O.synth_activation(m, k, seed=7 * m)
+    w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16)
+    smooth = (torch.rand(k, generator=gen) + 0.5).to(torch.bfloat16)
+    packed, blocked, ws2 = O.quant_nvfp4_weight(w.float() * smooth.float())
+    if per_channel:
+        ws2 = ws2.reshape(1, 1) * (torch.rand(1, n, generator=gen) + 0.5)
+    down = (torch.randn(k, rank, generator=gen) * 0.02).to(torch.bfloat16) if rank else None
+    up = (torch.randn(n, rank, generator=gen) * 0.02).to(torch.bfloat16) if rank else None
+    bias = (torch.randn(n, generator=gen) * 0.02).to(torch.bfloat16)
+    mod = build_svdq_nvfp4_linear({"weight": packed, "weight_scale": blocked,
+                                   "weight_scale_2": ws2, "smooth_factor": smooth,
+                                   "proj_down": down, "proj_up": up, "bias": bias}, device="cuda")
+    y = mod(x.cuda()).cpu()
+    want = O.svdq_nvfp4_linear(x, smooth, packed, blocked, ws2, down, up, bias)
     assert O.rel_l2(y, want["y"]) <= REL_TOL
     assert O.max_abs_beyond_bf16(y, want["y64"]) <= ABS_TOL
     assert native.device_error() == 0

@@ -52,21 +52,17 @@ def test_fp8_rowwise_quantiser_matches_reference_quant_src():
     assert int((GOLD["fp8_q"][11] & 0x78 == 0).sum()) > 100   # subnormal codes exercised
 
 
-def test_quantiser_structure_reproduces_reference_nvfp4():
-    """Restating quantize_activation_torch (nvfp4_quant.py:92-103) with the
-    oracle's ordering (amax -> scale rounded to storage dtype -> divide by the
-    rounded scale -> code) reproduces the reference bit for bit."""
+def test_nvfp4_quantiser_matches_reference_quantize_activation_torch():
+    """quant_nvfp4 restates quantize_activation_torch (nvfp4_quant.py:92-103)
+    with cast_e2m1's tie rule and the cuBLAS blocked scale layout: packed
+    codes and blocked scales bit for bit."""
     x, s2 = GOLD["nvfp4_x"], GOLD["nvfp4_s2"]
-    xb = x.float().reshape(-1, x.shape[1] // 16, 16)
-    sa = (xb.abs().amax(-1) / (6.0 * s2)).clamp(min=2.0 ** -9, max=448.0).to(torch.float8_e4m3fn)
-    q = xb / (sa.float().unsqueeze(-1) * s2)
-    bounds = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0])
-    a = q.abs()
-    code = torch.searchsorted(bounds, a.contiguous(), out_int32=True).to(torch.uint8)
-    tie = ((a == 0.75) | (a == 1.75) | (a == 2.5)).to(torch.uint8)
-    codes = (((q < 0).to(torch.uint8) << 3) + code + tie).reshape(x.shape)
-    packed = ((codes[..., 1::2] << 4) | codes[..., 0::2])
+    packed, blocked = O.quant_nvfp4(x, s2)
     assert torch.equal(packed, GOLD["nvfp4_q"])
+    assert torch.equal(blocked, GOLD["nvfp4_sa"].view(torch.uint8))
+    m, k = x.shape
+    flat = O.from_blocked_scales(blocked, m, k // 16)
+    assert torch.equal(O.to_blocked_scales(flat), blocked)
 
 
 @pytest.mark.parametrize("m,k", [(1, 64), (7, 128), (33, 3072)])
