@@ -27,6 +27,7 @@ import statistics
 import subprocess
 import sys
 import time
+from typing import Optional
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
@@ -273,7 +274,38 @@ CASES = {
     "cfg2": [("w4a4", 4608, 3072, 9216, 32, False), ("w4a4", 4608, 3072, 3072, 32, False),
              ("w4a4", 4608, 3072, 12288, 32, True), ("w4a4", 4608, 12288, 3072, 32, False)],
     "cfg3": [("w4a4", 4608, 3072, 3072, 48, False)],
+    # the same shapes in the reference's own SVDQuant format (NVFP4)
+    "cfg2nvfp4": [("nvfp4", 4608, 3072, 9216, 32, False), ("nvfp4", 4608, 3072, 3072, 32, False),
+                  ("nvfp4", 4608, 3072, 12288, 32, False),
+                  ("nvfp4", 4608, 12288, 3072, 32, False)],
+    "cfg3nvfp4": [("nvfp4", 4608, 3072, 3072, 48, False)],
 }
+
+
+def _scaled_mm_fp4_ms(codes, sblk, w_codes, w_sblk, steps: int) -> Optional[float]:
+    """The reference's own NVFP4 GEMM call (``_gemm_w4a4``: ``torch._scaled_mm``
+    on float4_e2m1fn_x2 with blocked scales, cuBLASLt) on the same operands,
+    for context; None when this torch build cannot run it."""
+    fp4 = getattr(torch, "float4_e2m1fn_x2", None)
+    if fp4 is None:
+        return None
+    try:
+        def call():
+            return torch._scaled_mm(codes.view(fp4), w_codes.view(fp4).t(),
+                                    scale_a=sblk.view(torch.float8_e4m3fn),
+                                    scale_b=w_sblk.view(torch.float8_e4m3fn),
+                                    out_dtype=torch.bfloat16)
+        call()
+        torch.cuda.synchronize()
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record()
+        for _ in range(steps):
+            call()
+        e_.record()
+        torch.cuda.synchronize()
+        return s_.elapsed_time(e_) / steps
+    except Exception:  # noqa: BLE001 - context figure only
+        return None
 
 
 def run_case(name: str, steps: int, warmup: int) -> dict:
@@ -281,8 +313,9 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
     launches) with CUDA events on the current stream; inputs are resident in
     HBM and a 256 MB buffer is overwritten between iterations to flush L2."""
     from gen_worker_b200.modules import (build_fp8_rowwise_linear, build_svdq_int4_linear,
-                                         build_w8a8_int8_linear, quantize_fp8_rows,
-                                         quantize_int4_rows, quantize_int8_rows)
+                                         build_svdq_nvfp4_linear, build_w8a8_int8_linear,
+                                         quantize_fp8_rows, quantize_int4_rows,
+                                         quantize_int8_rows)
     from gen_worker_b200 import ops
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
@@ -306,6 +339,16 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
             q, s_ = quantize_fp8_rows(w)
             mod = build_fp8_rowwise_linear({"weight": q, "weight_scale": s_, "bias": b},
                                            gelu=gelu, device=dev)
+        elif kind == "nvfp4":
+            sm = (x.abs().amax(0).clamp(min=1e-5).sqrt() / w.abs().amax(0).clamp(min=1e-5).sqrt()
+                  ).to(torch.bfloat16)
+            wc, wsb, wwork = ops.nvfp4_quant((w * sm.float()).to(torch.bfloat16), None)
+            mod = build_svdq_nvfp4_linear(
+                {"weight": wc, "weight_scale": wsb, "weight_scale_2": wwork[1:2].clone(),
+                 "smooth_factor": sm,
+                 "proj_down": (torch.randn(k, r, generator=g, device=dev) * 0.02).to(torch.bfloat16),
+                 "proj_up": (torch.randn(n, r, generator=g, device=dev) * 0.02).to(torch.bfloat16),
+                 "bias": b}, device=dev)
         else:
             q, s_ = quantize_int8_rows(w)
             mod = build_w8a8_int8_linear({"weight": q, "weight_scale": s_, "bias": b},
@@ -323,6 +366,16 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
                 e[1].record()
                 ops.svdq_w4a4_gemm(c, a, p["w_q8"], p["w_scale_k8"], la, p["proj_up_pad"],
                                    mod.bias.detach(), gelu)
+            elif kind == "nvfp4":
+                c, sb_, wk = ops.nvfp4_quant(xb, mod.smooth_factor)
+                rp = ops.rank_pad_of(mod.rank)
+                la = torch.zeros(m, rp, dtype=torch.bfloat16, device=dev)
+                la[:, :mod.rank] = xb @ mod.proj_down
+                upp = torch.zeros(n, rp, dtype=torch.bfloat16, device=dev)
+                upp[:, :mod.rank] = mod.proj_up
+                e[1].record()
+                ops.nvfp4_gemm(c, sb_, wk, mod.weight, mod.weight_scale, mod.weight_scale_2,
+                               la, upp, mod.bias.detach())
             elif kind == "fp8":
                 q, s_ = ops.fp8_quant(xb)
                 e[1].record()
@@ -338,13 +391,19 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
             if it >= warmup:
                 tot += e[0].elapsed_time(e[2]) / steps
                 gemm += e[1].elapsed_time(e[2]) / steps
+        lib_ms = None
+        if kind == "nvfp4":
+            c, sb_, _ = ops.nvfp4_quant(xb, mod.smooth_factor)
+            lib_ms = _scaled_mm_fp4_ms(c, sb_, mod.weight, mod.weight_scale, steps)
         ops_ = 2.0 * m * n * k
         act_bytes = m * k * 2 + (m * k // 2 + m * k // 4 + m * r * 2 if kind == "w4a4"
                                  else m * k + m * 4)
         rows.append({"kind": kind, "M": m, "K": k, "N": n, "rank": r, "gelu": gelu,
                      "ms": tot, "gemm_ms": gemm, "act_ms": tot - gemm,
                      "tops": ops_ / (tot / 1e3) / 1e12, "gemm_tops": ops_ / (gemm / 1e3) / 1e12,
-                     "act_gbs": act_bytes / ((tot - gemm) / 1e3) / 1e9})
+                     "act_gbs": act_bytes / ((tot - gemm) / 1e3) / 1e9,
+                     "cublaslt_scaled_mm_ms": lib_ms,
+                     "cublaslt_scaled_mm_tops": (ops_ / (lib_ms / 1e3) / 1e12) if lib_ms else None})
     total_ms = sum(r_["ms"] for r_ in rows)
     total_ops = sum(2.0 * r_["M"] * r_["N"] * r_["K"] for r_ in rows)
     tops = total_ops / (total_ms / 1e3) / 1e12
