@@ -185,8 +185,11 @@ int gwb_nvfp4_quant(const void* x, const void* smooth, int64_t M, int64_t K, voi
  * * s2 * w_scale_2[n] + la·proj_up^T + bias -> bf16 [M, N]. w_codes / w_sblk
  * / w_scale_2 are the reference module's `weight` / `weight_scale` /
  * `weight_scale_2` buffers as stored (w_scale_2 per channel [N] when
- * ws2_per_channel, else [1]); la = bf16(x · proj_down) [M, rank_pad] on raw
- * x. K % 256 == 0, N % 128 == 0. */
+ * ws2_per_channel, else [1]). The low-rank up-projection comes divided by the
+ * second-level scales, so the branch shares the accumulator: la =
+ * bf16(x · proj_down) [M, rank_pad] on raw x (as the reference), proj_up =
+ * bf16(proj_up / (w_scale_2[n] * s2)) [N, rank_pad]. K % 256 == 0,
+ * N % 256 == 0. */
 int gwb_nvfp4_gemm(const void* a_codes, const void* a_sblk, const float* a_work,
                    const void* w_codes, const void* w_sblk, const float* w_scale_2,
                    int ws2_per_channel, const void* la, const void* proj_up, const void* bias,

@@ -634,24 +634,28 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 // Activations and weights are packed e2m1 codes with e4m3 scales per
 // 16-element block in the cuBLAS blocked layout (exactly the reference's
 // `weight` / `weight_scale` buffers and its quantiser output); the tensor
-// core applies the block scales itself. Per k-block of 256 elements: TMA
-// brings the 128 x 128-byte A and B tiles (SWIZZLE_128B) and two 2 KB
-// bulk copies bring the four 128 x 4 scale tiles of A and of B; the MMA
-// thread copies each scale tile into TMEM (tcgen05.cp) and issues four
-// K = 64 MMAs. Epilogue: y = acc * s2 * weight_scale_2[n] + la·proj_upᵀ +
-// bias (the low-rank product accumulates in its own TMEM columns).
+// core applies the block scales itself. Tile 128 x 256, persistent. Per
+// k-block of 256 codes: TMA brings the 128 x 128-byte A and 256 x 128-byte B
+// tiles (SWIZZLE_128B) and three 2 KB bulk copies bring the blocked scale
+// tiles (A rows, B rows 0-127, B rows 128-255); the MMA thread copies each
+// 128 x 4 scale tile into TMEM (tcgen05.cp) and issues four K = 64 MMAs.
+// The low-rank product is issued first into the same accumulator with
+// operands pre-divided by the second-level scales (la / s2, proj_up /
+// weight_scale_2), so the epilogue is y = acc * s2 * weight_scale_2[n] + bias.
 namespace nv4 {
-constexpr int BN = 128;
+constexpr int BN = 256;
 constexpr int KB_BYTES = 128;                 // packed bytes of one k-block row (256 codes)
-constexpr int STAGES = 5;
+constexpr int STAGES = 4;
 constexpr int A_BYTES = kBM * KB_BYTES;       // 16 KB
-constexpr int B_BYTES = BN * KB_BYTES;        // 16 KB
-constexpr int SF_BYTES = 4 * 512;             // four 128 x 4 blocked scale tiles
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES + 2 * SF_BYTES;    // 36 KB
+constexpr int B_BYTES = BN * KB_BYTES;        // 32 KB
+constexpr int SFA_BYTES = 4 * 512;            // four 128 x 4 blocked scale tiles
+constexpr int SFB_BYTES = 2 * SFA_BYTES;      // two 128-row groups
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;   // 54 KB
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int TMEM_COLS = 512;
-constexpr int ACC_COL = 0, LR_COL = 128, SF_COL = 256;
-constexpr int SF_SLOTS = 4;                   // 32 columns each: SFA 16, SFB 16
+constexpr int ACC_COL = 0, SF_COL = 256;
+constexpr int SF_SLOT = 48;                   // SFA 16 columns + SFB 32 columns
+constexpr int SF_SLOTS = 4;
 constexpr int THREADS = 384;                  // warp 0 TMA, 1 MMA, 4-11 epilogue
 constexpr int EPI0 = 4;
 constexpr int EPI_WARPS = 8;
@@ -659,6 +663,7 @@ constexpr int EC = BN / 2;
 }  // namespace nv4
 
 static_assert(nv4::SMEM_BYTES <= 232448, "NVFP4 shared memory exceeds 227 KB");
+static_assert(nv4::SF_COL + nv4::SF_SLOTS * nv4::SF_SLOT <= nv4::TMEM_COLS, "TMEM overflow");
 
 __global__ void __launch_bounds__(nv4::THREADS, 1)
 gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -702,7 +707,7 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     if (warp == 0 && lane < 4) {
       // -------------------------------------------------------------- TMA
       // lane 0 A (and the low-rank operands), lane 1 B, lane 2 A scales,
-      // lane 3 B scales
+      // lane 3 the two groups of B scales
       const int pl = lane;
       int ui = 0;
       bool ok = true;
@@ -728,14 +733,19 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           if (pl == 0) mbar_arrive_expect_tx(&full[u], STAGE_BYTES);
           __syncwarp(0xFu);
           uint8_t* us = smem + u * STAGE_BYTES;
-          if (pl == 0) tma_load_2d(us, &tmA, &full[u], kb * KB_BYTES, m0);
-          else if (pl == 1) tma_load_2d(us + A_BYTES, &tmB, &full[u], kb * KB_BYTES, n0);
-          else if (pl == 2)
-            bulk_load(us + A_BYTES + B_BYTES, a_sblk + ((size_t)mt * ncb + 4 * kb) * 512,
-                      SF_BYTES, &full[u]);
-          else
-            bulk_load(us + A_BYTES + B_BYTES + SF_BYTES,
-                      w_sblk + ((size_t)(n0 / 128) * ncb + 4 * kb) * 512, SF_BYTES, &full[u]);
+          uint8_t* sfa = us + A_BYTES + B_BYTES;
+          if (pl == 0) {
+            tma_load_2d(us, &tmA, &full[u], kb * KB_BYTES, m0);
+          } else if (pl == 1) {
+            tma_load_2d(us + A_BYTES, &tmB, &full[u], kb * KB_BYTES, n0);
+          } else if (pl == 2) {
+            bulk_load(sfa, a_sblk + ((size_t)mt * ncb + 4 * kb) * 512, SFA_BYTES, &full[u]);
+          } else {
+            const size_t rb = (size_t)(n0 / 128);
+            bulk_load(sfa + SFA_BYTES, w_sblk + (rb * ncb + 4 * kb) * 512, SFA_BYTES, &full[u]);
+            bulk_load(sfa + 2 * SFA_BYTES, w_sblk + ((rb + 1) * ncb + 4 * kb) * 512, SFA_BYTES,
+                      &full[u]);
+          }
         }
       }
     } else if (warp == 1 && lane == 0) {
@@ -748,12 +758,13 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         if (!mbar_wait(acc_empty, (lt & 1) ^ 1, GWB_ERR_TIMEOUT_MMA)) break;
         tc_fence_after();
         if (has_lr) {
+          // acc <- (la / s2) · (proj_up / weight_scale_2)ᵀ
           const int u = ui % STAGES;
           if (!mbar_wait(&full[u], (ui / STAGES) & 1, GWB_ERR_TIMEOUT_MMA)) break;
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + u * STAGE_BYTES), b_base = a_base + A_BYTES;
           for (int k = 0; k < rank_pad / 16; ++k)
-            mma_f16(tmem + LR_COL, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k),
+            mma_f16(tmem + ACC_COL, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k),
                     idesc_lr, k > 0 ? 1u : 0u);
           mma_commit(&empty[u]);
           ++ui;
@@ -764,17 +775,21 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + u * STAGE_BYTES);
           const uint32_t b_base = a_base + A_BYTES;
-          const uint32_t sfa_s = b_base + B_BYTES, sfb_s = sfa_s + SF_BYTES;
-          const uint32_t sfa_t = tmem + SF_COL + (ui % SF_SLOTS) * 32, sfb_t = sfa_t + 16;
+          const uint32_t sfa_s = b_base + B_BYTES, sfb_s = sfa_s + SFA_BYTES;
+          const uint32_t sfa_t = tmem + SF_COL + (ui % SF_SLOTS) * SF_SLOT, sfb_t = sfa_t + 16;
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
+            // per K = 64 step: A scales 4 columns, B scales 8 columns (rows
+            // n / 32: the first 128-row group in 0-3, the second in 4-7)
             tmem_cp_32x128b_x4(sfa_t + 4 * ks, sdesc_noswz(sfa_s + 512 * ks, 0));
-            tmem_cp_32x128b_x4(sfb_t + 4 * ks, sdesc_noswz(sfb_s + 512 * ks, 0));
+            tmem_cp_32x128b_x4(sfb_t + 8 * ks, sdesc_noswz(sfb_s + 512 * ks, 0));
+            tmem_cp_32x128b_x4(sfb_t + 8 * ks + 4, sdesc_noswz(sfb_s + SFA_BYTES + 512 * ks, 0));
           }
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
             mma_mxf4(tmem + ACC_COL, sdesc_k128(a_base + 32 * ks), sdesc_k128(b_base + 32 * ks),
-                     idesc, sfa_t + 4 * ks, sfb_t + 4 * ks, (kb > 0 || ks > 0) ? 1u : 0u);
+                     idesc, sfa_t + 4 * ks, sfb_t + 8 * ks,
+                     (has_lr || kb > 0 || ks > 0) ? 1u : 0u);
           mma_commit(&empty[u]);
         }
         if (ok) mma_commit(acc_full);
@@ -791,14 +806,10 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       const int m0 = (tile / tiles_n) * kBM, n0 = (tile % tiles_n) * BN;
       if (!mbar_wait(acc_full, lt & 1, GWB_ERR_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
-      uint32_t v[EC], lr[EC];
-      const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) + cb;
+      uint32_t v[EC];
+      const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) + ACC_COL + cb;
 #pragma unroll
-      for (int c = 0; c < EC; c += 32) tmem_ld32(base + ACC_COL + c, v + c);
-      if (has_lr) {
-#pragma unroll
-        for (int c = 0; c < EC; c += 32) tmem_ld32(base + LR_COL + c, lr + c);
-      }
+      for (int c = 0; c < EC; c += 32) tmem_ld32(base + c, v + c);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
@@ -813,7 +824,6 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         for (int j = 0; j < 8; ++j) {
           const float w2 = ws2_per_channel ? __ldg(w_scale_2 + n0 + cb + c + j) : __ldg(w_scale_2);
           f[j] = __uint_as_float(v[c + j]) * (s2 * w2);
-          if (has_lr) f[j] += __uint_as_float(lr[c + j]);
         }
         if (bias != nullptr) {
           const uint4 bw = __ldg(reinterpret_cast<const uint4*>(bias + n0 + cb + c));

@@ -192,9 +192,10 @@ class SvdqNvfp4Linear(nn.Module):
     blocked layout), ``weight_scale_2`` f32 [1, N] or [1, 1], optional
     ``smooth_factor`` [K], ``proj_down`` [K, r], ``proj_up`` [N, r], ``bias``.
     Forward: the smoothing divide, per-tensor ``s2`` and NVFP4 activation
-    codes in two native launches, ``la = x · proj_down`` (bf16 on raw x), then
-    one block-scaled tcgen05 GEMM with ``s2 · weight_scale_2``, the low-rank
-    up-projection and the bias fused."""
+    codes in two native launches, ``la = x · proj_down`` (bf16 on raw x, as
+    the reference), then one block-scaled tcgen05 GEMM whose accumulator
+    starts from the low-rank product (up-projection divided by
+    ``weight_scale_2 · s2``) and ends with ``· s2 · weight_scale_2 + bias``."""
     _cozy_svdq_linear = True
     layout = LAYOUT_NVFP4
 
@@ -202,10 +203,10 @@ class SvdqNvfp4Linear(nn.Module):
                  per_channel_scale: bool = False, smooth: bool = True,
                  compute_dtype: Any = torch.bfloat16, device: Any = None) -> None:
         super().__init__()
-        if in_features % 256 or out_features % 128:
+        if in_features % 256 or out_features % 256:
             raise SvdqB200LayoutError(
                 f"SvdqNvfp4Linear dims [{out_features}, {in_features}] break the tile "
-                f"alignment (in%256, out%128)")
+                f"alignment (in%256, out%256)")
         if rank > 64:
             raise SvdqB200LayoutError(f"low-rank rank {rank} > 64 is not supported")
         self.in_features = int(in_features)
@@ -252,15 +253,9 @@ class SvdqNvfp4Linear(nn.Module):
         codes, sblk, work = ops.nvfp4_quant(x2, self.smooth_factor)
         la = up = None
         if self.rank:
-            rp = ops.rank_pad_of(self.rank)
             if self._up_pad is None:
-                up_pad = torch.zeros(self.out_features, rp, dtype=torch.bfloat16,
-                                     device=self.proj_up.device)
-                up_pad[:, :self.rank] = self.proj_up.to(torch.bfloat16)
-                self._up_pad = up_pad
-            up = self._up_pad
-            la = torch.zeros(x2.shape[0], rp, dtype=torch.bfloat16, device=x2.device)
-            la[:, :self.rank] = x2 @ self.proj_down.to(x2.dtype)
+                self._up_pad = ops.nvfp4_up_over_ws2(self.proj_up, self.weight_scale_2)
+            la, up = ops.nvfp4_lowrank_operands(x2, self.proj_down, self._up_pad, work)
         y = ops.nvfp4_gemm(codes, sblk, work, self.weight, self.weight_scale,
                            self.weight_scale_2, la, up,
                            self.bias.detach() if self.bias is not None else None)

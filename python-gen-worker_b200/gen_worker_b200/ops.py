@@ -361,7 +361,9 @@ def nvfp4_gemm(codes: torch.Tensor, sblk: torch.Tensor, work: torch.Tensor, w_co
                proj_up: Optional[torch.Tensor], bias: Optional[torch.Tensor]) -> torch.Tensor:
     """Block-scaled NVFP4 GEMM + ``s2 · weight_scale_2`` + low-rank + bias
     -> bf16 [M, N] (``_gemm_w4a4`` and the rest of the NVFP4
-    ``SvdqLinear.forward``, ``svdq_native.py:148-155``)."""
+    ``SvdqLinear.forward``, ``svdq_native.py:148-155``). The low-rank
+    up-projection comes divided by the second-level scales
+    (:func:`nvfp4_lowrank_operands`)."""
     _need(codes, "codes", torch.uint8, 2)
     _need(w_codes, "w_codes", torch.uint8, 2)
     _need(work, "work", torch.float32, 1)
@@ -392,6 +394,28 @@ def nvfp4_gemm(codes: torch.Tensor, sblk: torch.Tensor, work: torch.Tensor, w_co
                                     _ptr(proj_up) if rp else None, _ptr(bias), m, n, k, rp,
                                     out.data_ptr(), _stream()), "nvfp4_gemm")
     return out
+
+
+def nvfp4_lowrank_operands(x2: torch.Tensor, proj_down: torch.Tensor, up_over_ws2: torch.Tensor,
+                           work: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Low-rank operands of :func:`nvfp4_gemm`: ``la = bf16(x2 · proj_down)``
+    on raw x exactly as the reference's bf16 matmul (``svdq_native.py:153``)
+    and the up-projection ``bf16(proj_up / (weight_scale_2[n] · s2))`` (the
+    branch then shares the main accumulator, which the epilogue multiplies by
+    ``s2 · weight_scale_2``); both padded to rank_pad columns.
+    ``up_over_ws2`` = fp32 ``proj_up / weight_scale_2`` (load time)."""
+    n, r = up_over_ws2.shape
+    rp = rank_pad_of(r)
+    la = torch.zeros(x2.shape[0], rp, dtype=torch.bfloat16, device=x2.device)
+    la[:, :r] = x2 @ proj_down.to(x2.dtype)
+    up = torch.zeros(n, rp, dtype=torch.bfloat16, device=x2.device)
+    up[:, :r] = (up_over_ws2 / work[1]).to(torch.bfloat16)
+    return la, up
+
+
+def nvfp4_up_over_ws2(proj_up: torch.Tensor, w_scale_2: torch.Tensor) -> torch.Tensor:
+    """Load-time fp32 ``proj_up / weight_scale_2[n]``."""
+    return (proj_up.float() / w_scale_2.float().reshape(-1, 1)).contiguous()
 
 
 @nvfp4_gemm.register_fake

@@ -241,9 +241,10 @@ def test_nvfp4_quant_bit_exact(cuda_ready, m, k, smooth):
     assert torch.equal(sblk.cpu(), want_blk)
 
 
-@pytest.mark.parametrize("m,k,n,rank,per_channel", [(128, 256, 128, 0, False),
+@pytest.mark.parametrize("m,k,n,rank,per_channel", [(128, 256, 256, 0, False),
                                                     (300, 3072, 256, 32, False),
-                                                    (512, 1024, 384, 32, True)])
+                                                    (512, 1024, 768, 32, True),
+                                                    (1000, 3072, 1024, 48, False)])
 def test_nvfp4_linear_matches_oracle(cuda_ready, m, k, n, rank, per_channel):
     gen = torch.Generator().manual_seed(m + n)
     x = O.synth_activation(m, k, seed=7 * m)
