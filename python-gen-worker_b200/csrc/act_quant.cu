@@ -172,8 +172,14 @@ act_int4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
         sm[2 * j] = bf_lo(sw[j]);
         sm[2 * j + 1] = bf_hi(sw[j]);
       }
+      // the 8 lanes of a segment (same c) need the same 16 reciprocals: lane
+      // (g, c) computes those of columns 2g and 2g + 1 and the others arrive
+      // by shuffle from lane 4 * (j / 2) + c
+      const uint32_t pair = __ldg(reinterpret_cast<const uint32_t*>(smooth + k0 + 2 * g));
+      const float mine[2] = {__frcp_rn(bf_lo(pair)), __frcp_rn(bf_hi(pair))};
 #pragma unroll
-      for (int j = 0; j < 16; ++j) rsm[j] = __frcp_rn(sm[j]);
+      for (int j = 0; j < 16; ++j)
+        rsm[j] = __shfl_sync(0xffffffffu, mine[j & 1], 4 * (j >> 1) + c);
     } else {
 #pragma unroll
       for (int j = 0; j < 16; ++j) { sm[j] = 1.f; rsm[j] = 1.f; }
