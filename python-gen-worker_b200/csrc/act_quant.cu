@@ -54,26 +54,45 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// Pairwise a / b given rb = RN(1/b) (the div_rn rule on f32x2 lanes; the
+// packed FMUL2 / FFMA2 round each lane exactly like their scalar forms).
+__device__ __forceinline__ float2 div2_rn(float2 a, float2 b, float2 rb) {
+  const float2 q = __fmul2_rn(a, rb);
+  const float2 r = __ffma2_rn(make_float2(-q.x, -q.y), b, a);
+  return __ffma2_rn(r, rb, q);
+}
+
+// sign-magnitude nibbles of clamp(rint(v/s), -7, 7) for a pair (see q4).
+__device__ __forceinline__ uint32_t q4x2(float2 v, float2 s, float2 rs) {
+  const float2 q = div2_rn(v, s, rs);
+  const float2 m = __fadd2_rn(make_float2(fminf(fabsf(q.x), 7.0f), fminf(fabsf(q.y), 7.0f)),
+                              make_float2(8388608.0f, 8388608.0f));
+  const uint32_t m0 = __float_as_uint(m.x) & 7u, m1 = __float_as_uint(m.y) & 7u;
+  return (m0 | ((q.x < 0.0f && m0 != 0u) ? 8u : 0u)) |
+         ((m1 | ((q.y < 0.0f && m1 != 0u) ? 8u : 0u)) << 4);
+}
+
 // Quantise 16 consecutive raw elements (8 bf16x2 words) of one row-group
 // segment: smoothing divide rounded to bf16, then the group's INT4 codes.
 // The 4 lanes of a quad hold the 64 elements of one group.
 __device__ __forceinline__ void quant_seg16(const uint32_t (&xw)[8], const float (&sm)[16],
                                             const float (&rsm)[16], bool has_smooth,
                                             uint32_t& lo, uint32_t& hi, __half& scale_out) {
-  float v[16];
+  float2 v[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    float a = bf_lo(xw[j]), b = bf_hi(xw[j]);
+    float2 p = make_float2(bf_lo(xw[j]), bf_hi(xw[j]));
     if (has_smooth) {
-      a = __bfloat162float(__float2bfloat16_rn(div_rn(a, sm[2 * j], rsm[2 * j])));
-      b = __bfloat162float(__float2bfloat16_rn(div_rn(b, sm[2 * j + 1], rsm[2 * j + 1])));
+      const float2 q = div2_rn(p, make_float2(sm[2 * j], sm[2 * j + 1]),
+                               make_float2(rsm[2 * j], rsm[2 * j + 1]));
+      const __nv_bfloat162 hb = __float22bfloat162_rn(q);
+      p = __bfloat1622float2(hb);
     }
-    v[2 * j] = a;
-    v[2 * j + 1] = b;
+    v[j] = p;
   }
   float amax = 0.f;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
+  for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fmaxf(fabsf(v[j].x), fabsf(v[j].y)));
   amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
   amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
   float s32 = __fdiv_rn(amax, 7.0f);
@@ -81,12 +100,13 @@ __device__ __forceinline__ void quant_seg16(const uint32_t (&xw)[8], const float
   const __half sh = __float2half_rn(s32);
   const float s = __half2float(sh);
   const float rs = __frcp_rn(s);
+  const float2 s2 = make_float2(s, s), rs2 = make_float2(rs, rs);
   lo = 0;
   hi = 0;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) lo |= q4(v[j], s, rs) << (4 * j);
+  for (int j = 0; j < 4; ++j) lo |= q4x2(v[j], s2, rs2) << (8 * j);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) hi |= q4(v[8 + j], s, rs) << (4 * j);
+  for (int j = 0; j < 4; ++j) hi |= q4x2(v[4 + j], s2, rs2) << (8 * j);
   scale_out = sh;
 }
 
