@@ -265,3 +265,43 @@ def test_nvfp4_linear_matches_oracle(cuda_ready, m, k, n, rank, per_channel):
     assert O.max_abs_beyond_bf16(y, want["y64"]) <= ABS_TOL
     assert native.device_error() == 0
 
+
+# ---------------------------------------------------------------- empty and full-size inputs
+def test_empty_inputs_give_empty_outputs(cuda_ready):
+    """M = 0 (an empty token batch) is a no-op on every lane."""
+    x, L = _layer_case(8, 256, 256, 16, seed=1)
+    mod = build_svdq_int4_linear({"weight": L["w_packed"], "weight_scale": L["w_scale"],
+                                  "smooth_factor": L["smooth"], "proj_down": L["proj_down"],
+                                  "proj_up": L["proj_up"], "bias": L["bias"]}, device="cuda")
+    assert mod(torch.empty(0, 256, dtype=torch.bfloat16, device="cuda")).shape == (0, 256)
+    W = O.synth_w8a8_layer(256, 256, seed=2)
+    m8 = build_w8a8_int8_linear({"weight": W["w_q"], "weight_scale": W["w_scale"],
+                                 "bias": W["bias"]}, device="cuda")
+    assert m8(torch.empty(0, 256, dtype=torch.bfloat16, device="cuda")).shape == (0, 256)
+    F = O.synth_fp8_layer(256, 256, seed=3)
+    mf = build_fp8_rowwise_linear({"weight": F["w_q"], "weight_scale": F["w_scale"],
+                                   "bias": F["bias"]}, device="cuda")
+    assert mf(torch.empty(0, 256, dtype=torch.bfloat16, device="cuda")).shape == (0, 256)
+    assert native.device_error() == 0
+
+
+@pytest.mark.parametrize("k,n", [(15360, 3072), (3072, 21504)])
+def test_w4a4_full_size_rows_match_oracle(cuda_ready, k, n):
+    """BASELINE config 4's widest linears at the full token count (M =
+    16896): rows are quantised and multiplied independently, so 48 sampled
+    output rows must equal the oracle run on those rows alone."""
+    m = 16896
+    gen = torch.Generator().manual_seed(k + n)
+    x = O.synth_activation(m, k, seed=k)
+    rows = torch.randperm(m, generator=gen)[:48].sort().values
+    L = O.synth_svdq_layer(k, n, 32, seed=n, x_calib=x[rows])
+    mod = build_svdq_int4_linear({"weight": L["w_packed"], "weight_scale": L["w_scale"],
+                                  "smooth_factor": L["smooth"], "proj_down": L["proj_down"],
+                                  "proj_up": L["proj_up"], "bias": L["bias"]}, device="cuda")
+    y = mod(x.cuda())[rows.cuda()].cpu()
+    want = O.svdq_int4_linear(x[rows], L["smooth"], L["w_packed"], L["w_scale"],
+                              L["proj_down"], L["proj_up"], L["bias"])
+    assert O.rel_l2(y, want["y"]) <= REL_TOL
+    assert O.max_abs_beyond_bf16(y, want["y64"]) <= ABS_TOL
+    assert native.device_error() == 0
+
