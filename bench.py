@@ -368,8 +368,8 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
                                    mod.bias.detach(), gelu)
             elif kind == "nvfp4":
                 c, sb_, wk = ops.nvfp4_quant(xb, mod.smooth_factor)
-                la, upp = ops.nvfp4_lowrank_operands(
-                    xb, mod.proj_down, ops.nvfp4_up_over_ws2(mod.proj_up, mod.weight_scale_2), wk)
+                la, upp = ops.nvfp4_lowrank_operands(xb, *ops.nvfp4_lowrank_prepare(
+                    mod.proj_down, mod.proj_up, mod.weight_scale_2), wk)
                 e[1].record()
                 ops.nvfp4_gemm(c, sb_, wk, mod.weight, mod.weight_scale, mod.weight_scale_2,
                                la, upp, mod.bias.detach())

@@ -173,9 +173,9 @@ int gwb_fp8_linear(const void* x, const void* w_q, const float* w_scale, const v
  * src/gen_worker/models/nvfp4_quant.py:92-103, 272-280) preceded by the
  * smoothing divide and the per-tensor `s2` of `SvdqLinear.forward`
  * (svdq_native.py:144-146): codes u8 [M, K/2] (element 2j in the low
- * nibble), sblk = blocked e4m3 scales (ceil(M/128)*128 * K/16 bytes; the
- * caller zero-fills it so the row padding matches the reference), work f32
- * [2] (work[1] = s2 on return). Bit-identical to the reference. K % 64 == 0. */
+ * nibble), sblk = blocked e4m3 scales (ceil(M/128)*128 * K/16 bytes, the
+ * padding rows zero as in the reference), work f32 [4 + K] scratch (16-byte aligned;
+ * work[1] = s2 on return). Bit-identical to the reference. K % 64 == 0. */
 int gwb_nvfp4_quant(const void* x, const void* smooth, int64_t M, int64_t K, void* codes,
                     void* sblk, float* work, void* stream);
 

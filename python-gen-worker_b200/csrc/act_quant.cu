@@ -431,6 +431,9 @@ act_fp8_kernel(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q,
 // src/gen_worker/models/nvfp4_quant.py:92-103), after the smoothing divide
 // and the per-tensor second-level scale of SvdqLinear.forward
 // (svdq_native.py:144-146).
+//   work f32 [4 + K] (16-byte aligned): [0] amax (fp32 bits), [1] s2,
+//   [4, 4 + K) = RN(1 / smooth) (16-byte aligned for float4 reads).
+//   nvfp4_rsmooth_kernel: the smoothing reciprocals, once per call.
 //   nvfp4_amax_kernel: amax |bf16(x / smooth)| over the whole tensor (fp32
 //     bits, atomicMax; the values are non-negative) into work[0].
 //   act_nvfp4_kernel: s2 = max(amax / 2688, 1e-12) (written to work[1]);
@@ -440,16 +443,26 @@ act_fp8_kernel(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q,
 //     with element 2j in the low nibble, scales written at their cuBLAS
 //     blocked-layout address (to_blocked_scales, nvfp4_quant.py:72-84).
 
-// bf16(x / smooth) for 8 packed bf16 (smooth reciprocals precomputed)
-__device__ __forceinline__ void smooth8(const uint4& xv, const uint4& sv, float (&o)[8]) {
+// bf16(x / smooth) for 8 packed bf16 at column c8 (reciprocals from rsm)
+__device__ __forceinline__ void smooth8(const uint4& xv, const uint4& sv, const float* rsm,
+                                        float (&o)[8]) {
   const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
   const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+  const float4 r0 = *reinterpret_cast<const float4*>(rsm);
+  const float4 r1 = *reinterpret_cast<const float4*>(rsm + 4);
+  const float rr[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const float s0 = bf_lo(sw[j]), s1 = bf_hi(sw[j]);
-    o[2 * j] = __bfloat162float(__float2bfloat16_rn(div_rn(bf_lo(xw[j]), s0, __frcp_rn(s0))));
-    o[2 * j + 1] = __bfloat162float(__float2bfloat16_rn(div_rn(bf_hi(xw[j]), s1, __frcp_rn(s1))));
+    o[2 * j] = __bfloat162float(__float2bfloat16_rn(div_rn(bf_lo(xw[j]), bf_lo(sw[j]), rr[2 * j])));
+    o[2 * j + 1] =
+        __bfloat162float(__float2bfloat16_rn(div_rn(bf_hi(xw[j]), bf_hi(sw[j]), rr[2 * j + 1])));
   }
+}
+
+__global__ void nvfp4_rsmooth_kernel(const __nv_bfloat16* __restrict__ smooth,
+                                     float* __restrict__ rsm, int K) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < K) rsm[i] = __frcp_rn(__bfloat162float(smooth[i]));
 }
 
 __device__ __forceinline__ void raw8(const uint4& xv, float (&o)[8]) {
@@ -460,7 +473,8 @@ __device__ __forceinline__ void raw8(const uint4& xv, float (&o)[8]) {
 
 __global__ void __launch_bounds__(256)
 nvfp4_amax_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ smooth,
-                  unsigned int* __restrict__ amax_bits, int M, int K) {
+                  const float* __restrict__ rsm, unsigned int* __restrict__ amax_bits, int M,
+                  int K) {
   const int64_t nvec = (int64_t)M * K / 8;
   const int kv = K / 8;
   float m = 0.f;
@@ -468,7 +482,8 @@ nvfp4_amax_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __re
        i += (int64_t)gridDim.x * blockDim.x) {
     const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x) + i);
     float v[8];
-    if (smooth) smooth8(xv, __ldg(reinterpret_cast<const uint4*>(smooth) + (i % kv)), v);
+    const int cv = (int)(i % kv);
+    if (smooth) smooth8(xv, __ldg(reinterpret_cast<const uint4*>(smooth) + cv), rsm + 8 * cv, v);
     else raw8(xv, v);
 #pragma unroll
     for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
@@ -515,8 +530,8 @@ act_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __res
     float lo[8], hi[8];
     if (smooth) {
       const uint4* sp = reinterpret_cast<const uint4*>(smooth + c * 16);
-      smooth8(__ldg(xp), __ldg(sp), lo);
-      smooth8(__ldg(xp + 1), __ldg(sp + 1), hi);
+      smooth8(__ldg(xp), __ldg(sp), work + 4 + c * 16, lo);
+      smooth8(__ldg(xp + 1), __ldg(sp + 1), work + 4 + c * 16 + 8, hi);
     } else {
       raw8(__ldg(xp), lo);
       raw8(__ldg(xp + 1), hi);
@@ -545,17 +560,31 @@ act_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __res
                        ((row & 127) >> 5) * 4 + (c & 3);
     sblk[off] = (uint8_t)sbyte;
   }
+  // zero scales of the padding rows up to the next multiple of 128 (the
+  // reference's to_blocked_scales pads with zeros)
+  const int mpad = ((M + 127) / 128) * 128;
+  const int64_t npad = (int64_t)(mpad - M) * kb16;
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < npad;
+       b += (int64_t)gridDim.x * blockDim.x) {
+    const int row = M + (int)(b / kb16), c = (int)(b % kb16);
+    sblk[((size_t)(row >> 7) * ncb + (c >> 2)) * 512 + (row & 31) * 16 +
+         ((row & 127) >> 5) * 4 + (c & 3)] = 0;
+  }
 }
 
 int launch_act_nvfp4(const void* x, const void* smooth, float* work, void* codes, void* sblk,
                      int M, int K, cudaStream_t st) {
   if (cudaMemsetAsync(work, 0, sizeof(float), st) != cudaSuccess) return GWB_E_LAUNCH;
+  if (smooth)
+    nvfp4_rsmooth_kernel<<<(K + 255) / 256, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(smooth), work + 4, K);
   const int64_t nvec = (int64_t)M * K / 8;
   int64_t blocks = (nvec + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
   nvfp4_amax_kernel<<<(int)blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
                                                   static_cast<const __nv_bfloat16*>(smooth),
-                                                  reinterpret_cast<unsigned int*>(work), M, K);
+                                                  work + 4, reinterpret_cast<unsigned int*>(work),
+                                                  M, K);
   const int64_t nblk = (int64_t)M * (K / 16);
   blocks = (nblk + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;

@@ -213,8 +213,7 @@ int gwb_nvfp4_quant(const void* x, const void* smooth, int64_t M, int64_t K, voi
                     void* sblk, float* work, void* stream) {
   if (M == 0) return GWB_SUCCESS;
   if (!fits_int(M) || !fits_int(K) || K % 64 || K == 0) return GWB_E_SHAPE;
-  if (!al16(x) || !al16(codes) || (smooth && !al16(smooth)) || !sblk || !work ||
-      (reinterpret_cast<uintptr_t>(work) & 7u))
+  if (!al16(x) || !al16(codes) || (smooth && !al16(smooth)) || !sblk || !work || !al16(work))
     return GWB_E_ALIGN;
   return gwb::launch_act_nvfp4(x, smooth, work, codes, sblk, (int)M, (int)K, S(stream));
 }

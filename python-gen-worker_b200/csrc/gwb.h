@@ -23,8 +23,9 @@ int launch_act_int4(const void* x, const void* smooth, const void* down_t, void*
 int launch_scale_k8(const void* scale, void* scale_k8, int R, int K, cudaStream_t st);
 int launch_act_int8(const void* x, void* q, void* scale, int M, int K, cudaStream_t st);
 int launch_act_fp8(const void* x, void* q, void* scale, int M, int K, cudaStream_t st);
-// NVFP4 activations: work f32 [2] (work[0] amax scratch, work[1] = s2 out);
-// codes u8 [M, K/2]; sblk = blocked e4m3 scales (caller zero-fills the padding).
+// NVFP4 activations: work f32 [4 + K], 16-byte aligned (work[0] amax scratch,
+// work[1] = s2 out, work[4..] the smoothing reciprocals); codes u8 [M, K/2]; sblk = blocked
+// e4m3 scales (padding rows written as zeros).
 int launch_act_nvfp4(const void* x, const void* smooth, float* work, void* codes, void* sblk,
                      int M, int K, cudaStream_t st);
 

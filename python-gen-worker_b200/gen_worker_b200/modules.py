@@ -239,7 +239,7 @@ class SvdqNvfp4Linear(nn.Module):
                 torch.empty(out_features, dtype=compute_dtype, device=dev), requires_grad=False)
         else:
             self.bias = None
-        self._up_pad: Optional[torch.Tensor] = None
+        self._up_pad: Optional[tuple] = None
 
     def _apply(self, fn, recurse=True):
         self._up_pad = None
@@ -254,8 +254,9 @@ class SvdqNvfp4Linear(nn.Module):
         la = up = None
         if self.rank:
             if self._up_pad is None:
-                self._up_pad = ops.nvfp4_up_over_ws2(self.proj_up, self.weight_scale_2)
-            la, up = ops.nvfp4_lowrank_operands(x2, self.proj_down, self._up_pad, work)
+                self._up_pad = ops.nvfp4_lowrank_prepare(self.proj_down, self.proj_up,
+                                                         self.weight_scale_2)
+            la, up = ops.nvfp4_lowrank_operands(x2, self._up_pad[0], self._up_pad[1], work)
         y = ops.nvfp4_gemm(codes, sblk, work, self.weight, self.weight_scale,
                            self.weight_scale_2, la, up,
                            self.bias.detach() if self.bias is not None else None)

@@ -334,13 +334,13 @@ def nvfp4_quant(x2: torch.Tensor, smooth: Optional[torch.Tensor]
                 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """The reference's NVFP4 activation chain (smoothing divide, per-tensor
     ``s2``, ``quantize_activation``): x2 bf16 [M, K] -> (codes u8 [M, K/2],
-    blocked e4m3 scale bytes u8, work f32 [2] with ``work[1] = s2``)."""
+    blocked e4m3 scale bytes u8, work f32 [4 + K] with ``work[1] = s2``)."""
     _need(x2, "x2", torch.bfloat16, 2)
     _need(smooth, "smooth", torch.bfloat16, 1)
     m, k = x2.shape
     codes = torch.empty(m, k // 2, dtype=torch.uint8, device=x2.device)
-    sblk = torch.zeros(nvfp4_blocked_numel(m, k), dtype=torch.uint8, device=x2.device)
-    work = torch.empty(2, dtype=torch.float32, device=x2.device)
+    sblk = torch.empty(nvfp4_blocked_numel(m, k), dtype=torch.uint8, device=x2.device)
+    work = torch.empty(4 + k, dtype=torch.float32, device=x2.device)
     lib = native.require()
     native.check(lib.gwb_nvfp4_quant(x2.data_ptr(), _ptr(smooth), m, k, codes.data_ptr(),
                                      sblk.data_ptr(), work.data_ptr(), _stream()), "nvfp4_quant")
@@ -352,7 +352,7 @@ def _(x2, smooth):
     m, k = x2.shape
     return (x2.new_empty(m, k // 2, dtype=torch.uint8),
             x2.new_empty(nvfp4_blocked_numel(m, k), dtype=torch.uint8),
-            x2.new_empty(2, dtype=torch.float32))
+            x2.new_empty(4 + k, dtype=torch.float32))
 
 
 @torch.library.custom_op("gwb200::nvfp4_gemm", mutates_args=())
@@ -396,26 +396,32 @@ def nvfp4_gemm(codes: torch.Tensor, sblk: torch.Tensor, work: torch.Tensor, w_co
     return out
 
 
-def nvfp4_lowrank_operands(x2: torch.Tensor, proj_down: torch.Tensor, up_over_ws2: torch.Tensor,
+def nvfp4_lowrank_operands(x2: torch.Tensor, down_pad: torch.Tensor, up_over_ws2: torch.Tensor,
                            work: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Low-rank operands of :func:`nvfp4_gemm`: ``la = bf16(x2 · proj_down)``
     on raw x exactly as the reference's bf16 matmul (``svdq_native.py:153``)
     and the up-projection ``bf16(proj_up / (weight_scale_2[n] · s2))`` (the
     branch then shares the main accumulator, which the epilogue multiplies by
-    ``s2 · weight_scale_2``); both padded to rank_pad columns.
-    ``up_over_ws2`` = fp32 ``proj_up / weight_scale_2`` (load time)."""
-    n, r = up_over_ws2.shape
-    rp = rank_pad_of(r)
-    la = torch.zeros(x2.shape[0], rp, dtype=torch.bfloat16, device=x2.device)
-    la[:, :r] = x2 @ proj_down.to(x2.dtype)
-    up = torch.zeros(n, rp, dtype=torch.bfloat16, device=x2.device)
-    up[:, :r] = (up_over_ws2 / work[1]).to(torch.bfloat16)
+    ``s2 · weight_scale_2``). ``down_pad`` bf16 [K, rank_pad] and
+    ``up_over_ws2`` fp32 [N, rank_pad] are the load-time forms
+    (:func:`nvfp4_lowrank_prepare`)."""
+    la = x2 @ down_pad
+    up = (up_over_ws2 / work[1]).to(torch.bfloat16)
     return la, up
 
 
-def nvfp4_up_over_ws2(proj_up: torch.Tensor, w_scale_2: torch.Tensor) -> torch.Tensor:
-    """Load-time fp32 ``proj_up / weight_scale_2[n]``."""
-    return (proj_up.float() / w_scale_2.float().reshape(-1, 1)).contiguous()
+def nvfp4_lowrank_prepare(proj_down: torch.Tensor, proj_up: torch.Tensor,
+                          w_scale_2: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Load time: ``proj_down`` bf16 padded to [K, rank_pad] and the fp32
+    ``proj_up / weight_scale_2[n]`` padded to [N, rank_pad]."""
+    k, r = proj_down.shape
+    n = proj_up.shape[0]
+    rp = rank_pad_of(r)
+    down = torch.zeros(k, rp, dtype=torch.bfloat16, device=proj_down.device)
+    down[:, :r] = proj_down.to(torch.bfloat16)
+    up = torch.zeros(n, rp, dtype=torch.float32, device=proj_up.device)
+    up[:, :r] = proj_up.float() / w_scale_2.float().reshape(-1, 1)
+    return down, up
 
 
 @nvfp4_gemm.register_fake
