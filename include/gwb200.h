@@ -195,6 +195,40 @@ int gwb_nvfp4_gemm(const void* a_codes, const void* a_sblk, const float* a_work,
                    int ws2_per_channel, const void* la, const void* proj_up, const void* bias,
                    int64_t M, int64_t N, int64_t K, int rank_pad, void* out, void* stream);
 
+/* ---- Load-time codec: nunchaku "v1 single-file" SVDQuant tensors -> the
+ * NVFP4 lane's buffers as stored. Host-memory functions (no GPU needed).
+ * Together they replace `decode_linear` + `to_buffers` (reference
+ * src/gen_worker/models/svdq_layout.py:363-438, 473-483) without the
+ * logical-domain intermediate; GWB_E_SHAPE for sizes the format forbids. */
+
+/* qweight I8 [N, K/2] (fragment interleave, svdq_layout.py:89-110) ->
+ * `weight` u8 [N, K/2], packed e2m1 with element 2j in the low nibble
+ * (pack_e2m1, nvfp4_quant.py:54-56). N % 128 == 0, K % 128 == 0; both
+ * buffers 4-byte aligned. */
+int gwb_nunchaku_qweight_to_e2m1(const void* qweight, int64_t N, int64_t K, void* weight);
+
+/* wscales E4M3 [K/16, N] (micro-scale pack, svdq_layout.py:117-129) ->
+ * `weight_scale` in the cuBLAS blocked layout (to_blocked_scales,
+ * nvfp4_quant.py:72-84), N * K/16 bytes. N % 128 == 0, K % 64 == 0. */
+int gwb_nunchaku_wscales_to_blocked(const void* wscales, int64_t N, int64_t K, void* blocked);
+
+/* pack_scale vector (wcscales, smooth_factor, bias; svdq_layout.py:132-142)
+ * of n elements of elem_bytes (1, 2, 4 or 8) -> row-major. n % 128 == 0. */
+int gwb_nunchaku_vector_unpack(const void* vec, int64_t n, int elem_bytes, void* out);
+
+/* pack_lowrank_weight-packed 16-bit factor (svdq_layout.py:145-162):
+ * down = 1: proj_down [rows = in_features, rank] -> row-major [in, rank];
+ * down = 0: proj_up [rows = out_features, rank] -> row-major [out, rank].
+ * rows % 16 == 0, rank % 16 == 0. */
+int gwb_nunchaku_lowrank_unpack(const void* w, int64_t rows, int64_t rank, int down, void* out);
+
+/* Quantized low-rank factor (dequantize_lowrank, svdq_layout.py:284-306):
+ * q [rows, cols] int8 (scheme 0) or e4m3 (scheme 1), fp32 scales per
+ * 32-element block along block_dim (0: [rows/32, cols], 1: [rows, cols/32])
+ * -> bf16 [rows, cols] = bf16(q * scale), round to nearest even. */
+int gwb_lowrank_dequant(const void* q, const float* scale, int64_t rows, int64_t cols,
+                        int block_dim, int scheme, void* out);
+
 /* Reads and clears the device-side error flag set by a bounded wait that
  * expired (0 = none). Synchronises the device. */
 int gwb_device_error(int* code);

@@ -7,6 +7,7 @@
 #include "ptx.cuh"
 #include "act_quant.cu"
 #include "gemm.cu"
+#include "codec.cu"
 #include "../../include/gwb200.h"
 
 #ifndef GWB_ARCH_STRING
@@ -233,6 +234,47 @@ int gwb_device_error(int* code) {
   if (!code) return GWB_E_SHAPE;
   if (cudaDeviceSynchronize() != cudaSuccess) return GWB_E_LAUNCH;
   return gwb::device_error_read_and_clear(code);
+}
+
+int gwb_nunchaku_qweight_to_e2m1(const void* qweight, int64_t N, int64_t K, void* weight) {
+  if (N <= 0 || K <= 0 || N % 128 || K % 128) return GWB_E_SHAPE;
+  if (((uintptr_t)qweight | (uintptr_t)weight) & 3u) return GWB_E_ALIGN;
+  gwb::codec::qweight_to_e2m1(static_cast<const uint32_t*>(qweight), N, K,
+                              static_cast<uint32_t*>(weight));
+  return GWB_SUCCESS;
+}
+
+int gwb_nunchaku_wscales_to_blocked(const void* wscales, int64_t N, int64_t K, void* blocked) {
+  if (N <= 0 || K <= 0 || N % 128 || K % 64) return GWB_E_SHAPE;
+  gwb::codec::wscales_to_blocked(static_cast<const uint8_t*>(wscales), N, K,
+                                 static_cast<uint8_t*>(blocked));
+  return GWB_SUCCESS;
+}
+
+int gwb_nunchaku_vector_unpack(const void* vec, int64_t n, int elem_bytes, void* out) {
+  if (n <= 0 || n % 128) return GWB_E_SHAPE;
+  if (elem_bytes != 1 && elem_bytes != 2 && elem_bytes != 4 && elem_bytes != 8)
+    return GWB_E_SHAPE;
+  gwb::codec::vector_unpack(static_cast<const uint8_t*>(vec), n, elem_bytes,
+                            static_cast<uint8_t*>(out));
+  return GWB_SUCCESS;
+}
+
+int gwb_nunchaku_lowrank_unpack(const void* w, int64_t rows, int64_t rank, int down, void* out) {
+  if (rows <= 0 || rank <= 0 || rows % 16 || rank % 16) return GWB_E_SHAPE;
+  gwb::codec::lowrank_unpack(static_cast<const uint16_t*>(w), rows, rank, down != 0,
+                             static_cast<uint16_t*>(out));
+  return GWB_SUCCESS;
+}
+
+int gwb_lowrank_dequant(const void* q, const float* scale, int64_t rows, int64_t cols,
+                        int block_dim, int scheme, void* out) {
+  if (rows <= 0 || cols <= 0 || (block_dim != 0 && block_dim != 1)) return GWB_E_SHAPE;
+  if ((block_dim == 0 ? rows : cols) % 32) return GWB_E_SHAPE;
+  if (scheme != 0 && scheme != 1) return GWB_E_SHAPE;
+  gwb::codec::lowrank_dequant(static_cast<const uint8_t*>(q), scale, rows, cols, block_dim,
+                              scheme == 1, static_cast<uint16_t*>(out));
+  return GWB_SUCCESS;
 }
 
 int gwb_device_check(void) {

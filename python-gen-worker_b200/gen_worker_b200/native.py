@@ -53,6 +53,11 @@ _SIGNATURES = {
     "gwb_nvfp4_gemm": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                        c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_int, c_void_p,
                        c_void_p],
+    "gwb_nunchaku_qweight_to_e2m1": [c_void_p, c_i64, c_i64, c_void_p],
+    "gwb_nunchaku_wscales_to_blocked": [c_void_p, c_i64, c_i64, c_void_p],
+    "gwb_nunchaku_vector_unpack": [c_void_p, c_i64, c_int, c_void_p],
+    "gwb_nunchaku_lowrank_unpack": [c_void_p, c_i64, c_i64, c_int, c_void_p],
+    "gwb_lowrank_dequant": [c_void_p, c_void_p, c_i64, c_i64, c_int, c_int, c_void_p],
     "gwb_fp8_gemm": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64,
                      c_int, c_void_p, c_void_p],
     "gwb_fp8_linear": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_int,

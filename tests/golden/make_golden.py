@@ -24,7 +24,13 @@ Everything is produced by CALLING the reference's own functions:
   ``src/gen_worker/models/w8a8.py:261-273``, reached through
   ``_build_quantizer(torch).eager_source``) -> e4m3 codes and f32 row scales
   over rows spanning many binades, an all-zero row and a row whose values
-  fall into the e4m3 subnormal range after scaling.
+  fall into the e4m3 subnormal range after scaling;
+* the nunchaku "v1 single-file" packers ``pack_qweight``, ``pack_wscales``,
+  ``pack_vector``, ``pack_lowrank`` (``svdq_layout.py:165-221``) on seeded
+  logical tensors, and the reference's decode of the packed tensors
+  (``convert_linear``, ``split_decoded`` + ``to_buffers``,
+  ``svdq_layout.py:441-489``), including int8 / e4m3 quantized low-rank
+  factors (``quantize_lowrank``).
 """
 from __future__ import annotations
 
@@ -117,6 +123,66 @@ def main(ref_root: str = "/root/reference") -> None:
     xf = xf.to(torch.bfloat16)
     fq, fs = quant_src(xf, False, None)
     out["fp8_x"], out["fp8_q"], out["fp8_scale"] = xf, fq.view(torch.uint8), fs
+
+    # 7. nunchaku "v1 single-file" codec: logical tensors packed by the
+    # reference's own forward packers, and the reference's decode
+    # (`convert_linear` = decode_linear + to_buffers) of the packed tensors
+    n, k, r = 256, 256, 32
+    codes = torch.randint(0, 16, (n, k), generator=gen, dtype=torch.uint8)
+    scales = (torch.rand(n, k // nq.BLOCK, generator=gen) * 6 + 0.1).to(torch.float8_e4m3fn)
+    wc = torch.rand(n, generator=gen) * 0.02 + 0.001
+    smooth = (torch.rand(k, generator=gen) + 0.5).to(torch.bfloat16)
+    bias = torch.randn(n, generator=gen).to(torch.bfloat16)
+    down = (torch.randn(k, r, generator=gen) * 0.05).to(torch.bfloat16)     # [in, rank]
+    up = (torch.randn(n, r, generator=gen) * 0.05).to(torch.bfloat16)       # [out, rank]
+    packed = {
+        "qweight": sl.pack_qweight(codes),
+        "wscales": sl.pack_wscales(scales, n, k),
+        "wcscales": sl.pack_vector(wc, n),
+        "smooth_factor": sl.pack_vector(smooth, k),
+        "bias": sl.pack_vector(bias, n),
+        "proj_down": sl.pack_lowrank(down.t().contiguous(), down=True),
+        "proj_up": sl.pack_lowrank(up, down=False),
+    }
+    buf = sl.convert_linear(packed, n, k)
+    out["nk_codes"], out["nk_scales"] = codes, scales.view(torch.uint8)
+    out["nk_wc"], out["nk_smooth"], out["nk_bias"] = wc, smooth, bias
+    out["nk_down"], out["nk_up"] = down, up
+    for key, val in packed.items():
+        out["nk_packed_" + key] = val.view(torch.uint8) if val.dtype == torch.float8_e4m3fn else val
+    out["nk_buf_weight"] = buf.weight
+    out["nk_buf_weight_scale"] = buf.weight_scale.view(torch.uint8)
+    out["nk_buf_weight_scale_2"] = buf.weight_scale_2
+    out["nk_buf_proj_down"], out["nk_buf_proj_up"] = buf.proj_down, buf.proj_up
+    out["nk_buf_smooth"], out["nk_buf_bias"] = buf.smooth_factor, buf.bias
+    # per-tensor second-level scale, no low-rank branch, no smoothing
+    pt = {"qweight": packed["qweight"], "wscales": packed["wscales"],
+          "wtscale": torch.tensor([0.0125])}
+    bpt = sl.convert_linear(pt, n, k)
+    out["nk_pt_weight_scale_2"] = bpt.weight_scale_2
+    # quantized low-rank branch (int8 and e4m3, blocks of 32 along the
+    # contraction dim of each factor)
+    for scheme in ("int8", "fp8_e4m3"):
+        qd, sd = sl.quantize_lowrank(down, scheme=scheme, block_dim=0)
+        qu, su = sl.quantize_lowrank(up, scheme=scheme, block_dim=1)
+        tq = {"qweight": packed["qweight"], "wscales": packed["wscales"],
+              "wcscales": packed["wcscales"], "proj_down": qd, "proj_down_scale": sd,
+              "proj_up": qu, "proj_up_scale": su}
+        bq = sl.convert_linear(tq, n, k)
+        tag = "nk_" + scheme + "_"
+        out[tag + "qdown"] = qd.view(torch.uint8) if qd.dtype == torch.float8_e4m3fn else qd
+        out[tag + "qup"] = qu.view(torch.uint8) if qu.dtype == torch.float8_e4m3fn else qu
+        out[tag + "sdown"], out[tag + "sup"] = sd, su
+        out[tag + "down"], out[tag + "up"] = bq.proj_down, bq.proj_up
+    # fused projection split along N (split_decoded) on the decoded buffers
+    parts = sl.split_decoded(sl.decode_linear(packed, n, k), (128, 128))
+    for i, part in enumerate(parts):
+        bp = sl.to_buffers(part)
+        out[f"nk_split{i}_weight"] = bp.weight
+        out[f"nk_split{i}_weight_scale"] = bp.weight_scale.view(torch.uint8)
+        out[f"nk_split{i}_weight_scale_2"] = bp.weight_scale_2
+        out[f"nk_split{i}_proj_up"] = bp.proj_up
+        out[f"nk_split{i}_bias"] = bp.bias
 
     path = HERE / "reference_golden.pt"
     torch.save(out, path)

@@ -11,6 +11,8 @@ import torch
 
 from oracle import svdq_oracle as O
 from gen_worker_b200 import ops, native
+
+ROOT = Path(__file__).resolve().parent.parent
 from gen_worker_b200.modules import (build_fp8_rowwise_linear, build_svdq_int4_linear,
                                      build_svdq_nvfp4_linear, build_w8a8_int8_linear)
 
@@ -261,6 +263,25 @@ def test_nvfp4_linear_matches_oracle(cuda_ready, m, k, n, rank, per_channel):
                                    "proj_down": down, "proj_up": up, "bias": bias}, device="cuda")
     y = mod(x.cuda()).cpu()
     want = O.svdq_nvfp4_linear(x, smooth, packed, blocked, ws2, down, up, bias)
+    assert O.rel_l2(y, want["y"]) <= REL_TOL
+    assert O.max_abs_beyond_bf16(y, want["y64"]) <= ABS_TOL
+    assert native.device_error() == 0
+
+
+def test_nvfp4_linear_from_nunchaku_tensors(cuda_ready):
+    """The reference's packers' output (nunchaku v1 storage), decoded by the
+    native codec into the module, runs the NVFP4 GEMM and matches the oracle
+    on the reference's own decoded buffers."""
+    from gen_worker_b200 import codec
+    gold = torch.load(ROOT / "tests" / "golden" / "reference_golden.pt")
+    t = {k[len("nk_packed_"):]: v for k, v in gold.items() if k.startswith("nk_packed_")}
+    t["wscales"] = t["wscales"].view(torch.float8_e4m3fn)
+    mod = codec.build_svdq_nvfp4_from_nunchaku(t, 256, 256, device="cuda")
+    x = O.synth_activation(96, 256, seed=5)
+    y = mod(x.cuda()).cpu()
+    want = O.svdq_nvfp4_linear(x, gold["nk_buf_smooth"], gold["nk_buf_weight"],
+                               gold["nk_buf_weight_scale"], gold["nk_buf_weight_scale_2"],
+                               gold["nk_buf_proj_down"], gold["nk_buf_proj_up"], gold["nk_buf_bias"])
     assert O.rel_l2(y, want["y"]) <= REL_TOL
     assert O.max_abs_beyond_bf16(y, want["y64"]) <= ABS_TOL
     assert native.device_error() == 0
