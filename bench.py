@@ -442,6 +442,101 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
             "l2": "256 MB flush between iterations"}
 
 
+# --------------------------------------------------------------------------- AWQ modulation GEMV
+# Flux modulation layers: dual-stream blocks 3072 -> 6 x 3072, single-stream
+# blocks 3072 -> 3 x 3072; M is the batch (1, or 2 with classifier-free
+# guidance). Each layer's codes are read once per denoising step, so every
+# launch starts from a flushed L2.
+AWQ_SHAPES = [(1, 3072, 18432), (2, 3072, 18432), (1, 3072, 9216), (2, 3072, 9216)]
+
+
+def hbm_peak_gbs() -> tuple[float, str]:
+    try:
+        mp = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(mp["hbm_gbs"]), "measured HBM copy (MEASURED_PEAKS.json)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback HBM copy 6.65 TB/s"
+
+
+def run_awq_case(steps: int, warmup: int) -> dict:
+    """The AWQ W4A16 GEMV (``gwb_awq_w4a16_mm``) against the reference's
+    decode lane for the same layer (``decode_awq_linear``: a dense bf16
+    ``nn.Linear``, cuBLAS). Launches run back to back over rotating copies of
+    the layer whose total exceeds L2 by 2x or more, so every launch streams
+    its weights from HBM as consecutive layers of a step do, with no flush
+    kernel (and no dirty-line write-back) inside the timed region; bytes are
+    algorithmic (codes + scale/zero grids + x + bias + out; the dense lane
+    reads N x K bf16). Both lanes are replayed from a CUDA graph, so the
+    figures are device time."""
+    from gen_worker_b200 import awq
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    peak, peak_src = hbm_peak_gbs()
+
+    def timed(calls) -> float:
+        # captured once into a CUDA graph (4 passes over the copies) and
+        # replayed: the device time per launch, without the host-side cost
+        # of issuing each op
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for c in calls:
+                c()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(4):
+                for c in calls:
+                    c()
+        for _ in range(max(1, warmup)):
+            graph.replay()
+        torch.cuda.synchronize()
+        a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            graph.replay()
+        b_.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b_) / (steps * 4 * len(calls))
+
+    rows = []
+    for m, k, n in AWQ_SHAPES:
+        x = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
+        bias = torch.randn(n, generator=g, device=dev).to(torch.bfloat16)
+        nbytes = n * k // 2 + 2 * n * (k // 64) * 2 + m * k * 2 + n * 2 + m * n * 2
+        dense_bytes = n * k * 2 + m * k * 2 + n * 2 + m * n * 2
+        copies = max(2, -(-(256 << 20) // nbytes))
+        layers = []
+        for _ in range(copies):
+            weight = torch.randint(0, 256, (n, k // 2), generator=g, device=dev, dtype=torch.uint8)
+            ws = (torch.rand(n, k // 64, generator=g, device=dev) * 0.01 + 1e-3).to(torch.bfloat16)
+            wz = (-torch.rand(n, k // 64, generator=g, device=dev) * 0.05).to(torch.bfloat16)
+            layers.append((weight, ws, wz))
+        ms = timed([lambda L=L: awq.awq_w4a16_mm(x, L[0], L[1], L[2], bias) for L in layers])
+        weight, ws, wz = layers[0]
+        codes = torch.stack([weight & 0xF, weight >> 4], dim=-1).reshape(n, k)
+        dense = (codes.float().reshape(n, k // 64, 64) * ws.float().unsqueeze(-1)
+                 + wz.float().unsqueeze(-1)).reshape(n, k).to(torch.bfloat16)
+        del codes, layers
+        dcopies = max(2, -(-(256 << 20) // dense_bytes))
+        dense_layers = [dense] + [dense.clone() for _ in range(dcopies - 1)]
+        ms_dense = timed([lambda D=D: torch.nn.functional.linear(x, D, bias)
+                          for D in dense_layers])
+        del dense_layers, dense
+        gbs = nbytes / (ms / 1e3) / 1e9
+        rows.append({"M": m, "K": k, "N": n, "us": ms * 1e3, "gbs": gbs, "hbm_frac": gbs / peak,
+                     "bytes": nbytes, "copies": copies, "dense_bf16_linear_us": ms_dense * 1e3,
+                     "dense_bf16_linear_gbs": dense_bytes / (ms_dense / 1e3) / 1e9,
+                     "speedup_vs_dense": ms_dense / ms})
+    return {"metric": "AWQ W4A16 modulation GEMV achieved HBM GB/s", "unit": "GB/s",
+            "value": sum(r["bytes"] for r in rows) / (sum(r["us"] for r in rows) / 1e6) / 1e9,
+            "peak_gbs": peak, "peak": peak_src, "layers": rows, "steps": steps,
+            "warmup": warmup,
+            "l2": "back-to-back launches over rotating layer copies totalling >= 256 MB",
+            "timing": "CUDA graph replay, CUDA events"}
+
+
 # --------------------------------------------------------------------------- main
 def main() -> int:
     ap = argparse.ArgumentParser()
@@ -450,7 +545,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", choices=sorted(CASES), default=None,
+    ap.add_argument("--case", choices=sorted(CASES) + ["awq"], default=None,
                     help="time one BASELINE config's linears instead of the cfg4 stack")
     args = ap.parse_args()
     world, rank, local = dist_env()
@@ -458,7 +553,10 @@ def main() -> int:
     if args.case is not None:
         from gen_worker_b200 import native
         native.require()
-        print(json.dumps(run_case(args.case, args.steps, args.warmup)))
+        if args.case == "awq":
+            print(json.dumps(run_awq_case(args.steps, args.warmup)))
+        else:
+            print(json.dumps(run_case(args.case, args.steps, args.warmup)))
         return 0
 
     if args.impl == "reference":

@@ -229,6 +229,25 @@ int gwb_nunchaku_lowrank_unpack(const void* w, int64_t rows, int64_t rank, int d
 int gwb_lowrank_dequant(const void* q, const float* scale, int64_t rows, int64_t cols,
                         int block_dim, int scheme, void* out);
 
+/* ---- AWQ W4A16 modulation layers (timestep-embedding consumers). */
+
+/* qweight I32 [N/4, K/2] (TinyChat pack, reference svdq_awq.py:31-47) ->
+ * `weight` u8 [N, K/2], unsigned 4-bit codes, element 2j in the low nibble
+ * (the packed-resident module's buffer, svdq_awq_packed.py:262). Host
+ * memory. N % 4 == 0, K % 64 == 0. */
+int gwb_awq_qweight_unpack(const void* qweight, int64_t N, int64_t K, void* weight);
+
+/* Replaces `cozy_gen_worker::awq_w4a16_mm` (svdq_awq_packed.py:51-103):
+ * out bf16 [M, N] = x bf16 [M, K] · bf16(q * wscales + wzeros)^T + bias,
+ * q the codes of `weight` u8 [N, K/2], wscales / wzeros bf16 [N, K/64]
+ * (group 64, zeros pre-scaled and pre-negated), bias bf16 [N] or NULL; f32
+ * accumulation. The dequantised weight is q * s + z rounded once to bf16,
+ * equal to the reference's decode (`dequantize_w4x16` in f32, then bf16)
+ * whenever q * s + z fits 24 significant bits. N % 16 == 0, K % 128 == 0,
+ * x and weight 16-byte aligned. M == 0 is a no-op. */
+int gwb_awq_w4a16_mm(const void* x, const void* weight, const void* wscales, const void* wzeros,
+                     const void* bias, int64_t M, int64_t N, int64_t K, void* out, void* stream);
+
 /* Reads and clears the device-side error flag set by a bounded wait that
  * expired (0 = none). Synchronises the device. */
 int gwb_device_error(int* code);

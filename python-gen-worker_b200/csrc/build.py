@@ -20,7 +20,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 PKG = HERE.parent / "gen_worker_b200"
 OUT = PKG / "_lib" / "libgwb200.so"
-SOURCES = ["capi.cu", "act_quant.cu", "gemm.cu", "codec.cu", "noalloc.cu", "gwb.h", "ptx.cuh"]
+SOURCES = ["capi.cu", "act_quant.cu", "gemm.cu", "codec.cu", "awq.cu", "noalloc.cu", "gwb.h", "ptx.cuh"]
 HEADER = HERE.parent.parent / "include" / "gwb200.h"
 
 NVCC_FLAGS = [

@@ -8,6 +8,7 @@
 #include "act_quant.cu"
 #include "gemm.cu"
 #include "codec.cu"
+#include "awq.cu"
 #include "../../include/gwb200.h"
 
 #ifndef GWB_ARCH_STRING
@@ -275,6 +276,28 @@ int gwb_lowrank_dequant(const void* q, const float* scale, int64_t rows, int64_t
   gwb::codec::lowrank_dequant(static_cast<const uint8_t*>(q), scale, rows, cols, block_dim,
                               scheme == 1, static_cast<uint16_t*>(out));
   return GWB_SUCCESS;
+}
+
+int gwb_awq_qweight_unpack(const void* qweight, int64_t N, int64_t K, void* weight) {
+  if (N <= 0 || K <= 0 || N % 4 || K % 64) return GWB_E_SHAPE;
+  gwb::codec::awq_qweight_unpack(static_cast<const uint16_t*>(qweight), N, K,
+                                 static_cast<uint8_t*>(weight));
+  return GWB_SUCCESS;
+}
+
+int gwb_awq_w4a16_mm(const void* x, const void* weight, const void* wscales, const void* wzeros,
+                     const void* bias, int64_t M, int64_t N, int64_t K, void* out,
+                     void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  if (!fits_int(M) || !fits_int(N) || !fits_int(K) || N % 16 || K % 128 || N == 0)
+    return GWB_E_SHAPE;
+  if (!al16(x) || !al16(weight)) return GWB_E_ALIGN;
+  const cudaError_t e = gwb::launch_awq_w4a16(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const uint8_t*>(weight),
+      static_cast<const __nv_bfloat16*>(wscales), static_cast<const __nv_bfloat16*>(wzeros),
+      static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), (int)M, (int)N,
+      (int)K, S(stream));
+  return e == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }
 
 int gwb_device_check(void) {

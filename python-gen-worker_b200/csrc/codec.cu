@@ -19,9 +19,9 @@
 //    (_MICRO_FWD_PERM / _MICRO_ROW_DIMS, svdq_layout.py:24-25,
 //    unpack_wscales :117-129). Per 128 output rows x 4 scale groups the stored
 //    order is (row8, row4, row32, group4) with row = 32 row32 + 8 row4 + row8;
-//    the blocked layout (to_blocked_scales, nvfp4_quant.py:72-84) orders the
-//    same 512 bytes as (row32... ) 16 (row % 32) + 4 (row % 128 / 32) + group:
-//    a permutation inside each 512-byte tile.
+//    the blocked layout (to_blocked_scales, nvfp4_quant.py:72-84) puts the
+//    same 512 bytes at 16 (row % 32) + 4 (row % 128 / 32) + group: a
+//    permutation inside each 512-byte tile.
 //  * vectors (wcscales, smooth_factor, bias): pack_scale(group_size=-1)
 //    (_VEC_FWD_PERM / _VEC_ROW_DIMS, svdq_layout.py:27-28, unpack_vector
 //    :132-142); per 128 elements the stored order is (a8, c4, b2, e2) for
@@ -117,6 +117,34 @@ inline void lowrank_unpack(const uint16_t* __restrict__ src, int64_t rows, int64
     const int64_t o = down ? (cp * 16 + k16) * rank + rp * 16 + n16
                            : (cp * 16 + n16) * rank + rp * 16 + k16;
     dst[o] = src[s];
+  }
+}
+
+// AWQ W4A16 qweight (TinyChat pack_w4 of deepcompressor, stored I32
+// [N/4, K/2] = I16 [N/4, K]; svdq_awq.py:31-47 and its inverse pack_w4x16
+// :136-147) -> packed u8 [N, K/2], even k in the low nibble. The stored 16-bit
+// value t = (row group of 4, 64-code chunk, row in group, j16) holds, for
+// row n = 4 group + row and u = 16 chunk + j16, the codes of k = 32 (u / 8)
+// + (u % 8) + 8 i in its nibbles i = 0..3. N % 4 == 0, K % 64 == 0.
+inline void awq_qweight_unpack(const uint16_t* __restrict__ src, int64_t N, int64_t K,
+                               uint8_t* __restrict__ dst) {
+  const int64_t chunks = K / 64;
+  const int64_t total = N * K / 4;
+  std::memset(dst, 0, (size_t)(N * K / 2));
+  for (int64_t t = 0; t < total; ++t) {
+    int64_t v = t;
+    const int j16 = (int)(v & 15); v >>= 4;
+    const int r4 = (int)(v & 3); v >>= 2;
+    const int64_t c = v % chunks;
+    const int64_t R = v / chunks;
+    const int64_t n = R * 4 + r4;
+    const int64_t u = c * 16 + j16;
+    const uint16_t word = src[t];
+    for (int i = 0; i < 4; ++i) {
+      const int64_t k = 32 * (u / 8) + (u % 8) + 8 * i;
+      const uint8_t code = (uint8_t)((word >> (4 * i)) & 0xF);
+      dst[n * (K / 2) + k / 2] |= (k & 1) ? (uint8_t)(code << 4) : code;
+    }
   }
 }
 

@@ -58,6 +58,9 @@ _SIGNATURES = {
     "gwb_nunchaku_vector_unpack": [c_void_p, c_i64, c_int, c_void_p],
     "gwb_nunchaku_lowrank_unpack": [c_void_p, c_i64, c_i64, c_int, c_void_p],
     "gwb_lowrank_dequant": [c_void_p, c_void_p, c_i64, c_i64, c_int, c_int, c_void_p],
+    "gwb_awq_qweight_unpack": [c_void_p, c_i64, c_i64, c_void_p],
+    "gwb_awq_w4a16_mm": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64,
+                         c_void_p, c_void_p],
     "gwb_fp8_gemm": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64,
                      c_int, c_void_p, c_void_p],
     "gwb_fp8_linear": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_int,

@@ -30,7 +30,12 @@ Everything is produced by CALLING the reference's own functions:
   logical tensors, and the reference's decode of the packed tensors
   (``convert_linear``, ``split_decoded`` + ``to_buffers``,
   ``svdq_layout.py:441-489``), including int8 / e4m3 quantized low-rank
-  factors (``quantize_lowrank``).
+  factors (``quantize_lowrank``);
+* the AWQ W4A16 exporter ``encode_awq_linear`` (``svdq_awq.py:175-210``), the
+  packed-resident module's buffers ``build_awq_packed_linear``
+  (``svdq_awq_packed.py:204-249``) and the decoded dense layer
+  ``decode_awq_linear`` (``svdq_awq.py:108-132``), plain and with the adaLN
+  split interleave (6 splits).
 """
 from __future__ import annotations
 
@@ -183,6 +188,28 @@ def main(ref_root: str = "/root/reference") -> None:
         out[f"nk_split{i}_weight_scale_2"] = bp.weight_scale_2
         out[f"nk_split{i}_proj_up"] = bp.proj_up
         out[f"nk_split{i}_bias"] = bp.bias
+
+    # 8. AWQ W4A16 modulation layers: the reference's exporter
+    # (encode_awq_linear), its packed-resident module buffers
+    # (build_awq_packed_linear) and its decoded dense weights (decode_awq_linear)
+    from gen_worker.models import svdq_awq as sa
+    from gen_worker.models import svdq_awq_packed as sp
+    for oc, ic, splits in ((256, 256, 1), (384, 128, 6)):
+        w = torch.randn(oc, ic, generator=gen) * 0.05
+        b = torch.randn(oc, generator=gen)
+        t = sa.encode_awq_linear(w, b, adanorm_splits=splits)
+        ref = sa.decode_awq_linear(t, oc, ic, adanorm_splits=splits)
+        tag = f"awq{oc}_"
+        for key, val in t.items():
+            out[tag + "t_" + key] = val
+        out[tag + "dense_w"] = ref.weight.detach().clone()
+        out[tag + "dense_b"] = ref.bias.detach().clone()
+        if sp.awq_op() is not None:
+            mod = sp.build_awq_packed_linear(t, oc, ic, adanorm_splits=splits)
+            out[tag + "mod_weight"] = mod.weight.clone()
+            out[tag + "mod_wscales"] = mod.wscales.clone()
+            out[tag + "mod_wzeros"] = mod.wzeros.clone()
+            out[tag + "mod_bias"] = mod.bias.detach().clone()
 
     path = HERE / "reference_golden.pt"
     torch.save(out, path)
