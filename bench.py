@@ -274,12 +274,42 @@ CASES = {
     "cfg2": [("w4a4", 4608, 3072, 9216, 32, False), ("w4a4", 4608, 3072, 3072, 32, False),
              ("w4a4", 4608, 3072, 12288, 32, True), ("w4a4", 4608, 12288, 3072, 32, False)],
     "cfg3": [("w4a4", 4608, 3072, 3072, 48, False)],
+    # the cfg4 stack's own linears at its full 16896 tokens (one dual-stream
+    # and one single-stream block)
+    "cfg4dual": [("w4a4", 16896, 3072, 9216, 32, False), ("w4a4", 16896, 3072, 3072, 32, False),
+                 ("w4a4", 16896, 3072, 12288, 32, True), ("w4a4", 16896, 12288, 3072, 32, False)],
+    "cfg4single": [("w4a4", 16896, 3072, 21504, 32, False), ("w4a4", 16896, 15360, 3072, 32, False)],
     # the same shapes in the reference's own SVDQuant format (NVFP4)
     "cfg2nvfp4": [("nvfp4", 4608, 3072, 9216, 32, False), ("nvfp4", 4608, 3072, 3072, 32, False),
                   ("nvfp4", 4608, 3072, 12288, 32, False),
                   ("nvfp4", 4608, 12288, 3072, 32, False)],
     "cfg3nvfp4": [("nvfp4", 4608, 3072, 3072, 48, False)],
 }
+
+
+def graph_ms(call, steps: int, reps: int = 8) -> float:
+    """Device time of one ``call``: captured ``reps`` times into a CUDA graph
+    and replayed ``steps`` times between CUDA events (no host-side issue cost
+    inside the timed region)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        call()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            call()
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / (steps * reps)
 
 
 def _scaled_mm_fp4_ms(codes, sblk, w_codes, w_sblk, steps: int) -> Optional[float]:
@@ -295,15 +325,7 @@ def _scaled_mm_fp4_ms(codes, sblk, w_codes, w_sblk, steps: int) -> Optional[floa
                                     scale_a=sblk.view(torch.float8_e4m3fn),
                                     scale_b=w_sblk.view(torch.float8_e4m3fn),
                                     out_dtype=torch.bfloat16)
-        call()
-        torch.cuda.synchronize()
-        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s_.record()
-        for _ in range(steps):
-            call()
-        e_.record()
-        torch.cuda.synchronize()
-        return s_.elapsed_time(e_) / steps
+        return graph_ms(call, steps)
     except Exception:  # noqa: BLE001 - context figure only
         return None
 
@@ -388,9 +410,9 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
             if it >= warmup:
                 tot += e[0].elapsed_time(e[2]) / steps
                 gemm += e[1].elapsed_time(e[2]) / steps
-        # the GEMM alone, launched back to back on resident operands (warm
-        # L2, no host gaps between launches): the figure comparable with a
-        # library GEMM timed the same way
+        # the GEMM alone, replayed back to back from a CUDA graph on resident
+        # operands (warm L2, no host-side issue cost): the figure comparable
+        # with a library GEMM timed the same way
         if kind == "w4a4":
             p = mod.prepare()
             c, a, la = ops.svdq_w4a4_quant_mma(xb, mod.smooth_factor, p["proj_down_t"])
@@ -410,15 +432,10 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
             q, s_ = ops.w8a8_quant(xb)
             gemm_call = lambda: ops.w8a8_gemm(q, s_, mod.weight, mod.weight_scale.reshape(-1),  # noqa: E731
                                               mod.bias.detach(), gelu)
-        gemm_call()
-        torch.cuda.synchronize()
-        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        b0.record()
-        for _ in range(4 * steps):
-            gemm_call()
-        b1.record()
-        torch.cuda.synchronize()
-        b2b_ms = b0.elapsed_time(b1) / (4 * steps)
+        b2b_ms = graph_ms(gemm_call, steps)
+        # the whole module forward (quantiser + GEMM, plus the NVFP4 lane's
+        # torch ops), replayed from a CUDA graph: its device time
+        module_dev_ms = graph_ms(lambda: mod(xb), steps)
         lib_ms = None
         if kind == "nvfp4":
             lib_ms = _scaled_mm_fp4_ms(c, sb_, mod.weight, mod.weight_scale, 4 * steps)
@@ -430,6 +447,7 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
                      "tops": ops_ / (tot / 1e3) / 1e12, "gemm_tops": ops_ / (gemm / 1e3) / 1e12,
                      "act_gbs": act_bytes / ((tot - gemm) / 1e3) / 1e9,
                      "gemm_b2b_ms": b2b_ms, "gemm_b2b_tops": ops_ / (b2b_ms / 1e3) / 1e12,
+                     "module_graph_ms": module_dev_ms,
                      "cublaslt_scaled_mm_ms": lib_ms,
                      "cublaslt_scaled_mm_tops": (ops_ / (lib_ms / 1e3) / 1e12) if lib_ms else None})
     total_ms = sum(r_["ms"] for r_ in rows)

@@ -128,12 +128,23 @@ act_int4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
   constexpr int RP = NB * 8;
   constexpr int ROWS = 16 * MT;
   constexpr int kActWarps = act_warps<MT>();
-  extern __shared__ float red[];   // [kActWarps][ROWS][RP]
+  extern __shared__ float smem_f[];   // [K] smoothing reciprocals, then [kActWarps][ROWS][RP]
+  float* rs = smem_f;
+  float* red = smem_f + K;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int nchunks = K / 64;
   const int G = K / 64;
   const bool has_smooth = smooth != nullptr;
+  // RN(1 / smooth[k]) once per CTA (each column's divide needs it in every row)
+  if (has_smooth) {
+    for (int i = threadIdx.x; i < K / 2; i += blockDim.x) {
+      const uint32_t pair = __ldg(reinterpret_cast<const uint32_t*>(smooth) + i);
+      rs[2 * i] = __frcp_rn(bf_lo(pair));
+      rs[2 * i + 1] = __frcp_rn(bf_hi(pair));
+    }
+    __syncthreads();
+  }
 
   int rows[MT][2];
   bool valid[MT][2];
@@ -192,14 +203,14 @@ act_int4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
         sm[2 * j] = bf_lo(sw[j]);
         sm[2 * j + 1] = bf_hi(sw[j]);
       }
-      // the 8 lanes of a segment (same c) need the same 16 reciprocals: lane
-      // (g, c) computes those of columns 2g and 2g + 1 and the others arrive
-      // by shuffle from lane 4 * (j / 2) + c
-      const uint32_t pair = __ldg(reinterpret_cast<const uint32_t*>(smooth + k0 + 2 * g));
-      const float mine[2] = {__frcp_rn(bf_lo(pair)), __frcp_rn(bf_hi(pair))};
+      // the segment's 16 reciprocals from shared memory (the 8 lanes of a
+      // segment read the same addresses: broadcast)
+      const float4* rp = reinterpret_cast<const float4*>(rs + k0);
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        rsm[j] = __shfl_sync(0xffffffffu, mine[j & 1], 4 * (j >> 1) + c);
+      for (int j = 0; j < 4; ++j) {
+        const float4 r4 = rp[j];
+        rsm[4 * j] = r4.x; rsm[4 * j + 1] = r4.y; rsm[4 * j + 2] = r4.z; rsm[4 * j + 3] = r4.w;
+      }
     } else {
 #pragma unroll
       for (int j = 0; j < 16; ++j) { sm[j] = 1.f; rsm[j] = 1.f; }
@@ -282,7 +293,7 @@ static int launch_act_int4_mt(const void* x, const void* smooth, const void* dow
   auto C = static_cast<uint8_t*>(codes);
   auto A = static_cast<__half*>(ascale);
   auto L = static_cast<__nv_bfloat16*>(la);
-  const size_t smem = (size_t)kActWarps * 16 * MT * rank_pad * sizeof(float);
+  const size_t smem = ((size_t)K + (size_t)kActWarps * 16 * MT * rank_pad) * sizeof(float);
 #define GWB_ACT_CASE(RPAD, NBV)                                                              \
   case RPAD: {                                                                               \
     auto k = act_int4_kernel<NBV, MMA_FORM, MT>;                                             \
@@ -306,8 +317,8 @@ static int launch_act_int4_mt(const void* x, const void* smooth, const void* dow
 int launch_act_int4(const void* x, const void* smooth, const void* down_t, void* codes,
                     void* ascale, void* la, int M, int K, int rank_pad, bool mma_form,
                     cudaStream_t st) {
-  // two row tiles per CTA when that still gives every SM a CTA
-  const bool two = false;   // one m16 row tile per CTA measured fastest
+  // one m16 row tile per CTA measured fastest (M = 4608 and M = 16896)
+  const bool two = false;
   if (mma_form)
     return two ? launch_act_int4_mt<true, 2>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st)
                : launch_act_int4_mt<true, 1>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st);
