@@ -514,12 +514,21 @@ nvfp4_amax_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __re
 // e2m1 magnitude code of |q| with the reference's rounding: the number of the
 // bounds 0.25 0.75 1.25 1.75 2.5 3.5 5.0 strictly below |q|, plus one when
 // |q| is exactly 0.75, 1.75 or 2.5.
-__device__ __forceinline__ uint32_t e2m1_code(float q) {
-  const float a = fabsf(q);
-  uint32_t c = (a > 0.25f) + (a > 0.75f) + (a > 1.25f) + (a > 1.75f) + (a > 2.5f) +
-               (a > 3.5f) + (a > 5.0f);
-  c += (a == 0.75f) | (a == 1.75f) | (a == 2.5f);
-  return c | (q < 0.0f ? 8u : 0u);
+// (sign bit set when q < 0.) Two such codes (a in the low nibble) come from
+// the hardware conversion: cvt.rn.satfinite.e2m1x2.f32 rounds to nearest-even and
+// saturates at 6, which is the rule above except at the ties |q| = 2.5 and
+// 3.5 (the reference takes 3.0 for both, nearest-even takes 2.0 and 4.0) and
+// at q = -0 (the reference sets no sign bit); those three cases are patched.
+__device__ __forceinline__ uint32_t e2m1x2_code(float a, float b) {
+  a = __fadd_rn(a, 0.0f);   // -0 -> +0
+  b = __fadd_rn(b, 0.0f);
+  uint32_t r;
+  asm("{ .reg .b8 t;\n\t cvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\t cvt.u32.u8 %0, t;\n\t}"
+      : "=r"(r) : "f"(b), "f"(a));
+  const float aa = fabsf(a), ab = fabsf(b);
+  if (aa == 2.5f || aa == 3.5f) r = (r & 0xF0u) | 5u | (a < 0.0f ? 8u : 0u);
+  if (ab == 2.5f || ab == 3.5f) r = (r & 0x0Fu) | ((5u | (b < 0.0f ? 8u : 0u)) << 4);
+  return r;
 }
 
 __global__ void __launch_bounds__(256)
@@ -562,9 +571,10 @@ act_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __res
     const float rden = __frcp_rn(den);
     uint32_t w0 = 0, w1 = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      w0 |= e2m1_code(div_rn(v[j], den, rden)) << (4 * j);
-      w1 |= e2m1_code(div_rn(v[8 + j], den, rden)) << (4 * j);
+    for (int j = 0; j < 4; ++j) {
+      w0 |= e2m1x2_code(div_rn(v[2 * j], den, rden), div_rn(v[2 * j + 1], den, rden)) << (8 * j);
+      w1 |= e2m1x2_code(div_rn(v[8 + 2 * j], den, rden), div_rn(v[9 + 2 * j], den, rden))
+            << (8 * j);
     }
     *reinterpret_cast<uint2*>(codes + (size_t)row * (K / 2) + c * 8) = make_uint2(w0, w1);
     const size_t off = ((size_t)(row >> 7) * ncb + (c >> 2)) * 512 + (row & 31) * 16 +

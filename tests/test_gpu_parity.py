@@ -243,6 +243,28 @@ def test_nvfp4_quant_bit_exact(cuda_ready, m, k, smooth):
     assert torch.equal(sblk.cpu(), want_blk)
 
 
+def test_nvfp4_quant_rounding_ties(cuda_ready):
+    """Codes at the e2m1 rounding ties and at -0: with amax = 2688 the
+    per-tensor s2 is 1, and a 16-block whose largest magnitude is 6 gets the
+    block scale 1, so q = x exactly. The reference's rule (count of bounds
+    below |q|, plus one at 0.75, 1.75 and 2.5; sign bit when q < 0) differs
+    from round-to-nearest-even at 2.5 and 3.5."""
+    ties = [6.0, 2.5, 3.5, -2.5, -3.5, -0.0, 0.25, 0.75, 1.25, 1.75, 5.0, -0.25, -0.1,
+            0.1, -5.0, -6.0]
+    x = torch.zeros(128, 64)
+    x[0, :16] = torch.tensor(ties)
+    x[1, :16] = -torch.tensor(ties)
+    x[2, 16] = 2688.0
+    x[3, 32:48] = torch.tensor(ties) * 0.5
+    x = x.to(torch.bfloat16)
+    codes, sblk, work = ops.nvfp4_quant(x.cuda(), None)
+    s2 = O.nvfp4_s2(x)
+    want_codes, want_blk = O.quant_nvfp4(x, s2)
+    assert float(s2) == 1.0
+    assert torch.equal(codes.cpu(), want_codes)
+    assert torch.equal(sblk.cpu(), want_blk)
+
+
 @pytest.mark.parametrize("m,k,n,rank,per_channel", [(128, 256, 256, 0, False),
                                                     (300, 3072, 256, 32, False),
                                                     (512, 1024, 768, 32, True),
