@@ -389,9 +389,12 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
                 ops.svdq_w4a4_gemm(c, a, p["w_q8"], p["w_scale_k8"], la, p["proj_up_pad"],
                                    mod.bias.detach(), gelu)
             elif kind == "nvfp4":
-                c, sb_, wk = ops.nvfp4_quant(xb, mod.smooth_factor)
-                la, upp = ops.nvfp4_lowrank_operands(xb, *ops.nvfp4_lowrank_prepare(
-                    mod.proj_down, mod.proj_up, mod.weight_scale_2), wk)
+                # the module's own path: load-time low-rank forms cached by a
+                # first forward, la from the amax pass
+                if mod._up_pad is None:
+                    mod(xb)
+                c, sb_, wk, la = ops.nvfp4_quant_lowrank(xb, mod.smooth_factor, mod._up_pad[0])
+                upp = (mod._up_pad[1] / wk[1]).to(torch.bfloat16)
                 e[1].record()
                 ops.nvfp4_gemm(c, sb_, wk, mod.weight, mod.weight_scale, mod.weight_scale_2,
                                la, upp, mod.bias.detach())
@@ -419,9 +422,8 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
             gemm_call = lambda: ops.svdq_w4a4_gemm(c, a, p["w_q8"], p["w_scale_k8"], la,  # noqa: E731
                                                    p["proj_up_pad"], mod.bias.detach(), gelu)
         elif kind == "nvfp4":
-            c, sb_, wk = ops.nvfp4_quant(xb, mod.smooth_factor)
-            la, upp = ops.nvfp4_lowrank_operands(xb, *ops.nvfp4_lowrank_prepare(
-                mod.proj_down, mod.proj_up, mod.weight_scale_2), wk)
+            c, sb_, wk, la = ops.nvfp4_quant_lowrank(xb, mod.smooth_factor, mod._up_pad[0])
+            upp = (mod._up_pad[1] / wk[1]).to(torch.bfloat16)
             gemm_call = lambda: ops.nvfp4_gemm(c, sb_, wk, mod.weight, mod.weight_scale,  # noqa: E731
                                                mod.weight_scale_2, la, upp, mod.bias.detach())
         elif kind == "fp8":

@@ -179,6 +179,16 @@ int gwb_fp8_linear(const void* x, const void* w_q, const float* w_scale, const v
 int gwb_nvfp4_quant(const void* x, const void* smooth, int64_t M, int64_t K, void* codes,
                     void* sblk, float* work, void* stream);
 
+/* gwb_nvfp4_quant plus the low-rank down-projection of the same
+ * `SvdqLinear.forward` (la = x2 @ proj_down on raw x, svdq_native.py:153),
+ * computed in the pass that takes amax, so x is read twice instead of three
+ * times: down_t bf16 [rank_pad, K] (proj_down transposed, zero-padded rows),
+ * la bf16 [M, rank_pad] = bf16(x · proj_down) with f32 accumulation.
+ * rank_pad in {16, 32, 48, 64}; other arguments as gwb_nvfp4_quant. */
+int gwb_nvfp4_quant_lowrank(const void* x, const void* smooth, const void* down_t, int64_t M,
+                            int64_t K, int rank_pad, void* codes, void* sblk, float* work,
+                            void* la, void* stream);
+
 /* Replaces `_gemm_w4a4` (`torch._scaled_mm` on float4_e2m1fn_x2 with blocked
  * scales, reference w4a4.py:173-180) and the rest of the NVFP4
  * `SvdqLinear.forward` (svdq_native.py:148-155): y = (A·B^T with block scales)

@@ -593,6 +593,102 @@ act_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __res
   }
 }
 
+// amax |bf16(x / smooth)| (as nvfp4_amax_kernel) fused with the low-rank
+// down-projection la = bf16(x · L1) on RAW x, so the NVFP4 lane reads x twice
+// per call (this pass and the quantiser) instead of three times. Layout and
+// MMA fragments as act_int4_kernel: 16 rows per CTA, 8 warps splitting K in
+// 64-wide chunks, lane (g, c) on rows g and g + 8 and the 16 columns
+// 64 kc + 16 c; k is permuted alike in the x and L1 fragments (logical
+// positions (2c, 2c+1 | 2c+8, 2c+9) of k16-step s are physical
+// 16c + 4s + (0, 1 | 2, 3)); the per-warp partial sums of la are added in a
+// fixed order through shared memory (deterministic).
+template <int NB>
+__global__ void __launch_bounds__(256, 2)
+nvfp4_amax_la_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ smooth,
+                     const float* __restrict__ rsm, const __nv_bfloat16* __restrict__ down_t,
+                     unsigned int* __restrict__ amax_bits, __nv_bfloat16* __restrict__ la, int M,
+                     int K) {
+  constexpr int RP = NB * 8, ROWS = 16, WARPS = 8;
+  __shared__ float red[WARPS][ROWS][RP];
+  __shared__ float wmax[WARPS];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int nchunks = K / 64;
+  int rows[2];
+  bool valid[2];
+  const uint4* xr[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    rows[h] = blockIdx.x * ROWS + 8 * h + g;
+    valid[h] = rows[h] < M;
+    xr[h] = reinterpret_cast<const uint4*>(x + (size_t)(valid[h] ? rows[h] : 0) * K);
+  }
+  float acc[NB][4];
+#pragma unroll
+  for (int j = 0; j < NB; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  float m = 0.f;
+  for (int kc = warp; kc < nchunks; kc += WARPS) {
+    const int k0 = kc * 64 + 16 * c;
+    uint32_t w[2][8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 p0 = valid[h] ? __ldg(xr[h] + k0 / 8) : make_uint4(0, 0, 0, 0);
+      const uint4 p1 = valid[h] ? __ldg(xr[h] + k0 / 8 + 1) : make_uint4(0, 0, 0, 0);
+      w[h][0] = p0.x; w[h][1] = p0.y; w[h][2] = p0.z; w[h][3] = p0.w;
+      w[h][4] = p1.x; w[h][5] = p1.y; w[h][6] = p1.z; w[h][7] = p1.w;
+      float v[8];
+      if (smooth) {
+        smooth8(p0, __ldg(reinterpret_cast<const uint4*>(smooth + k0)), rsm + k0, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(v[e]));
+        smooth8(p1, __ldg(reinterpret_cast<const uint4*>(smooth + k0) + 1), rsm + k0 + 8, v);
+      } else {
+        raw8(p0, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(v[e]));
+        raw8(p1, v);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(v[e]));
+    }
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      const uint4* dp = reinterpret_cast<const uint4*>(down_t + (size_t)(8 * j + g) * K + k0);
+      const uint4 d0 = __ldg(dp), d1 = __ldg(dp + 1);
+      const uint32_t dw[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const uint32_t a[4] = {w[0][2 * s], w[1][2 * s], w[0][2 * s + 1], w[1][2 * s + 1]};
+        mma_bf16_16816(acc[j], a, dw[2 * s], dw[2 * s + 1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) wmax[warp] = m;
+#pragma unroll
+  for (int j = 0; j < NB; ++j) {
+    red[warp][g][8 * j + 2 * c] = acc[j][0];
+    red[warp][g][8 * j + 2 * c + 1] = acc[j][1];
+    red[warp][g + 8][8 * j + 2 * c] = acc[j][2];
+    red[warp][g + 8][8 * j + 2 * c + 1] = acc[j][3];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = wmax[0];
+    for (int w2 = 1; w2 < WARPS; ++w2) b = fmaxf(b, wmax[w2]);
+    atomicMax(amax_bits, __float_as_uint(b));
+  }
+  for (int i = threadIdx.x; i < ROWS * RP; i += blockDim.x) {
+    const int r = i / RP, col = i % RP;
+    float sum = 0.f;
+#pragma unroll
+    for (int w2 = 0; w2 < WARPS; ++w2) sum += red[w2][r][col];
+    const int row = blockIdx.x * ROWS + r;
+    if (row < M) la[(size_t)row * RP + col] = __float2bfloat16_rn(sum);
+  }
+}
+
 int launch_act_nvfp4(const void* x, const void* smooth, float* work, void* codes, void* sblk,
                      int M, int K, cudaStream_t st) {
   if (cudaMemsetAsync(work, 0, sizeof(float), st) != cudaSuccess) return GWB_E_LAUNCH;
@@ -612,6 +708,34 @@ int launch_act_nvfp4(const void* x, const void* smooth, float* work, void* codes
   act_nvfp4_kernel<<<(int)blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
                                                  static_cast<const __nv_bfloat16*>(smooth), work,
                                                  static_cast<uint8_t*>(codes),
+                                                 static_cast<uint8_t*>(sblk), M, K);
+  return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
+}
+
+int launch_act_nvfp4_lowrank(const void* x, const void* smooth, const void* down_t, float* work,
+                             void* codes, void* sblk, void* la, int M, int K, int rank_pad,
+                             cudaStream_t st) {
+  if (cudaMemsetAsync(work, 0, sizeof(float), st) != cudaSuccess) return GWB_E_LAUNCH;
+  if (smooth)
+    nvfp4_rsmooth_kernel<<<(K + 255) / 256, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(smooth), work + 4, K);
+  const dim3 grid((M + 15) / 16);
+  auto X = static_cast<const __nv_bfloat16*>(x);
+  auto Sm = static_cast<const __nv_bfloat16*>(smooth);
+  auto D = static_cast<const __nv_bfloat16*>(down_t);
+  auto A = reinterpret_cast<unsigned int*>(work);
+  auto L = static_cast<__nv_bfloat16*>(la);
+  switch (rank_pad) {
+    case 16: nvfp4_amax_la_kernel<2><<<grid, 256, 0, st>>>(X, Sm, work + 4, D, A, L, M, K); break;
+    case 32: nvfp4_amax_la_kernel<4><<<grid, 256, 0, st>>>(X, Sm, work + 4, D, A, L, M, K); break;
+    case 48: nvfp4_amax_la_kernel<6><<<grid, 256, 0, st>>>(X, Sm, work + 4, D, A, L, M, K); break;
+    case 64: nvfp4_amax_la_kernel<8><<<grid, 256, 0, st>>>(X, Sm, work + 4, D, A, L, M, K); break;
+    default: return GWB_E_SHAPE;
+  }
+  const int64_t nblk = (int64_t)M * (K / 16);
+  int64_t blocks = (nblk + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  act_nvfp4_kernel<<<(int)blocks, 256, 0, st>>>(X, Sm, work, static_cast<uint8_t*>(codes),
                                                  static_cast<uint8_t*>(sblk), M, K);
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }

@@ -220,6 +220,19 @@ int gwb_nvfp4_quant(const void* x, const void* smooth, int64_t M, int64_t K, voi
   return gwb::launch_act_nvfp4(x, smooth, work, codes, sblk, (int)M, (int)K, S(stream));
 }
 
+int gwb_nvfp4_quant_lowrank(const void* x, const void* smooth, const void* down_t, int64_t M,
+                            int64_t K, int rank_pad, void* codes, void* sblk, float* work,
+                            void* la, void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  if (!fits_int(M) || !fits_int(K) || K % 64 || K == 0) return GWB_E_SHAPE;
+  if (rank_pad != 16 && rank_pad != 32 && rank_pad != 48 && rank_pad != 64) return GWB_E_SHAPE;
+  if (!al16(x) || !al16(codes) || (smooth && !al16(smooth)) || !sblk || !work || !al16(work) ||
+      !al16(down_t) || !la)
+    return GWB_E_ALIGN;
+  return gwb::launch_act_nvfp4_lowrank(x, smooth, down_t, work, codes, sblk, la, (int)M, (int)K,
+                                       rank_pad, S(stream));
+}
+
 int gwb_nvfp4_gemm(const void* a_codes, const void* a_sblk, const float* a_work,
                    const void* w_codes, const void* w_sblk, const float* w_scale_2,
                    int ws2_per_channel, const void* la, const void* proj_up, const void* bias,

@@ -28,6 +28,9 @@ int launch_act_fp8(const void* x, void* q, void* scale, int M, int K, cudaStream
 // e4m3 scales (padding rows written as zeros).
 int launch_act_nvfp4(const void* x, const void* smooth, float* work, void* codes, void* sblk,
                      int M, int K, cudaStream_t st);
+int launch_act_nvfp4_lowrank(const void* x, const void* smooth, const void* down_t, float* work,
+                             void* codes, void* sblk, void* la, int M, int K, int rank_pad,
+                             cudaStream_t st);
 
 struct NvFp4Args {
   const void* a_codes;     // u8 [M, K/2] packed e2m1 (element 2j low nibble)

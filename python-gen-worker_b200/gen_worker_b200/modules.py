@@ -191,9 +191,9 @@ class SvdqNvfp4Linear(nn.Module):
     u8 [N, K/2] (packed e2m1), ``weight_scale`` e4m3 [blocked numel] (cuBLAS
     blocked layout), ``weight_scale_2`` f32 [1, N] or [1, 1], optional
     ``smooth_factor`` [K], ``proj_down`` [K, r], ``proj_up`` [N, r], ``bias``.
-    Forward: the smoothing divide, per-tensor ``s2`` and NVFP4 activation
-    codes in two native launches, ``la = x · proj_down`` (bf16 on raw x, as
-    the reference), then one block-scaled tcgen05 GEMM whose accumulator
+    Forward: the smoothing divide, per-tensor ``s2`` with ``la = x ·
+    proj_down`` (bf16 on raw x, as the reference) in the same pass, the NVFP4
+    activation codes in a second pass, then one block-scaled tcgen05 GEMM whose accumulator
     starts from the low-rank product (up-projection divided by
     ``weight_scale_2 · s2``) and ends with ``· s2 · weight_scale_2 + bias``."""
     _cozy_svdq_linear = True
@@ -250,13 +250,18 @@ class SvdqNvfp4Linear(nn.Module):
         x2 = x.reshape(-1, self.in_features)
         if not x2.is_contiguous():
             x2 = x2.contiguous()
-        codes, sblk, work = ops.nvfp4_quant(x2, self.smooth_factor)
         la = up = None
         if self.rank:
             if self._up_pad is None:
-                self._up_pad = ops.nvfp4_lowrank_prepare(self.proj_down, self.proj_up,
-                                                         self.weight_scale_2)
-            la, up = ops.nvfp4_lowrank_operands(x2, self._up_pad[0], self._up_pad[1], work)
+                down_pad, up_over_ws2 = ops.nvfp4_lowrank_prepare(self.proj_down, self.proj_up,
+                                                                  self.weight_scale_2)
+                self._up_pad = (down_pad.t().contiguous(), up_over_ws2)
+            # la from the amax pass (x is read twice per call, not three times)
+            codes, sblk, work, la = ops.nvfp4_quant_lowrank(x2, self.smooth_factor,
+                                                            self._up_pad[0])
+            up = (self._up_pad[1] / work[1]).to(torch.bfloat16)
+        else:
+            codes, sblk, work = ops.nvfp4_quant(x2, self.smooth_factor)
         y = ops.nvfp4_gemm(codes, sblk, work, self.weight, self.weight_scale,
                            self.weight_scale_2, la, up,
                            self.bias.detach() if self.bias is not None else None)

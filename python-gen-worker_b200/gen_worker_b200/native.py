@@ -50,6 +50,8 @@ _SIGNATURES = {
     "gwb_w8a8_quant": [c_void_p, c_i64, c_i64, c_void_p, c_void_p, c_void_p],
     "gwb_fp8_quant": [c_void_p, c_i64, c_i64, c_void_p, c_void_p, c_void_p],
     "gwb_nvfp4_quant": [c_void_p, c_void_p, c_i64, c_i64, c_void_p, c_void_p, c_void_p, c_void_p],
+    "gwb_nvfp4_quant_lowrank": [c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_int, c_void_p,
+                                c_void_p, c_void_p, c_void_p, c_void_p],
     "gwb_nvfp4_gemm": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                        c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_int, c_void_p,
                        c_void_p],

@@ -355,6 +355,38 @@ def _(x2, smooth):
             x2.new_empty(4 + k, dtype=torch.float32))
 
 
+@torch.library.custom_op("gwb200::nvfp4_quant_lowrank", mutates_args=())
+def nvfp4_quant_lowrank(x2: torch.Tensor, smooth: Optional[torch.Tensor], down_t: torch.Tensor
+                        ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """:func:`nvfp4_quant` plus ``la = bf16(x2 · proj_down)`` on raw x from the
+    same pass over x: down_t bf16 [rank_pad, K] -> (codes, blocked scales,
+    work, la bf16 [M, rank_pad])."""
+    _need(x2, "x2", torch.bfloat16, 2)
+    _need(smooth, "smooth", torch.bfloat16, 1)
+    _need(down_t, "down_t", torch.bfloat16, 2)
+    m, k = x2.shape
+    rp = int(down_t.shape[0])
+    if int(down_t.shape[1]) != k:
+        raise SvdqB200Error(f"down_t K {down_t.shape[1]} != activation K {k}")
+    codes = torch.empty(m, k // 2, dtype=torch.uint8, device=x2.device)
+    sblk = torch.empty(nvfp4_blocked_numel(m, k), dtype=torch.uint8, device=x2.device)
+    work = torch.empty(4 + k, dtype=torch.float32, device=x2.device)
+    la = torch.empty(m, rp, dtype=torch.bfloat16, device=x2.device)
+    native.check(native.require().gwb_nvfp4_quant_lowrank(
+        x2.data_ptr(), _ptr(smooth), down_t.data_ptr(), m, k, rp, codes.data_ptr(),
+        sblk.data_ptr(), work.data_ptr(), la.data_ptr(), _stream()), "nvfp4_quant_lowrank")
+    return codes, sblk, work, la
+
+
+@nvfp4_quant_lowrank.register_fake
+def _(x2, smooth, down_t):
+    m, k = x2.shape
+    return (x2.new_empty(m, k // 2, dtype=torch.uint8),
+            x2.new_empty(nvfp4_blocked_numel(m, k), dtype=torch.uint8),
+            x2.new_empty(4 + k, dtype=torch.float32),
+            x2.new_empty(m, down_t.shape[0], dtype=torch.bfloat16))
+
+
 @torch.library.custom_op("gwb200::nvfp4_gemm", mutates_args=())
 def nvfp4_gemm(codes: torch.Tensor, sblk: torch.Tensor, work: torch.Tensor, w_codes: torch.Tensor,
                w_sblk: torch.Tensor, w_scale_2: torch.Tensor, la: Optional[torch.Tensor],

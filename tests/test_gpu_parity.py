@@ -243,6 +243,27 @@ def test_nvfp4_quant_bit_exact(cuda_ready, m, k, smooth):
     assert torch.equal(sblk.cpu(), want_blk)
 
 
+@pytest.mark.parametrize("m,k,rank,smooth", [(300, 3072, 32, True), (128, 512, 16, False),
+                                            (1000, 1024, 64, True)])
+def test_nvfp4_quant_lowrank_matches_separate_passes(cuda_ready, m, k, rank, smooth):
+    """The fused amax + down-projection pass: codes, scales and s2 identical
+    to gwb_nvfp4_quant, la = bf16(x · proj_down) on raw x within bf16
+    rounding of the exact product."""
+    gen = torch.Generator().manual_seed(m + k)
+    x = O.synth_activation(m, k, seed=m)
+    sm = (torch.rand(k, generator=gen) + 0.5).to(torch.bfloat16) if smooth else None
+    down = (torch.randn(k, rank, generator=gen) * 0.05).to(torch.bfloat16)
+    down_t = down.t().contiguous().cuda()
+    smc = None if sm is None else sm.cuda()
+    c1, b1, w1, la = ops.nvfp4_quant_lowrank(x.cuda(), smc, down_t)
+    c0, b0, w0 = ops.nvfp4_quant(x.cuda(), smc)
+    assert torch.equal(c1, c0) and torch.equal(b1, b0)
+    assert torch.equal(w1[:2], w0[:2])
+    want = x.double() @ down.double()
+    assert O.rel_l2(la.cpu(), want) <= 4e-3
+    assert native.device_error() == 0
+
+
 def test_nvfp4_quant_rounding_ties(cuda_ready):
     """Codes at the e2m1 rounding ties and at -0: with amax = 2688 the
     per-tensor s2 is 1, and a 16-block whose largest magnitude is 6 gets the
