@@ -72,12 +72,29 @@ __device__ __forceinline__ uint32_t q4x2(float2 v, float2 s, float2 rs) {
          ((m1 | ((q.y < 0.0f && m1 != 0u) ? 8u : 0u)) << 4);
 }
 
+// GEMM operand bytes (e4m3 of q * 2^-9: sign bit 7, magnitude in bits 0-2)
+// of clamp(rint(v/s), -7, 7) for a pair. The magnitude is non-zero exactly
+// when |v/s| > 0.5 (0.5 rounds to even 0), so the sign bit is set when
+// v/s < -0.5: no separate test of the magnitude.
+__device__ __forceinline__ void q8x2(float2 v, float2 s, float2 rs, uint32_t& b0, uint32_t& b1) {
+  const float2 q = div2_rn(v, s, rs);
+  const float2 m = __fadd2_rn(make_float2(fminf(fabsf(q.x), 7.0f), fminf(fabsf(q.y), 7.0f)),
+                              make_float2(8388608.0f, 8388608.0f));
+  b0 = (__float_as_uint(m.x) & 7u) | (q.x < -0.5f ? 0x80u : 0u);
+  b1 = (__float_as_uint(m.y) & 7u) | (q.y < -0.5f ? 0x80u : 0u);
+}
+
 // Quantise 16 consecutive raw elements (8 bf16x2 words) of one row-group
 // segment: smoothing divide rounded to bf16, then the group's INT4 codes.
-// The 4 lanes of a quad hold the 64 elements of one group.
+// The 4 lanes of a quad hold the 64 elements of one group. E4M3: write the
+// GEMM operand form (elements 0 2 4 6 | 1 3 5 7 | 8 10 12 14 | 9 11 13 15
+// as e4m3 bytes, the order unpack8_e4m3 gives) into lo, hi, e2, e3;
+// otherwise the packed sign-magnitude nibbles into lo, hi.
+template <bool E4M3 = false>
 __device__ __forceinline__ void quant_seg16(const uint32_t (&xw)[8], const float (&sm)[16],
                                             const float (&rsm)[16], bool has_smooth,
-                                            uint32_t& lo, uint32_t& hi, __half& scale_out) {
+                                            uint32_t& lo, uint32_t& hi, __half& scale_out,
+                                            uint32_t* e23 = nullptr) {
   float2 v[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -103,10 +120,26 @@ __device__ __forceinline__ void quant_seg16(const uint32_t (&xw)[8], const float
   const float2 s2 = make_float2(s, s), rs2 = make_float2(rs, rs);
   lo = 0;
   hi = 0;
+  if constexpr (E4M3) {
+    uint32_t e2 = 0, e3 = 0;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) lo |= q4x2(v[j], s2, rs2) << (8 * j);
+    for (int j = 0; j < 4; ++j) {
+      uint32_t b0, b1;
+      q8x2(v[j], s2, rs2, b0, b1);
+      lo |= b0 << (8 * j);
+      hi |= b1 << (8 * j);
+      q8x2(v[4 + j], s2, rs2, b0, b1);
+      e2 |= b0 << (8 * j);
+      e3 |= b1 << (8 * j);
+    }
+    e23[0] = e2;
+    e23[1] = e3;
+  } else {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) hi |= q4x2(v[4 + j], s2, rs2) << (8 * j);
+    for (int j = 0; j < 4; ++j) lo |= q4x2(v[j], s2, rs2) << (8 * j);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) hi |= q4x2(v[4 + j], s2, rs2) << (8 * j);
+  }
   scale_out = sh;
 }
 
@@ -219,16 +252,14 @@ act_int4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
     for (int t = 0; t < MT; ++t)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        uint32_t lo, hi;
+        uint32_t lo, hi, e23[2];
         __half sc;
-        quant_seg16(w[t][h], sm, rsm, has_smooth, lo, hi, sc);
+        quant_seg16<MMA_FORM>(w[t][h], sm, rsm, has_smooth, lo, hi, sc, e23);
         if (valid[t][h]) {
           const int row = rows[t][h];
           if constexpr (MMA_FORM) {
-            uint4 o;
-            unpack8_e4m3(lo, o.x, o.y);
-            unpack8_e4m3(hi, o.z, o.w);
-            *reinterpret_cast<uint4*>(codes + (size_t)row * K + k0) = o;
+            *reinterpret_cast<uint4*>(codes + (size_t)row * K + k0) =
+                make_uint4(lo, hi, e23[0], e23[1]);
             if (c == 0)
               *reinterpret_cast<uint4*>(ascale + ((size_t)kc * M + row) * 8) =
                   make_uint4(__half_as_ushort(sc), 0u, 0u, 0u);
