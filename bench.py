@@ -26,6 +26,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from typing import Optional
 from pathlib import Path
@@ -44,22 +45,30 @@ DUAL = [("qkv", HIDDEN, 9216, False), ("out", HIDDEN, HIDDEN, False),
 SINGLE = [("qkv_mlp", HIDDEN, 21504, False), ("out", 15360, HIDDEN, False)]
 N_DUAL, N_SINGLE = 19, 38
 INT8_DENSE_PEAK_TOPS = 4500.0   # B200 datasheet dense INT8 / FP8, for context
-# DRAM bytes (read + write) of one gemm_w4a4_kernel launch on the cfg3 shape
-# (M 4608, K 3072, N 3072) from one ncu capture (profiles/gemm_w4a4_cfg3.md);
-# its algorithmic bytes are 29.5 MB (a_q8 + w_q8 + both scale-operand arrays).
-GEMM_TRAFFIC_CFG3_BYTES = 30.29e6 + 0.42e6
+PEAKS_FILE = ROOT / "profiles" / "tensor_peaks_b200.json"
 
 
 def tensor_peak_tops() -> tuple[float, str]:
-    """The e4m3 MMA (tcgen05 kind::f8f6f4) issues at twice the bf16 rate, so
-    the roofline denominator is 2x the measured sustained bf16 cuBLAS figure
-    (the GEMM is timed inside a long step)."""
+    """Roofline denominator of the W4A4 GEMM, which issues e4m3 MMAs
+    (kind::f8f6f4): the measured sustained e4m3 ``torch._scaled_mm`` 8192^3
+    ceiling (``--case peaks`` writes it), because the GEMM is timed inside a
+    long step. Falls back to 2 x the driver's measured sustained bf16 figure
+    (the e4m3 MMA issues at twice the bf16 rate), then to the recipe's
+    fallback."""
+    try:
+        pk = json.loads(PEAKS_FILE.read_text())
+        return float(pk["e4m3_tops_sustained"]), \
+            "measured sustained e4m3 torch._scaled_mm 8192^3 (profiles/tensor_peaks_b200.json)"
+    except (OSError, KeyError, ValueError):
+        pass
     try:
         mp = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
         return 2.0 * float(mp["bf16_tflops_sustained"]), \
             "2 x measured sustained bf16 (MEASURED_PEAKS.json): e4m3 MMA rate"
     except (OSError, KeyError, ValueError):
         return 2.0 * 1400.0, "2 x fallback sustained bf16 1.4 PFLOP/s: e4m3 MMA rate"
+
+
 METRIC = "W4A4 DiT-stack tokens/s (cfg4 Flux linear stack, 16896 tokens)"
 
 
@@ -330,6 +339,65 @@ def _scaled_mm_fp4_ms(codes, sblk, w_codes, w_sblk, steps: int) -> Optional[floa
         return None
 
 
+def _reference_nvfp4_lane_lb_ms(xb, mod, codes, sblk, steps: int) -> Optional[float]:
+    """Lower bound of the reference's NVFP4 ``SvdqLinear.forward``
+    (``svdq_native.py:140-156``) on this GPU: every op of its chain except
+    the activation quantiser kernel, issued as the reference issues them:
+    the smoothing divide, the per-tensor amax for s2, ``torch._scaled_mm``
+    FP4 (cuBLASLt), the ``s2 · weight_scale_2`` multiply, the two low-rank
+    matmuls on raw x and the bias add. Replayed from a CUDA graph (device
+    time). The quantiser is left out, so the reference lane can only be
+    slower than this figure."""
+    fp4 = getattr(torch, "float4_e2m1fn_x2", None)
+    if fp4 is None:
+        return None
+    w2 = mod.weight_scale_2.float().reshape(1, -1)
+    down = mod.proj_down
+    up = mod.proj_up
+    bias = mod.bias.detach() if mod.bias is not None else None
+
+    def call():
+        xs = (xb / mod.smooth_factor).to(torch.bfloat16)
+        s2 = (xs.abs().amax().float() / (6.0 * 448.0)).clamp(min=1e-12)
+        y0 = torch._scaled_mm(codes.view(fp4), mod.weight.view(fp4).t(),
+                              scale_a=sblk.view(torch.float8_e4m3fn),
+                              scale_b=mod.weight_scale.view(torch.float8_e4m3fn),
+                              out_dtype=torch.bfloat16)
+        y = (y0.float() * (s2 * w2)).to(torch.bfloat16)
+        if down is not None:
+            y = y + (xb @ down) @ up.t()
+        if bias is not None:
+            y = y + bias
+        return y
+    try:
+        return graph_ms(call, steps)
+    except Exception:  # noqa: BLE001 - context figure only
+        return None
+
+
+def _reference_fp8_lane_lb_ms(q, scale, mod, gelu: bool, steps: int) -> Optional[float]:
+    """Lower bound of the reference's ``Fp8ScaledLinear.forward`` rowwise
+    (``w8a8.py:359-381``): its ``torch._scaled_mm`` with per-token and
+    per-channel scales and the bias (cuBLASLt), then the GELU(tanh) that
+    diffusers applies after the projection; the activation quantiser
+    (``_quant_src``) is left out. CUDA-graph device time."""
+    wq = mod.weight.view(torch.float8_e4m3fn)
+    ws = mod.weight_scale.reshape(1, -1).float().contiguous()
+    sa = scale.reshape(-1, 1).float().contiguous()
+    bias = mod.bias.detach() if mod.bias is not None else None
+
+    def call():
+        y = torch._scaled_mm(q.view(torch.float8_e4m3fn), wq.t(), scale_a=sa, scale_b=ws,
+                             bias=bias, out_dtype=torch.bfloat16)
+        if gelu:
+            y = torch.nn.functional.gelu(y, approximate="tanh")
+        return y
+    try:
+        return graph_ms(call, steps)
+    except Exception:  # noqa: BLE001 - context figure only
+        return None
+
+
 def run_case(name: str, steps: int, warmup: int) -> dict:
     """Time one BASELINE config's linears (quantiser + GEMM, the module's two
     launches) with CUDA events on the current stream; inputs are resident in
@@ -439,8 +507,12 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
         # torch ops), replayed from a CUDA graph: its device time
         module_dev_ms = graph_ms(lambda: mod(xb), steps)
         lib_ms = None
+        ref_lb_ms = None
         if kind == "nvfp4":
             lib_ms = _scaled_mm_fp4_ms(c, sb_, mod.weight, mod.weight_scale, 4 * steps)
+            ref_lb_ms = _reference_nvfp4_lane_lb_ms(xb, mod, c, sb_, steps)
+        elif kind == "fp8":
+            ref_lb_ms = _reference_fp8_lane_lb_ms(q, s_, mod, gelu, steps)
         ops_ = 2.0 * m * n * k
         act_bytes = m * k * 2 + (m * k // 2 + m * k // 4 + m * r * 2 if kind == "w4a4"
                                  else m * k + m * 4)
@@ -451,7 +523,10 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
                      "gemm_b2b_ms": b2b_ms, "gemm_b2b_tops": ops_ / (b2b_ms / 1e3) / 1e12,
                      "module_graph_ms": module_dev_ms,
                      "cublaslt_scaled_mm_ms": lib_ms,
-                     "cublaslt_scaled_mm_tops": (ops_ / (lib_ms / 1e3) / 1e12) if lib_ms else None})
+                     "cublaslt_scaled_mm_tops": (ops_ / (lib_ms / 1e3) / 1e12) if lib_ms else None,
+                     "reference_lane_lower_bound_ms": ref_lb_ms,
+                     "speedup_vs_reference_lane_lower_bound":
+                         (ref_lb_ms / module_dev_ms) if ref_lb_ms else None})
     total_ms = sum(r_["ms"] for r_ in rows)
     total_ops = sum(2.0 * r_["M"] * r_["N"] * r_["K"] for r_ in rows)
     tops = total_ops / (total_ms / 1e3) / 1e12
@@ -460,6 +535,77 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
             "frac_int8_peak": tops / INT8_DENSE_PEAK_TOPS,
             "linears": rows, "steps": steps, "warmup": warmup,
             "l2": "256 MB flush between iterations"}
+
+
+# --------------------------------------------------------------------------- tensor ceilings
+def run_peaks(seconds: float = 4.0) -> dict:
+    """Measured tensor-core ceilings on this GPU, with the protocol of the
+    driver's bf16 figure: an 8192^3 library GEMM timed with CUDA events,
+    best of 10 (burst) and back to back for ``seconds`` (sustained, under the
+    power cap), nvidia-smi clocks sampled during the sustained loops. Lanes:
+    bf16 ``torch.matmul``; e4m3 ``torch._scaled_mm`` (tensorwise scales, the
+    same kind::f8f6f4 rate the W4A4 GEMM issues at); INT8 ``torch._int_mm``;
+    NVFP4 ``torch._scaled_mm`` with 16-element e4m3 block scales."""
+    dev = torch.device("cuda", 0)
+    n = 8192
+    g = torch.Generator(device=dev).manual_seed(0)
+    ops_ = 2.0 * n ** 3
+    lanes = {}
+    a16 = torch.randn(n, n, generator=g, device=dev).to(torch.bfloat16)
+    b16 = torch.randn(n, n, generator=g, device=dev).to(torch.bfloat16)
+    lanes["bf16"] = lambda: torch.matmul(a16, b16)
+    a8 = (torch.randn(n, n, generator=g, device=dev) * 8).to(torch.float8_e4m3fn)
+    b8 = (torch.randn(n, n, generator=g, device=dev) * 8).to(torch.float8_e4m3fn)
+    one = torch.ones((), device=dev)
+    lanes["e4m3"] = lambda: torch._scaled_mm(a8, b8.t(), scale_a=one, scale_b=one,
+                                             out_dtype=torch.bfloat16)
+    ai = torch.randint(-127, 128, (n, n), generator=g, device=dev, dtype=torch.int8)
+    bi = torch.randint(-127, 128, (n, n), generator=g, device=dev, dtype=torch.int8)
+    lanes["int8"] = lambda: torch._int_mm(ai, bi.t())
+    fp4 = getattr(torch, "float4_e2m1fn_x2", None)
+    if fp4 is not None:
+        a4 = torch.randint(0, 256, (n, n // 2), generator=g, device=dev, dtype=torch.uint8)
+        b4 = torch.randint(0, 256, (n, n // 2), generator=g, device=dev, dtype=torch.uint8)
+        sa4 = torch.full((n * n // 16,), 1.0, device=dev).to(torch.float8_e4m3fn)
+        lanes["nvfp4"] = lambda: torch._scaled_mm(a4.view(fp4), b4.view(fp4).t(), scale_a=sa4,
+                                                  scale_b=sa4, out_dtype=torch.bfloat16)
+    out = {"metric": "tensor-core ceilings, 8192^3 library GEMMs", "unit": "TOP/s",
+           "how": ("CUDA events; burst = best of 10 single launches after 3 warm-up; "
+                   f"sustained = back to back for {seconds:.0f} s"), "lanes": {}}
+    clock_dir = Path(os.environ.get("GWB_CLOCKS_DIR") or tempfile.mkdtemp(prefix="gwb_clocks_"))
+    for name, fn in lanes.items():
+        try:
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            best = float("inf")
+            for _ in range(10):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                best = min(best, e0.elapsed_time(e1))
+            reps = max(10, int(seconds * 1e3 / best))
+            with ClockSampler(0, clock_dir / f"clocks_peaks_{name}.csv") as clk:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    fn()
+                e1.record()
+                torch.cuda.synchronize()
+            sus = e0.elapsed_time(e1) / reps
+            out["lanes"][name] = {"burst_tops": ops_ / (best / 1e3) / 1e12,
+                                  "sustained_tops": ops_ / (sus / 1e3) / 1e12,
+                                  "burst_ms": best, "sustained_ms": sus, "reps": reps,
+                                  "clocks": clk.summary()}
+        except Exception as exc:  # noqa: BLE001 - a lane this torch build cannot run
+            out["lanes"][name] = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+    e4 = out["lanes"].get("e4m3", {})
+    if "sustained_tops" in e4:
+        out["e4m3_tops_sustained"] = e4["sustained_tops"]
+        out["e4m3_tops_burst"] = e4["burst_tops"]
+    return out
 
 
 # --------------------------------------------------------------------------- AWQ modulation GEMV
@@ -565,7 +711,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", choices=sorted(CASES) + ["awq"], default=None,
+    ap.add_argument("--case", choices=sorted(CASES) + ["awq", "peaks"], default=None,
                     help="time one BASELINE config's linears instead of the cfg4 stack")
     args = ap.parse_args()
     world, rank, local = dist_env()
@@ -575,6 +721,8 @@ def main() -> int:
         native.require()
         if args.case == "awq":
             print(json.dumps(run_awq_case(args.steps, args.warmup)))
+        elif args.case == "peaks":
+            print(json.dumps(run_peaks()))
         else:
             print(json.dumps(run_case(args.case, args.steps, args.warmup)))
         return 0
@@ -634,7 +782,8 @@ def main() -> int:
     barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local, ROOT / "gpurun_out" / f"clocks_rank{rank}.csv") as clk:
+    clock_dir = Path(os.environ.get("GWB_CLOCKS_DIR") or tempfile.mkdtemp(prefix="gwb_clocks_"))
+    with ClockSampler(local, clock_dir / f"clocks_rank{rank}.csv") as clk:
         start.record()
         for _ in range(args.steps):
             y = run_stack(layers, x, side, timer=timer)
@@ -672,21 +821,26 @@ def main() -> int:
         gathered = torch.empty(TOKENS, HIDDEN, dtype=torch.bfloat16, device=dev)
         dist.all_gather_into_tensor(gathered, y.contiguous())
         if rank == 0:
-            # rank 0 recomputes the first 128 rows of rank 1's shard from the
-            # same seeded global inputs; rows are independent, so the sharded
-            # result must be bit-identical
+            # rank 0 recomputes 64 rows of EVERY rank's shard (32 at its start,
+            # 32 at its end) from the same seeded global inputs; rows are
+            # independent, so the sharded result must be bit-identical
             g2 = torch.Generator(device=dev).manual_seed(99)
             xf = torch.randn(TOKENS, HIDDEN, generator=g2, device=dev)
             idx2 = torch.randperm(HIDDEN, generator=g2, device=dev)[:31]
             xf[:, idx2] *= 20
-            rows = xf[m:m + 128].to(torch.bfloat16).contiguous()
             g3 = torch.Generator(device=dev).manual_seed(100)
             sf = torch.randn(TOKENS, 15360, generator=g3, device=dev)
-            side_r = sf[m:m + 128].to(torch.bfloat16).contiguous()
+            sel = torch.cat([torch.cat([torch.arange(r * m, r * m + 32),
+                                        torch.arange((r + 1) * m - 32, (r + 1) * m)])
+                             for r in range(world)]).to(dev)
+            rows = xf[sel].to(torch.bfloat16).contiguous()
+            side_r = sf[sel].to(torch.bfloat16).contiguous()
             del xf, sf
             ref = run_stack(layers, rows, side_r)
-            shard_check = ("bit-identical" if torch.equal(ref, gathered[m:m + 128])
-                           else "MISMATCH")
+            bad = [r for r in range(world)
+                   if not torch.equal(ref[64 * r:64 * (r + 1)], gathered[sel[64 * r:64 * (r + 1)]])]
+            shard_check = ("bit-identical (64 rows of each of %d shards)" % world if not bad
+                           else "MISMATCH on ranks %s" % bad)
 
     if rank == 0:
         tps = TOKENS / (ms_max / 1e3)
@@ -697,7 +851,7 @@ def main() -> int:
             "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "int8 (INT4 codes, s32 group sums, f32 promotion)", "data": "synthetic",
+            "dtype": "e4m3-encoded INT4 codes (exact), f32 group sums and promotion", "data": "synthetic",
             "config": {"workload": "cfg4 Flux DiT W4A4 linear stack, 19 dual + 38 single blocks",
                        "tokens": TOKENS, "tokens_per_rank": m, "hidden": HIDDEN, "rank": RANK,
                        "group": 64, "parallelism": f"token-shard x{world}, weights replicated",

@@ -122,7 +122,9 @@ int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_dow
  * (each part rounded up to 256); larger calls return GWB_E_CAPACITY. Calls
  * share the array: work from calls that overlap on the GPU races. The first
  * call on a device looks up the array's address; make it before any stream
- * capture. Allocates nothing. */
+ * capture. The address is cached per process and device and is not looked
+ * up again after a device reset. `stream` must belong to the current device
+ * (another device's stream returns GWB_E_SHAPE). Allocates nothing. */
 int gwb_svdq_w4a4_linear_noalloc(const void* x, const void* smooth, const void* proj_down_t,
                                  const void* w_q8, const void* w_scale_k8,
                                  const void* proj_up, const void* bias, int64_t M, int64_t N,

@@ -70,6 +70,7 @@ int gwb_svdq_w4a4_quant(const void* x, const void* smooth, const void* proj_down
   if (!fits_int(M) || !fits_int(K) || K % 64) return GWB_E_SHAPE;
   if (rank_pad < 0 || rank_pad > 64 || rank_pad % 16) return GWB_E_SHAPE;
   if (rank_pad > 0 && (!proj_down_t || !la)) return GWB_E_SHAPE;
+  if (!x || !codes || !ascale) return GWB_E_SHAPE;
   if (!al16(x) || !al16(codes) || (smooth && !al16(smooth)) ||
       (proj_down_t && !al16(proj_down_t)) || (la && !al16(la)) ||
       (reinterpret_cast<uintptr_t>(ascale) & 1u))
@@ -85,6 +86,7 @@ int gwb_svdq_w4a4_quant_mma(const void* x, const void* smooth, const void* proj_
   if (!fits_int(M) || !fits_int(K) || K % 64 || (K / 64) * M > 0x7fffffff) return GWB_E_SHAPE;
   if (rank_pad < 0 || rank_pad > 64 || rank_pad % 16) return GWB_E_SHAPE;
   if (rank_pad > 0 && (!proj_down_t || !la)) return GWB_E_SHAPE;
+  if (!x || !a_q8 || !a_scale_k8) return GWB_E_SHAPE;
   if (!al16(x) || !al16(a_q8) || !al16(a_scale_k8) || (smooth && !al16(smooth)) ||
       (proj_down_t && !al16(proj_down_t)) || (la && !al16(la)))
     return GWB_E_ALIGN;
@@ -96,6 +98,7 @@ int gwb_svdq_w4a4_scale_k8(const void* scale, int64_t R, int64_t K, void* scale_
                            void* stream) {
   if (R == 0) return GWB_SUCCESS;
   if (!fits_int(R) || !fits_int(K) || K % 64 || (K / 64) * R > 0x7fffffff) return GWB_E_SHAPE;
+  if (!scale || !scale_k8) return GWB_E_SHAPE;
   if ((reinterpret_cast<uintptr_t>(scale) & 1u) || !al16(scale_k8)) return GWB_E_ALIGN;
   return gwb::launch_scale_k8(scale, scale_k8, (int)R, (int)K, S(stream));
 }
@@ -104,6 +107,7 @@ int gwb_svdq_w4a4_weight_expand(const void* w_codes, int64_t N, int64_t K, void*
                                 void* stream) {
   if (N == 0) return GWB_SUCCESS;
   if (!fits_int(N) || !fits_int(K)) return GWB_E_SHAPE;
+  if (!w_codes || !w_q8) return GWB_E_SHAPE;
   return gwb::launch_w4a4_weight_expand(w_codes, w_q8, N, K, S(stream));
 }
 
@@ -160,6 +164,7 @@ int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_dow
 int gwb_w8a8_quant(const void* x, int64_t M, int64_t K, void* q, void* scale, void* stream) {
   if (M == 0) return GWB_SUCCESS;
   if (!fits_int(M) || !fits_int(K) || K % 8 || K == 0) return GWB_E_SHAPE;
+  if (!x || !q || !scale) return GWB_E_SHAPE;
   if (!al16(x) || !al16(q) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return GWB_E_ALIGN;
   return gwb::launch_act_int8(x, q, scale, (int)M, (int)K, S(stream));
 }
@@ -187,6 +192,7 @@ int gwb_w8a8_linear(const void* x, const void* w_q, const float* w_scale, const 
 int gwb_fp8_quant(const void* x, int64_t M, int64_t K, void* q, void* scale, void* stream) {
   if (M == 0) return GWB_SUCCESS;
   if (!fits_int(M) || !fits_int(K) || K % 8 || K == 0) return GWB_E_SHAPE;
+  if (!x || !q || !scale) return GWB_E_SHAPE;
   if (!al16(x) || !al16(q) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return GWB_E_ALIGN;
   return gwb::launch_act_fp8(x, q, scale, (int)M, (int)K, S(stream));
 }
@@ -215,6 +221,7 @@ int gwb_nvfp4_quant(const void* x, const void* smooth, int64_t M, int64_t K, voi
                     void* sblk, float* work, void* stream) {
   if (M == 0) return GWB_SUCCESS;
   if (!fits_int(M) || !fits_int(K) || K % 64 || K == 0) return GWB_E_SHAPE;
+  if (!x || !codes) return GWB_E_SHAPE;
   if (!al16(x) || !al16(codes) || (smooth && !al16(smooth)) || !sblk || !work || !al16(work))
     return GWB_E_ALIGN;
   return gwb::launch_act_nvfp4(x, smooth, work, codes, sblk, (int)M, (int)K, S(stream));
@@ -226,6 +233,7 @@ int gwb_nvfp4_quant_lowrank(const void* x, const void* smooth, const void* down_
   if (M == 0) return GWB_SUCCESS;
   if (!fits_int(M) || !fits_int(K) || K % 64 || K == 0) return GWB_E_SHAPE;
   if (rank_pad != 16 && rank_pad != 32 && rank_pad != 48 && rank_pad != 64) return GWB_E_SHAPE;
+  if (!x || !codes || !down_t) return GWB_E_SHAPE;
   if (!al16(x) || !al16(codes) || (smooth && !al16(smooth)) || !sblk || !work || !al16(work) ||
       !al16(down_t) || !la)
     return GWB_E_ALIGN;
@@ -304,6 +312,7 @@ int gwb_awq_w4a16_mm(const void* x, const void* weight, const void* wscales, con
   if (M == 0) return GWB_SUCCESS;
   if (!fits_int(M) || !fits_int(N) || !fits_int(K) || N % 16 || K % 128 || N == 0)
     return GWB_E_SHAPE;
+  if (!x || !weight || !wscales || !wzeros || !out) return GWB_E_SHAPE;
   if (!al16(x) || !al16(weight)) return GWB_E_ALIGN;
   const cudaError_t e = gwb::launch_awq_w4a16(
       static_cast<const __nv_bfloat16*>(x), static_cast<const uint8_t*>(weight),

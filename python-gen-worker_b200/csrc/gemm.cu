@@ -896,6 +896,7 @@ static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) 
 
 int launch_gemm_w8a8(const W8A8Args& a, bool fp8, cudaStream_t st) {
   if (a.M <= 0 || a.K <= 0 || a.K % kBK || a.N % w8::BN) return GWB_E_SHAPE;
+  if (!a.a_q || !a.a_scale || !a.w_q || !a.w_scale || !a.out) return GWB_E_SHAPE;
   if (!al16(a.a_q) || !al16(a.w_q) || !al16(a.out) || !al16(a.w_scale) ||
       (a.bias && !al16(a.bias)))
     return GWB_E_ALIGN;
@@ -929,6 +930,8 @@ int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, cudaStream_t st) {
   if (a.rank_pad < 0 || a.rank_pad > 64 || a.rank_pad % 16) return GWB_E_SHAPE;
   if (a.rank_pad > 0 && !a.partials && (!a.la || !a.up)) return GWB_E_SHAPE;
   if (!a.partials && !a.out) return GWB_E_SHAPE;
+  if (!a.a_codes || !a.w_q8) return GWB_E_SHAPE;
+  if (!a.partials && (!a.a_scale_k8 || !a.w_scale_k8)) return GWB_E_SHAPE;
   const int G = a.K / 64;
   if ((int64_t)G * a.M > 0x7fffffff || (int64_t)G * a.N > 0x7fffffff) return GWB_E_SHAPE;
   if (!al16(a.a_codes) || !al16(a.w_q8) || (a.out && !al16(a.out)) ||

@@ -23,7 +23,10 @@
 //    threads) race on the array and corrupt each other's results;
 //  * the first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current; make that first call
-//    before any stream capture begins.
+//    before any stream capture begins. The address is cached per process and
+//    per device, and is not looked up again after a device reset;
+//  * `stream` must belong to the current device (the array's address is the
+//    current device's); a stream of another device returns GWB_E_SHAPE.
 #include <cuda_runtime.h>
 #include <mutex>
 
@@ -73,6 +76,14 @@ extern "C" int gwb_svdq_w4a4_linear_noalloc(const void* x, const void* smooth,
   const uint64_t scale_b = round256((uint64_t)M * (uint64_t)(K / 64) * 16u);
   const uint64_t la_b = round256((uint64_t)M * (uint64_t)rank_pad * 2u);
   if (codes_b + scale_b + la_b > GWB_NOALLOC_SCRATCH_BYTES) return GWB_E_CAPACITY;
+  if (!x || !w_q8 || !w_scale_k8 || !out) return GWB_E_SHAPE;
+  if (stream != nullptr) {
+    int cur = 0, sdev = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess ||
+        cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev) != cudaSuccess)
+      return GWB_E_LAUNCH;
+    if (sdev != cur) return GWB_E_SHAPE;
+  }
   unsigned char* base = nullptr;
   rc = noalloc_scratch(&base);
   if (rc) return rc;

@@ -55,6 +55,22 @@ def test_entry_points_reject_bad_shapes_before_touching_memory():
     assert lib.gwb_svdq_w4a4_quant_mma(None, None, None, 4, 100, 0, None, None, None, None) == 1
     assert lib.gwb_svdq_w4a4_scale_k8(None, 4, 100, None, None) == 1
     assert lib.gwb_w8a8_linear(None, None, None, None, 4, 128, 100, 0, None, None, None, None) == 1
+    # null data pointers with valid sizes -> GWB_E_SHAPE (1), no launch
+    assert lib.gwb_svdq_w4a4_quant(None, None, None, 4, 128, 0, None, None, None, None) == 1
+    assert lib.gwb_svdq_w4a4_quant_mma(None, None, None, 4, 128, 0, None, None, None, None) == 1
+    assert lib.gwb_svdq_w4a4_gemm(None, None, None, None, None, None, None, 4, 128, 128, 0, 0,
+                                  None, None) == 1
+    assert lib.gwb_svdq_w4a4_gemm_packed(None, None, None, None, None, None, None, 4, 128, 128,
+                                         0, 0, None, None) == 1
+    assert lib.gwb_svdq_w4a4_linear(*([None] * 7), 4, 128, 128, 0, 0, *([None] * 5)) == 1
+    assert lib.gwb_svdq_w4a4_linear_noalloc(*([None] * 7), 4, 128, 128, 0, 0, None, None) == 1
+    assert lib.gwb_svdq_w4a4_group_partials(None, None, 4, 128, 128, None, None) == 1
+    assert lib.gwb_w8a8_quant(None, 4, 128, None, None, None) == 1
+    assert lib.gwb_fp8_quant(None, 4, 128, None, None, None) == 1
+    assert lib.gwb_w8a8_gemm(None, None, None, None, None, 4, 256, 128, 0, None, None) == 1
+    assert lib.gwb_fp8_gemm(None, None, None, None, None, 4, 256, 128, 0, None, None) == 1
+    assert lib.gwb_nvfp4_quant(None, None, 4, 128, None, None, None, None) == 1
+    assert lib.gwb_awq_w4a16_mm(None, None, None, None, None, 1, 128, 128, None, None) == 1
     # M == 0 is a no-op success
     assert lib.gwb_svdq_w4a4_linear(*([None] * 7), 0, 128, 128, 0, 0, *([None] * 5)) == 0
 

@@ -28,48 +28,68 @@ def _call(lib, name, *args):
     assert rc == 0, f"{name}: {native.status_string(rc)}"
 
 
-@pytest.mark.parametrize("m,k,n,rank", [(300, 3072, 384, 32), (128, 1024, 256, 0)])
-def test_noalloc_linear_matches_allocating_entry_point(cuda_ready, m, k, n, rank):
-    lib = native.require()
-    dev = torch.device("cuda", 0)
-    stream = torch.cuda.current_stream().cuda_stream
-    x0 = O.synth_activation(m, k, seed=41)
-    L = O.synth_svdq_layer(k, n, rank, seed=42, x_calib=x0)
+def _layer(dev, k, n, rank, seed):
+    x0 = O.synth_activation(64, k, seed=seed)
+    L = O.synth_svdq_layer(k, n, rank, seed=seed + 1, x_calib=x0)
     p = ops.prepare_w4a4_weights(L["w_scale"].to(dev),
                                  None if rank == 0 else L["proj_down"].to(dev),
                                  None if rank == 0 else L["proj_up"].to(dev),
                                  weight=L["w_packed"].to(dev))
-    rp = 0 if rank == 0 else int(p["proj_down_t"].shape[0])
-    w = p["w_q8"]
-    smooth = L["smooth"].to(dev)
-    bias = L["bias"].to(dev)
-    down_t = p["proj_down_t"]
-    up = p["proj_up_pad"]
-    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    return L, p
 
+
+def _both(lib, dev, L, p, m, k, n, seed):
+    """One call of each entry point on the same seeded input; returns both outputs."""
+    stream = torch.cuda.current_stream().cuda_stream
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    rp = 0 if p["proj_down_t"] is None else int(p["proj_down_t"].shape[0])
+    x = O.synth_activation(m, k, seed=seed).to(dev)
+    smooth, bias = L["smooth"].to(dev), L["bias"].to(dev)
+    codes = torch.empty(m, k, dtype=torch.uint8, device=dev)
+    ascale = torch.empty(k // 64, m, 8, dtype=torch.float16, device=dev)
+    la = torch.empty(m, max(rp, 1), dtype=torch.bfloat16, device=dev)
+    y_ref = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    y_na = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=dev)
+    _call(lib, "gwb_svdq_w4a4_linear", x.data_ptr(), smooth.data_ptr(), ptr(p["proj_down_t"]),
+          p["w_q8"].data_ptr(), p["w_scale_k8"].data_ptr(), ptr(p["proj_up_pad"]),
+          bias.data_ptr(), m, n, k, rp, 0, codes.data_ptr(), ascale.data_ptr(),
+          la.data_ptr() if rp else None, y_ref.data_ptr(), stream)
+    _call(lib, "gwb_svdq_w4a4_linear_noalloc", x.data_ptr(), smooth.data_ptr(),
+          ptr(p["proj_down_t"]), p["w_q8"].data_ptr(), p["w_scale_k8"].data_ptr(),
+          ptr(p["proj_up_pad"]), bias.data_ptr(), m, n, k, rp, 0, y_na.data_ptr(), stream)
+    torch.cuda.synchronize()
+    assert native.device_error() == 0
+    return y_ref.cpu(), y_na.cpu()
+
+
+@pytest.mark.parametrize("m,k,n,rank", [(300, 3072, 384, 32), (128, 1024, 256, 0)])
+def test_noalloc_linear_matches_allocating_entry_point(cuda_ready, m, k, n, rank):
+    lib = native.require()
+    dev = torch.device("cuda", 0)
+    L, p = _layer(dev, k, n, rank, seed=41)
     for seed in (43, 44):   # two calls in a row, different inputs
-        x = O.synth_activation(m, k, seed=seed).to(dev)
-        codes = torch.empty(m, k, dtype=torch.uint8, device=dev)
-        ascale = torch.empty(k // 64, m, 8, dtype=torch.float16, device=dev)
-        la = torch.empty(m, max(rp, 1), dtype=torch.bfloat16, device=dev)
-        y_ref = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-        y_na = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=dev)
-        _call(lib, "gwb_svdq_w4a4_linear", x.data_ptr(), smooth.data_ptr(), ptr(down_t),
-              w.data_ptr(), p["w_scale_k8"].data_ptr(), ptr(up), bias.data_ptr(), m, n, k, rp,
-              0, codes.data_ptr(), ascale.data_ptr(), la.data_ptr() if rp else None,
-              y_ref.data_ptr(), stream)
-        _call(lib, "gwb_svdq_w4a4_linear_noalloc", x.data_ptr(), smooth.data_ptr(),
-              ptr(down_t), w.data_ptr(), p["w_scale_k8"].data_ptr(), ptr(up), bias.data_ptr(),
-              m, n, k, rp, 0, y_na.data_ptr(), stream)
-        torch.cuda.synchronize()
-        assert native.device_error() == 0
+        y_ref, y_na = _both(lib, dev, L, p, m, k, n, seed)
         assert not torch.isnan(y_na.float()).any()
-        assert O.rel_l2(y_na.cpu(), y_ref.cpu()) <= REL_TOL
+        assert O.rel_l2(y_na, y_ref) <= REL_TOL
+
+
+def test_noalloc_shrinking_calls_do_not_see_stale_scratch(cuda_ready):
+    """A large call (rank 32) leaves its intermediates in the shared array;
+    the smaller calls after it (rank 0, then rank 16) must not pick any of
+    them up."""
+    lib = native.require()
+    dev = torch.device("cuda", 0)
+    k, n = 1024, 256
+    for m, rank, seed in ((2000, 32, 51), (96, 0, 52), (200, 16, 53)):
+        L, p = _layer(dev, k, n, rank, seed=seed)
+        y_ref, y_na = _both(lib, dev, L, p, m, k, n, seed + 100)
+        assert not torch.isnan(y_na.float()).any()
+        assert O.rel_l2(y_na, y_ref) <= REL_TOL
 
 
 def test_noalloc_rejects_requests_beyond_its_capacity(cuda_ready):
     lib = native.require()
-    # 20000 x 3072 needs 20000*(1536+768+64) bytes > 32 MiB -> GWB_E_CAPACITY (8),
+    # 20000 x 3072 needs 20000*(3072+768+64) bytes > 32 MiB -> GWB_E_CAPACITY (8),
     # refused before any pointer is touched
     rc = lib.gwb_svdq_w4a4_linear_noalloc(None, None, None, None, None, None, None,
                                           20000, 3072, 3072, 32, 0, None, None)
