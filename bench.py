@@ -46,6 +46,10 @@ SINGLE = [("qkv_mlp", HIDDEN, 21504, False), ("out", 15360, HIDDEN, False)]
 N_DUAL, N_SINGLE = 19, 38
 INT8_DENSE_PEAK_TOPS = 4500.0   # B200 datasheet dense INT8 / FP8, for context
 PEAKS_FILE = ROOT / "profiles" / "tensor_peaks_b200.json"
+# DRAM bytes (read + write) of one gemm_w4a4_kernel launch at the cfg4 qkv
+# shape (M 16896, K 3072, N 9216) from one ncu capture; None until measured
+GEMM_TRAFFIC_BYTES: Optional[float] = None
+GEMM_TRAFFIC_NOTE = "not captured"
 
 
 def tensor_peak_tops() -> tuple[float, str]:
@@ -862,10 +866,8 @@ def main() -> int:
                          "achieved": achieved, "peak": peak, "unit": "TOP/s",
                          "peak_source": peak_src, "frac": achieved / peak,
                          "frac_of_datasheet_dense_int8_fp8": achieved / INT8_DENSE_PEAK_TOPS,
-                         "traffic": GEMM_TRAFFIC_CFG3_BYTES,
-                         "traffic_note": "DRAM read+write bytes of one launch, cfg3 shape "
-                                         "(4608x3072x3072), one ncu capture; algorithmic "
-                                         "29.5 MB",
+                         "traffic": GEMM_TRAFFIC_BYTES,
+                         "traffic_note": GEMM_TRAFFIC_NOTE,
                          "avg_launch_ms": gemm_avg_ms, "launches_timed": gemm_n},
             "e2e": {"value": TOKENS / (e2e_max / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": m * HIDDEN * 2, "d2h_bytes_per_step": m * HIDDEN * 2},

@@ -154,7 +154,7 @@ __device__ __forceinline__ void quant_seg16(const uint32_t (&xw)[8], const float
 // mma.sync; the per-warp partials are summed in a fixed order through
 // shared memory, so la is deterministic.
 template <int NB, bool MMA_FORM, int MT>
-__global__ void __launch_bounds__(act_warps<MT>() * 32, 2)
+__global__ void __launch_bounds__(act_warps<MT>() * 32, NB > 8 ? 1 : 2)
 act_int4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ smooth,
                 const __nv_bfloat16* __restrict__ down_t, uint8_t* __restrict__ codes,
                 __half* __restrict__ ascale, __nv_bfloat16* __restrict__ la, int M, int K) {
@@ -339,6 +339,10 @@ static int launch_act_int4_mt(const void* x, const void* smooth, const void* dow
     GWB_ACT_CASE(32, 4)
     GWB_ACT_CASE(48, 6)
     GWB_ACT_CASE(64, 8)
+    GWB_ACT_CASE(80, 10)
+    GWB_ACT_CASE(96, 12)
+    GWB_ACT_CASE(112, 14)
+    GWB_ACT_CASE(128, 16)
     default: return GWB_E_SHAPE;
   }
 #undef GWB_ACT_CASE
@@ -349,12 +353,9 @@ int launch_act_int4(const void* x, const void* smooth, const void* down_t, void*
                     void* ascale, void* la, int M, int K, int rank_pad, bool mma_form,
                     cudaStream_t st) {
   // one m16 row tile per CTA measured fastest (M = 4608 and M = 16896)
-  const bool two = false;
   if (mma_form)
-    return two ? launch_act_int4_mt<true, 2>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st)
-               : launch_act_int4_mt<true, 1>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st);
-  return two ? launch_act_int4_mt<false, 2>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st)
-             : launch_act_int4_mt<false, 1>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st);
+    return launch_act_int4_mt<true, 1>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st);
+  return launch_act_int4_mt<false, 1>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st);
 }
 
 // Scale interchange form f16 [R, K/64] -> GEMM scale-operand rows
@@ -634,13 +635,16 @@ act_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __res
 // 16c + 4s + (0, 1 | 2, 3)); the per-warp partial sums of la are added in a
 // fixed order through shared memory (deterministic).
 template <int NB>
-__global__ void __launch_bounds__(256, 2)
+__global__ void __launch_bounds__(256, NB > 8 ? 1 : 2)
 nvfp4_amax_la_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ smooth,
                      const float* __restrict__ rsm, const __nv_bfloat16* __restrict__ down_t,
                      unsigned int* __restrict__ amax_bits, __nv_bfloat16* __restrict__ la, int M,
                      int K) {
   constexpr int RP = NB * 8, ROWS = 16, WARPS = 8;
-  __shared__ float red[WARPS][ROWS][RP];
+  // per-warp partial sums of la: [WARPS][ROWS][RP] floats (64 KB at rank 128,
+  // beyond the static limit, hence dynamic)
+  extern __shared__ float red_dyn[];
+  float (*red)[ROWS][RP] = reinterpret_cast<float (*)[ROWS][RP]>(red_dyn);
   __shared__ float wmax[WARPS];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -756,13 +760,27 @@ int launch_act_nvfp4_lowrank(const void* x, const void* smooth, const void* down
   auto D = static_cast<const __nv_bfloat16*>(down_t);
   auto A = reinterpret_cast<unsigned int*>(work);
   auto L = static_cast<__nv_bfloat16*>(la);
+  const size_t red_bytes = (size_t)8 * 16 * rank_pad * sizeof(float);
+#define GWB_AMAX_LA_CASE(RPAD, NBV)                                                          \
+  case RPAD: {                                                                               \
+    auto k = nvfp4_amax_la_kernel<NBV>;                                                      \
+    if (red_bytes > 48 * 1024)                                                               \
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)red_bytes);  \
+    k<<<grid, 256, red_bytes, st>>>(X, Sm, work + 4, D, A, L, M, K);                          \
+    break;                                                                                   \
+  }
   switch (rank_pad) {
-    case 16: nvfp4_amax_la_kernel<2><<<grid, 256, 0, st>>>(X, Sm, work + 4, D, A, L, M, K); break;
-    case 32: nvfp4_amax_la_kernel<4><<<grid, 256, 0, st>>>(X, Sm, work + 4, D, A, L, M, K); break;
-    case 48: nvfp4_amax_la_kernel<6><<<grid, 256, 0, st>>>(X, Sm, work + 4, D, A, L, M, K); break;
-    case 64: nvfp4_amax_la_kernel<8><<<grid, 256, 0, st>>>(X, Sm, work + 4, D, A, L, M, K); break;
+    GWB_AMAX_LA_CASE(16, 2)
+    GWB_AMAX_LA_CASE(32, 4)
+    GWB_AMAX_LA_CASE(48, 6)
+    GWB_AMAX_LA_CASE(64, 8)
+    GWB_AMAX_LA_CASE(80, 10)
+    GWB_AMAX_LA_CASE(96, 12)
+    GWB_AMAX_LA_CASE(112, 14)
+    GWB_AMAX_LA_CASE(128, 16)
     default: return GWB_E_SHAPE;
   }
+#undef GWB_AMAX_LA_CASE
   const int64_t nblk = (int64_t)M * (K / 16);
   int64_t blocks = (nblk + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;

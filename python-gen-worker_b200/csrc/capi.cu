@@ -31,7 +31,7 @@ inline bool fits_int(int64_t v) { return v >= 0 && v <= 0x7fffffff; }
 inline int check_w4a4_shape(int64_t M, int64_t N, int64_t K, int rank_pad) {
   if (!fits_int(M) || !fits_int(N) || !fits_int(K) || M == 0) return GWB_E_SHAPE;
   if (K % 128 || N % 128) return GWB_E_SHAPE;
-  if (rank_pad < 0 || rank_pad > 64 || rank_pad % 16) return GWB_E_SHAPE;
+  if (rank_pad < 0 || rank_pad > 128 || rank_pad % 16) return GWB_E_SHAPE;
   return GWB_SUCCESS;
 }
 
@@ -68,7 +68,7 @@ int gwb_svdq_w4a4_quant(const void* x, const void* smooth, const void* proj_down
                         void* stream) {
   if (M == 0) return GWB_SUCCESS;
   if (!fits_int(M) || !fits_int(K) || K % 64) return GWB_E_SHAPE;
-  if (rank_pad < 0 || rank_pad > 64 || rank_pad % 16) return GWB_E_SHAPE;
+  if (rank_pad < 0 || rank_pad > 128 || rank_pad % 16) return GWB_E_SHAPE;
   if (rank_pad > 0 && (!proj_down_t || !la)) return GWB_E_SHAPE;
   if (!x || !codes || !ascale) return GWB_E_SHAPE;
   if (!al16(x) || !al16(codes) || (smooth && !al16(smooth)) ||
@@ -84,7 +84,7 @@ int gwb_svdq_w4a4_quant_mma(const void* x, const void* smooth, const void* proj_
                             void* la, void* stream) {
   if (M == 0) return GWB_SUCCESS;
   if (!fits_int(M) || !fits_int(K) || K % 64 || (K / 64) * M > 0x7fffffff) return GWB_E_SHAPE;
-  if (rank_pad < 0 || rank_pad > 64 || rank_pad % 16) return GWB_E_SHAPE;
+  if (rank_pad < 0 || rank_pad > 128 || rank_pad % 16) return GWB_E_SHAPE;
   if (rank_pad > 0 && (!proj_down_t || !la)) return GWB_E_SHAPE;
   if (!x || !a_q8 || !a_scale_k8) return GWB_E_SHAPE;
   if (!al16(x) || !al16(a_q8) || !al16(a_scale_k8) || (smooth && !al16(smooth)) ||
@@ -232,7 +232,7 @@ int gwb_nvfp4_quant_lowrank(const void* x, const void* smooth, const void* down_
                             void* la, void* stream) {
   if (M == 0) return GWB_SUCCESS;
   if (!fits_int(M) || !fits_int(K) || K % 64 || K == 0) return GWB_E_SHAPE;
-  if (rank_pad != 16 && rank_pad != 32 && rank_pad != 48 && rank_pad != 64) return GWB_E_SHAPE;
+  if (rank_pad < 16 || rank_pad > 128 || rank_pad % 16) return GWB_E_SHAPE;
   if (!x || !codes || !down_t) return GWB_E_SHAPE;
   if (!al16(x) || !al16(codes) || (smooth && !al16(smooth)) || !sblk || !work || !al16(work) ||
       !al16(down_t) || !la)

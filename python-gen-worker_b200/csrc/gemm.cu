@@ -349,6 +349,8 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const int G = K / 64;
   const bool dump = partials != nullptr;
   const int has_lr = (!dump && rank_pad > 0) ? 1 : 0;
+  // the low-rank operands take one ring slot per 64 ranks (128-byte rows)
+  const int lr_slots = has_lr ? (rank_pad + 63) / 64 : 0;
   // Persistent: this CTA takes tiles blockIdx.x, +gridDim.x, ... (N-tile
   // fastest). Ring slots and TMEM group buffers are counted across tiles, so
   // the next tile's loads and MMAs start while this tile's epilogue finishes.
@@ -391,17 +393,18 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
       const int m0 = (tile / tiles_n) * kBM, n0 = (tile % tiles_n) * BN;
-      if (has_lr) {
-        // low-rank operands go straight into an operand ring slot
+      for (int h = 0; h < lr_slots; ++h, ++ui) {
+        // low-rank operands (ranks 64h .. 64h+63) go straight into an operand ring slot
         const int u = ui % USTAGES;
-        if (!mbar_wait(&u_empty[u], ((ui / USTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) break;
+        ok = mbar_wait(&u_empty[u], ((ui / USTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER);
+        if (!ok) break;
         mbar_arrive_expect_tx(&u_full[u], kBM * 128 + BN * 128);
         if (A_PACKED) mbar_arrive(&u_full[u]);
         uint8_t* us = ustage + u * USTAGE_BYTES;
-        tma_load_2d(us, &tmLA, &u_full[u], 0, m0);
-        tma_load_2d(us + UA_BYTES, &tmUP, &u_full[u], 0, n0);
-        ++ui;
+        tma_load_2d(us, &tmLA, &u_full[u], 64 * h, m0);
+        tma_load_2d(us + UA_BYTES, &tmUP, &u_full[u], 64 * h, n0);
       }
+      if (!ok) break;
       for (int kb = 0; kb < nk; ++kb, ++ui) {
         if (A_PACKED) {
           const int s = pk % PSTAGES;
@@ -446,19 +449,23 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       int ui = 0, gi = 0;   // operand-ring slots and group buffers used so far
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
       if (has_lr) {
-        // the tile's first group slot <- la · proj_upᵀ (f32)
-        const int u = ui % USTAGES, b = gi & 1;
-        ok = mbar_wait(&u_full[u], (ui / USTAGES) & 1, GWB_ERR_TIMEOUT_MMA) &&
-             mbar_wait(&acc_empty[b], ((gi >> 1) & 1) ^ 1, GWB_ERR_TIMEOUT_MMA);
+        // the tile's first group slot <- la · proj_upᵀ (f32), 64 ranks per ring slot
+        const int b = gi & 1;
+        for (int h = 0; h < lr_slots; ++h, ++ui) {
+          const int u = ui % USTAGES;
+          ok = mbar_wait(&u_full[u], (ui / USTAGES) & 1, GWB_ERR_TIMEOUT_MMA) &&
+               (h > 0 || mbar_wait(&acc_empty[b], ((gi >> 1) & 1) ^ 1, GWB_ERR_TIMEOUT_MMA));
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(ustage + u * USTAGE_BYTES), b_base = a_base + UA_BYTES;
+          const int nk16 = min(4, (rank_pad - 64 * h) / 16);
+          for (int k = 0; k < nk16; ++k)
+            mma_f16(tmem + b * BN, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k),
+                    idesc_lr, (h > 0 || k > 0) ? 1u : 0u);
+          mma_commit(&u_empty[u]);
+        }
         if (!ok) break;
-        tc_fence_after();
-        const uint32_t a_base = smem_u32(ustage + u * USTAGE_BYTES), b_base = a_base + UA_BYTES;
-        for (int k = 0; k < rank_pad / 16; ++k)
-          mma_f16(tmem + b * BN, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k),
-                  idesc_lr, k > 0 ? 1u : 0u);
         mma_commit(&acc_full[b]);
-        mma_commit(&u_empty[u]);
-        ++ui;
         ++gi;
       }
       for (int kb = 0; kb < nk && ok; ++kb, ++ui) {
@@ -498,7 +505,7 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       int ui = 0, pk = 0;
       bool live = true;
       for (int tile = blockIdx.x; live && tile < ntiles; tile += gridDim.x) {
-      ui += has_lr;   // the low-rank slot is filled by the TMA thread alone
+      ui += lr_slots;   // the low-rank slots are filled by the TMA thread alone
       for (int kb = 0; kb < nk; ++kb, ++ui, ++pk) {
         const int s = pk % PSTAGES;
         const int u = ui % USTAGES;
@@ -685,7 +692,11 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   const int nk = K / 256;
   const int ncb = K / 64;                     // blocked-layout tile columns per 128 rows
   const int has_lr = rank_pad > 0 ? 1 : 0;
-  const int tiles_n = N / BN;
+  // the low-rank operands take one ring stage per 64 ranks (128-byte rows)
+  const int lr_slots = has_lr ? (rank_pad + 63) / 64 : 0;
+  // N % 256 == 128: the last N tile is half a tile (B rows past N read as
+  // zeros by TMA; their scale tiles are not loaded and their columns not stored)
+  const int tiles_n = (N + BN - 1) / BN;
   const int ntiles = ((M + kBM - 1) / kBM) * tiles_n;
 
   if (threadIdx.x == 0) {
@@ -713,24 +724,26 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
         const int mt = tile / tiles_n, m0 = mt * kBM, n0 = (tile % tiles_n) * BN;
-        if (has_lr) {
+        const bool half_n = n0 + 128 >= N;   // only B rows n0 .. n0+127 exist
+        for (int h = 0; h < lr_slots; ++h, ++ui) {
           const int u = ui % STAGES;
           ok = mbar_wait(&empty[u], ((ui / STAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER);
-          if (!__all_sync(0xFu, ok)) break;
+          ok = __all_sync(0xFu, ok);
+          if (!ok) break;
           if (pl == 0) {
             uint8_t* us = smem + u * STAGE_BYTES;
             mbar_arrive_expect_tx(&full[u], kBM * 128 + BN * 128);
-            tma_load_2d(us, &tmLA, &full[u], 0, m0);
-            tma_load_2d(us + A_BYTES, &tmUP, &full[u], 0, n0);
+            tma_load_2d(us, &tmLA, &full[u], 64 * h, m0);
+            tma_load_2d(us + A_BYTES, &tmUP, &full[u], 64 * h, n0);
           }
           __syncwarp(0xFu);
-          ++ui;
         }
+        if (!ok) break;
         for (int kb = 0; kb < nk; ++kb, ++ui) {
           const int u = ui % STAGES;
           ok = mbar_wait(&empty[u], ((ui / STAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER);
           if (!__all_sync(0xFu, ok)) break;
-          if (pl == 0) mbar_arrive_expect_tx(&full[u], STAGE_BYTES);
+          if (pl == 0) mbar_arrive_expect_tx(&full[u], half_n ? STAGE_BYTES - SFA_BYTES : STAGE_BYTES);
           __syncwarp(0xFu);
           uint8_t* us = smem + u * STAGE_BYTES;
           uint8_t* sfa = us + A_BYTES + B_BYTES;
@@ -743,8 +756,9 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           } else {
             const size_t rb = (size_t)(n0 / 128);
             bulk_load(sfa + SFA_BYTES, w_sblk + (rb * ncb + 4 * kb) * 512, SFA_BYTES, &full[u]);
-            bulk_load(sfa + 2 * SFA_BYTES, w_sblk + ((rb + 1) * ncb + 4 * kb) * 512, SFA_BYTES,
-                      &full[u]);
+            if (!half_n)
+              bulk_load(sfa + 2 * SFA_BYTES, w_sblk + ((rb + 1) * ncb + 4 * kb) * 512, SFA_BYTES,
+                        &full[u]);
           }
         }
       }
@@ -757,18 +771,20 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++lt) {
         if (!mbar_wait(acc_empty, (lt & 1) ^ 1, GWB_ERR_TIMEOUT_MMA)) break;
         tc_fence_after();
-        if (has_lr) {
-          // acc <- (la / s2) · (proj_up / weight_scale_2)ᵀ
+        for (int h = 0; h < lr_slots; ++h, ++ui) {
+          // acc <- (la / s2) · (proj_up / weight_scale_2)ᵀ, 64 ranks per ring stage
           const int u = ui % STAGES;
-          if (!mbar_wait(&full[u], (ui / STAGES) & 1, GWB_ERR_TIMEOUT_MMA)) break;
+          ok = mbar_wait(&full[u], (ui / STAGES) & 1, GWB_ERR_TIMEOUT_MMA);
+          if (!ok) break;
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + u * STAGE_BYTES), b_base = a_base + A_BYTES;
-          for (int k = 0; k < rank_pad / 16; ++k)
+          const int nk16 = min(4, (rank_pad - 64 * h) / 16);
+          for (int k = 0; k < nk16; ++k)
             mma_f16(tmem + ACC_COL, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k),
-                    idesc_lr, k > 0 ? 1u : 0u);
+                    idesc_lr, (h > 0 || k > 0) ? 1u : 0u);
           mma_commit(&empty[u]);
-          ++ui;
         }
+        if (!ok) break;
         for (int kb = 0; kb < nk; ++kb, ++ui) {
           const int u = ui % STAGES;
           if (!mbar_wait(&full[u], (ui / STAGES) & 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
@@ -815,7 +831,7 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
       const int row = m0 + 32 * q + lane;
-      if (row >= M) continue;
+      if (row >= M || n0 + cb >= N) continue;
       uint4* op = reinterpret_cast<uint4*>(out + (size_t)row * N + n0 + cb);
 #pragma unroll
       for (int c = 0; c < EC; c += 8) {
@@ -927,7 +943,7 @@ int launch_gemm_w8a8(const W8A8Args& a, bool fp8, cudaStream_t st) {
 
 int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, cudaStream_t st) {
   if (a.M <= 0 || a.K <= 0 || a.K % kBK || a.N % w4::BN) return GWB_E_SHAPE;
-  if (a.rank_pad < 0 || a.rank_pad > 64 || a.rank_pad % 16) return GWB_E_SHAPE;
+  if (a.rank_pad < 0 || a.rank_pad > 128 || a.rank_pad % 16) return GWB_E_SHAPE;
   if (a.rank_pad > 0 && !a.partials && (!a.la || !a.up)) return GWB_E_SHAPE;
   if (!a.partials && !a.out) return GWB_E_SHAPE;
   if (!a.a_codes || !a.w_q8) return GWB_E_SHAPE;
@@ -988,8 +1004,8 @@ int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, cudaStream_t st) {
 }
 
 int launch_gemm_nvfp4(const NvFp4Args& a, cudaStream_t st) {
-  if (a.M <= 0 || a.K <= 0 || a.K % 256 || a.N % nv4::BN) return GWB_E_SHAPE;
-  if (a.rank_pad < 0 || a.rank_pad > 64 || a.rank_pad % 16) return GWB_E_SHAPE;
+  if (a.M <= 0 || a.K <= 0 || a.K % 256 || a.N <= 0 || a.N % 128) return GWB_E_SHAPE;
+  if (a.rank_pad < 0 || a.rank_pad > 128 || a.rank_pad % 16) return GWB_E_SHAPE;
   if (a.rank_pad > 0 && (!a.la || !a.up)) return GWB_E_SHAPE;
   if (!a.a_codes || !a.w_codes || !a.a_sblk || !a.w_sblk || !a.a_work || !a.w_scale_2 || !a.out)
     return GWB_E_SHAPE;
@@ -1021,7 +1037,7 @@ int launch_gemm_nvfp4(const NvFp4Args& a, cudaStream_t st) {
                          nv4::SMEM_BYTES);
     attr = true;
   }
-  const int ntiles = ((a.M + kBM - 1) / kBM) * (a.N / nv4::BN);
+  const int ntiles = ((a.M + kBM - 1) / kBM) * ((a.N + nv4::BN - 1) / nv4::BN);
   const int n_sm = sm_count();
   gemm_nvfp4_kernel<<<ntiles < n_sm ? ntiles : n_sm, nv4::THREADS, nv4::SMEM_BYTES, st>>>(
       tA, tB, tLA, tUP, static_cast<const uint8_t*>(a.a_sblk),

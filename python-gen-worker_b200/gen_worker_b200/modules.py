@@ -203,12 +203,12 @@ class SvdqNvfp4Linear(nn.Module):
                  per_channel_scale: bool = False, smooth: bool = True,
                  compute_dtype: Any = torch.bfloat16, device: Any = None) -> None:
         super().__init__()
-        if in_features % 256 or out_features % 256:
+        if in_features % 256 or out_features % 128:
             raise SvdqB200LayoutError(
                 f"SvdqNvfp4Linear dims [{out_features}, {in_features}] break the tile "
-                f"alignment (in%256, out%256)")
-        if rank > 64:
-            raise SvdqB200LayoutError(f"low-rank rank {rank} > 64 is not supported")
+                f"alignment (in%256, out%128)")
+        if rank > 128:
+            raise SvdqB200LayoutError(f"low-rank rank {rank} > 128 is not supported")
         self.in_features = int(in_features)
         self.out_features = int(out_features)
         self.rank = int(rank)

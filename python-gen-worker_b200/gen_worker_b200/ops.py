@@ -482,8 +482,8 @@ def prepare_w4a4_weights(w_scale: Optional[torch.Tensor], proj_down: Optional[to
         k, r = proj_down.shape
         n = proj_up.shape[0]
         rp = rank_pad_of(r)
-        if rp > 64:
-            raise SvdqB200Error(f"low-rank rank {r} > 64 is not supported")
+        if rp > 128:
+            raise SvdqB200Error(f"low-rank rank {r} > 128 is not supported")
         dt = torch.zeros(rp, k, dtype=torch.bfloat16, device=proj_down.device)
         dt[:r] = proj_down.to(torch.bfloat16).t()
         up = torch.zeros(n, rp, dtype=torch.bfloat16, device=proj_up.device)

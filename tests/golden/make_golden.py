@@ -214,6 +214,49 @@ def main(ref_root: str = "/root/reference") -> None:
     path = HERE / "reference_golden.pt"
     torch.save(out, path)
     print(f"wrote {path} ({path.stat().st_size} bytes)")
+    rank128(sl, nq)
+
+
+def rank128(sl, nq) -> None:
+    """Rank-128 nunchaku v1 linears at the reference's self-check probe
+    shapes (``svdq_fused.py:25``, rank 128 at ``:430``; the rank the
+    reference's own tests synthesise, ``tests/test_svdq_native_pgw685.py:224``):
+    logical tensors packed by the reference's forward packers, and the
+    reference's ``convert_linear`` buffers of the packed tensors. Written to
+    its own file so the main fixture stays byte-identical."""
+    gen = torch.Generator().manual_seed(4321)
+    out = {}
+    r = 128
+    for k, n in ((512, 256), (3072, 384)):
+        codes = torch.randint(0, 16, (n, k), generator=gen, dtype=torch.uint8)
+        scales = (torch.rand(n, k // nq.BLOCK, generator=gen) * 6 + 0.1).to(torch.float8_e4m3fn)
+        wc = torch.rand(n, generator=gen) * 0.02 + 0.001
+        smooth = (torch.rand(k, generator=gen) + 0.5).to(torch.bfloat16)
+        bias = torch.randn(n, generator=gen).to(torch.bfloat16)
+        down = (torch.randn(k, r, generator=gen) * 0.05).to(torch.bfloat16)
+        up = (torch.randn(n, r, generator=gen) * 0.05).to(torch.bfloat16)
+        packed = {
+            "qweight": sl.pack_qweight(codes),
+            "wscales": sl.pack_wscales(scales, n, k),
+            "wcscales": sl.pack_vector(wc, n),
+            "smooth_factor": sl.pack_vector(smooth, k),
+            "bias": sl.pack_vector(bias, n),
+            "proj_down": sl.pack_lowrank(down.t().contiguous(), down=True),
+            "proj_up": sl.pack_lowrank(up, down=False),
+        }
+        buf = sl.convert_linear(packed, n, k)
+        tag = f"r128_{k}x{n}_"
+        for key, val in packed.items():
+            out[tag + "packed_" + key] = (val.view(torch.uint8) if val.dtype == torch.float8_e4m3fn
+                                          else val)
+        out[tag + "buf_weight"] = buf.weight
+        out[tag + "buf_weight_scale"] = buf.weight_scale.view(torch.uint8)
+        out[tag + "buf_weight_scale_2"] = buf.weight_scale_2
+        out[tag + "buf_proj_down"], out[tag + "buf_proj_up"] = buf.proj_down, buf.proj_up
+        out[tag + "buf_smooth"], out[tag + "buf_bias"] = buf.smooth_factor, buf.bias
+    path = HERE / "reference_rank128.pt"
+    torch.save(out, path)
+    print(f"wrote {path} ({path.stat().st_size} bytes)")
 
 
 if __name__ == "__main__":

@@ -133,3 +133,32 @@ def test_refusals():
         codec.split_nvfp4_buffers(b, (128, 64))
     with pytest.raises(SvdqB200LayoutError, match="multiples"):
         codec.split_nvfp4_buffers(b, (192, 64))
+
+
+R128 = torch.load(Path(__file__).resolve().parent / "golden" / "reference_rank128.pt")
+
+
+def r128_packed(k: int, n: int) -> dict:
+    """The rank-128 nunchaku tensors of shape (k, n) packed by the reference's
+    own packers (``tests/golden/make_golden.py``)."""
+    tag = f"r128_{k}x{n}_packed_"
+    t = {key[len(tag):]: v for key, v in R128.items() if key.startswith(tag)}
+    t["wscales"] = t["wscales"].view(torch.float8_e4m3fn)
+    return t
+
+
+@pytest.mark.parametrize("k,n", [(512, 256), (3072, 384)])
+def test_rank128_decode_matches_reference_convert_linear(k, n):
+    """Rank 128, the rank of the reference's self-check and of its own
+    synthesised test linears: the native decode is bit-identical to
+    ``convert_linear`` at the self-check probe shapes."""
+    b = codec.decode_nunchaku_linear(r128_packed(k, n), n, k)
+    tag = f"r128_{k}x{n}_buf_"
+    assert b["rank"] == 128
+    assert torch.equal(b["weight"], R128[tag + "weight"])
+    assert torch.equal(b["weight_scale"].view(torch.uint8), R128[tag + "weight_scale"])
+    assert torch.equal(b["weight_scale_2"], R128[tag + "weight_scale_2"])
+    assert torch.equal(b["proj_down"], R128[tag + "proj_down"])
+    assert torch.equal(b["proj_up"], R128[tag + "proj_up"])
+    assert torch.equal(b["smooth_factor"], R128[tag + "smooth"])
+    assert torch.equal(b["bias"], R128[tag + "bias"])

@@ -98,7 +98,7 @@ def test_prepare_repacks_layouts():
     assert torch.equal(p["proj_down_t"][:20], down.t())
     assert p["proj_up_pad"].shape == (128, 32) and torch.all(p["proj_up_pad"][:, 20:] == 0)
     with pytest.raises(ops.SvdqB200Error):
-        ops.prepare_w4a4_weights(ws, torch.zeros(256, 80), torch.zeros(128, 80))
+        ops.prepare_w4a4_weights(ws, torch.zeros(256, 144), torch.zeros(128, 144))
 
 
 def test_module_surface_and_swap():
