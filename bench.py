@@ -47,9 +47,14 @@ N_DUAL, N_SINGLE = 19, 38
 INT8_DENSE_PEAK_TOPS = 4500.0   # B200 datasheet dense INT8 / FP8, for context
 PEAKS_FILE = ROOT / "profiles" / "tensor_peaks_b200.json"
 # DRAM bytes (read + write) of one gemm_w4a4_kernel launch at the cfg4 qkv
-# shape (M 16896, K 3072, N 9216) from one ncu capture; None until measured
-GEMM_TRAFFIC_BYTES: Optional[float] = None
-GEMM_TRAFFIC_NOTE = "not captured"
+# shape (M 16896, K 3072, N 9216), one ncu capture (dram__bytes_read.sum +
+# dram__bytes_write.sum, --clock-control none): 114.4 MB read (operands
+# 101 MB) + 276.7 MB written (the 311 MB bf16 output, part of it still in L2
+# when the kernel ends)
+GEMM_TRAFFIC_BYTES: Optional[float] = 114376192.0 + 276746752.0
+GEMM_TRAFFIC_NOTE = ("DRAM read+write of one launch at the cfg4 qkv shape (16896x3072->9216), "
+                     "one ncu capture; algorithmic 413 MB in the operand form (101 MB operands "
+                     "+ 311 MB bf16 output)")
 
 
 def tensor_peak_tops() -> tuple[float, str]:
@@ -466,7 +471,7 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
                 if mod._up_pad is None:
                     mod(xb)
                 c, sb_, wk, la = ops.nvfp4_quant_lowrank(xb, mod.smooth_factor, mod._up_pad[0])
-                upp = (mod._up_pad[1] / wk[1]).to(torch.bfloat16)
+                upp = mod._up_pad[1]
                 e[1].record()
                 ops.nvfp4_gemm(c, sb_, wk, mod.weight, mod.weight_scale, mod.weight_scale_2,
                                la, upp, mod.bias.detach())
@@ -495,7 +500,7 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
                                                    p["proj_up_pad"], mod.bias.detach(), gelu)
         elif kind == "nvfp4":
             c, sb_, wk, la = ops.nvfp4_quant_lowrank(xb, mod.smooth_factor, mod._up_pad[0])
-            upp = (mod._up_pad[1] / wk[1]).to(torch.bfloat16)
+            upp = mod._up_pad[1]
             gemm_call = lambda: ops.nvfp4_gemm(c, sb_, wk, mod.weight, mod.weight_scale,  # noqa: E731
                                                mod.weight_scale_2, la, upp, mod.bias.detach())
         elif kind == "fp8":

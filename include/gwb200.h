@@ -25,7 +25,7 @@
  *   la           bf16 [M, rank_pad]   x·L1 on raw x
  *   proj_up      bf16 [N, rank_pad];  bias bf16 [N] (or NULL);  out bf16 [M, N]
  * Constraints: K % 128 == 0; N % 128 == 0 (W4A4) / N % 256 == 0 (W8A8);
- * rank_pad in {0, 16, 32, 48, 64}.
+ * rank_pad a multiple of 16, at most 128.
  */
 #ifndef GWB200_H
 #define GWB200_H
@@ -197,11 +197,12 @@ int gwb_nvfp4_quant_lowrank(const void* x, const void* smooth, const void* down_
  * * s2 * w_scale_2[n] + la·proj_up^T + bias -> bf16 [M, N]. w_codes / w_sblk
  * / w_scale_2 are the reference module's `weight` / `weight_scale` /
  * `weight_scale_2` buffers as stored (w_scale_2 per channel [N] when
- * ws2_per_channel, else [1]). The low-rank up-projection comes divided by the
- * second-level scales, so the branch shares the accumulator: la =
- * bf16(x · proj_down) [M, rank_pad] on raw x (as the reference), proj_up =
- * bf16(proj_up / (w_scale_2[n] * s2)) [N, rank_pad]. K % 256 == 0,
- * N % 256 == 0. */
+ * ws2_per_channel, else [1]). The low-rank branch shares the accumulator:
+ * la = bf16(x · proj_down) [M, rank_pad] on raw x (as the reference) and
+ * proj_up = f32 proj_up / w_scale_2[n] [N, rank_pad] (the load-time form);
+ * the kernel divides it by the call's s2 (a_work[1]) and splits it into two
+ * bf16 operands in shared memory. K % 256 == 0, N % 128 == 0,
+ * rank_pad <= 128. */
 int gwb_nvfp4_gemm(const void* a_codes, const void* a_sblk, const float* a_work,
                    const void* w_codes, const void* w_sblk, const float* w_scale_2,
                    int ws2_per_channel, const void* la, const void* proj_up, const void* bias,

@@ -41,7 +41,7 @@ struct NvFp4Args {
   const float* w_scale_2;  // f32 [1] or [N]
   int ws2_per_channel;
   const void* la;          // bf16 [M, rank_pad] or null
-  const void* up;          // bf16 [N, rank_pad] or null
+  const void* up;          // f32 [N, rank_pad] = proj_up / weight_scale_2 (load time), or null
   const void* bias;        // bf16 [N] or null
   void* out;               // bf16 [M, N]
   int M, N, K, rank_pad;

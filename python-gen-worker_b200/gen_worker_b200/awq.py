@@ -26,8 +26,10 @@ from . import native
 from .ops import SvdqB200Error, _need, _ptr, _stream
 
 GROUP_SIZE = 64
-_PACK_SIZE = 8
-_NUM_PACKS_FACTOR = {32: 4, 64: 2}
+# The exporter pads the [rows, N] scale / zero grids to a whole number of
+# row quanta: 8 groups per pack, and packs in pairs (group 64) or fours
+# (group 32), i.e. 16 or 32 rows; other group sizes pad to packs of 8.
+_ROW_QUANTUM = {64: 16, 32: 32}
 
 
 class AwqPackedError(RuntimeError):
@@ -39,14 +41,14 @@ def awq_packed_supported(out_features: int, in_features: int) -> bool:
 
 
 def num_scale_rows(in_features: int, group_size: int) -> int:
-    """The exporter's padded scale-row count (``ceil_num_groups``,
-    ``svdq_awq.py:18-28``): groups rounded up to packs of 8, packs to a
-    multiple of 2 (group 64) or 4 (group 32)."""
+    """Rows of the exporter's padded scale grid for ``in_features`` split in
+    groups of ``group_size`` (the count ``ceil_num_groups`` gives,
+    ``svdq_awq.py:18-28``): the group count rounded up to the row quantum."""
     if in_features % group_size:
-        raise AwqPackedError(f"in_features {in_features} not divisible by group size {group_size}")
-    packs = -(-(in_features // group_size) // _PACK_SIZE)
-    factor = _NUM_PACKS_FACTOR.get(group_size, 1)
-    return -(-packs // factor) * factor * _PACK_SIZE
+        raise AwqPackedError(f"{in_features} input features do not split into groups of "
+                             f"{group_size}")
+    quantum = _ROW_QUANTUM.get(group_size, 8)
+    return -(-(in_features // group_size) // quantum) * quantum
 
 
 # ---------------------------------------------------------------- op
@@ -83,10 +85,11 @@ def unpack_qweight(qweight: torch.Tensor, out_features: int, in_features: int) -
     host code, ``gwb_awq_qweight_unpack``)."""
     n, k = int(out_features), int(in_features)
     if n % 4 or k % 64:
-        raise AwqPackedError(f"AWQ W4A16 [{n}, {k}] needs oc%4==0 and ic%64==0")
+        raise AwqPackedError(f"TinyChat unpack of a [{n}, {k}] linear needs out % 4 == 0 and "
+                             f"in % 64 == 0")
     if tuple(qweight.shape) != (n // 4, k // 2):
-        raise AwqPackedError(f"AWQ qweight shape {tuple(qweight.shape)} != expected "
-                             f"{(n // 4, k // 2)} for [{n}, {k}]")
+        raise AwqPackedError(f"qweight shape {tuple(qweight.shape)}: a [{n}, {k}] linear "
+                             f"stores {(n // 4, k // 2)}")
     src = qweight.detach().to("cpu").contiguous()
     out = torch.empty(n, k // 2, dtype=torch.uint8)
     native.check(native.lib().gwb_awq_qweight_unpack(ctypes.c_void_p(src.data_ptr()), n, k,
@@ -97,26 +100,34 @@ def unpack_qweight(qweight: torch.Tensor, out_features: int, in_features: int) -
 
 def scales_and_zeros(wscales: torch.Tensor, wzeros: torch.Tensor, out_features: int,
                      in_features: int) -> tuple[torch.Tensor, torch.Tensor, int]:
-    """[rows, N] grids -> ([N, ng], [N, ng], group size), the live rows only;
-    the same checks as the reference (``_scales_and_zeros``, ``svdq_awq.py:50-73``)."""
+    """[rows, N] scale / zero grids -> ([N, ng], [N, ng], group size).
+
+    The live groups are the rows above the exporter's all-zero padding,
+    found by scanning up from the last row. The grid is accepted when no
+    all-zero row sits among the live ones, the live count divides
+    ``in_features`` and the padded height is the exporter's for that group
+    size (the grids ``_scales_and_zeros`` accepts, ``svdq_awq.py:50-73``)."""
     n, k = int(out_features), int(in_features)
-    if wscales.shape[1] != n or wzeros.shape != wscales.shape:
-        raise AwqPackedError(f"AWQ scale/zero grids {tuple(wscales.shape)}/{tuple(wzeros.shape)} "
-                             f"do not match out_features {n}")
+    if wscales.dim() != 2 or int(wscales.shape[1]) != n or wzeros.shape != wscales.shape:
+        raise AwqPackedError(f"scale grid {tuple(wscales.shape)} / zero grid "
+                             f"{tuple(wzeros.shape)}: want matching [rows, {n}] grids")
     s = wscales.detach().to("cpu").float()
-    live = (s != 0).any(dim=1)
-    ng = int(torch.count_nonzero(live))
-    if ng == 0 or not bool(live[:ng].all()):
-        raise AwqPackedError("AWQ wscales has zero rows before its last live row — not the "
-                             "ceil_num_groups padding this decoder understands")
-    if k % ng:
-        raise AwqPackedError(f"in_features {k} not divisible by {ng} live scale groups")
-    gs = k // ng
-    if num_scale_rows(k, gs) != int(wscales.shape[0]):
-        raise AwqPackedError(f"AWQ scale rows {int(wscales.shape[0])} != ceil_num_groups("
-                             f"{k}, {gs}) = {num_scale_rows(k, gs)}")
+    row_used = (s != 0).any(dim=1)
+    rows = int(s.shape[0])
+    live = rows
+    while live > 0 and not bool(row_used[live - 1]):
+        live -= 1
+    if live == 0 or not bool(row_used[:live].all()):
+        raise AwqPackedError("scale grid has an all-zero row among its groups (not trailing "
+                             "padding)")
+    if k % live:
+        raise AwqPackedError(f"{live} scale groups do not divide {k} input features")
+    gs = k // live
+    if num_scale_rows(k, gs) != rows:
+        raise AwqPackedError(f"scale grid has {rows} rows; group size {gs} pads to "
+                             f"{num_scale_rows(k, gs)}")
     z = wzeros.detach().to("cpu").float()
-    return s[:ng].t().contiguous(), z[:ng].t().contiguous(), gs
+    return s[:live].t().contiguous(), z[:live].t().contiguous(), gs
 
 
 class AwqPackedLinear(nn.Module):
@@ -129,8 +140,8 @@ class AwqPackedLinear(nn.Module):
                  compute_dtype: Any = torch.bfloat16, device: Any = None) -> None:
         super().__init__()
         if not awq_packed_supported(out_features, in_features):
-            raise AwqPackedError(f"AwqPackedLinear [{out_features}, {in_features}] breaks the "
-                                 f"packed contract (out%16, in%128)")
+            raise AwqPackedError(f"AwqPackedLinear [{out_features}, {in_features}]: the GEMV "
+                                 f"needs out % 16 == 0 and in % 128 == 0")
         if compute_dtype != torch.bfloat16:
             raise AwqPackedError(f"compute dtype {compute_dtype} is not supported (bf16 only)")
         self.compute_dtype = compute_dtype
@@ -172,31 +183,32 @@ def build_awq_packed_linear(tensors: Dict[str, torch.Tensor], out_features: int,
     ``adanorm_splits`` > 1 the exporter's row interleave (stored row
     ``j * splits + s`` is row ``s * (N / splits) + j``) is undone and 1 is taken
     off the bias of splits 1 and ``splits - 2``."""
-    missing = [k for k in ("qweight", "wscales", "wzeros") if k not in tensors]
-    if missing:
-        raise AwqPackedError(f"not an AWQ W4A16 linear (missing {missing})")
+    absent = [k for k in ("qweight", "wscales", "wzeros") if k not in tensors]
+    if absent:
+        raise AwqPackedError(f"AWQ W4A16 linear lacks required tensor(s) {absent}")
     compute = compute_dtype or torch.bfloat16
     n, k = int(out_features), int(in_features)
     codes = unpack_qweight(tensors["qweight"], n, k)
     scale, zero, gs = scales_and_zeros(tensors["wscales"], tensors["wzeros"], n, k)
     if gs != GROUP_SIZE:
-        raise AwqPackedError(f"AWQ group size {gs} != {GROUP_SIZE} — the packed lane only ships "
-                             f"the g{GROUP_SIZE} contract")
+        raise AwqPackedError(f"group size {gs}: this lane runs group {GROUP_SIZE} only")
     bias = tensors.get("bias")
     splits = int(adanorm_splits)
     if splits > 1:
         if n % splits:
-            raise AwqPackedError(f"out_features {n} not divisible by adanorm_splits {splits}")
+            raise AwqPackedError(f"{n} output rows do not split into adanorm_splits={splits}")
         per = n // splits
-        idx = torch.arange(n)
-        perm = (idx % per) * splits + idx // per
-        codes, scale, zero = codes[perm], scale[perm], zero[perm]
+        # stored row j * splits + s holds logical row s * per + j
+        logical = torch.arange(n)
+        stored = (logical % per) * splits + logical // per
+        codes, scale, zero = codes[stored], scale[stored], zero[stored]
         if bias is not None:
-            b = bias.detach().to("cpu").float().view(per, splits).t().contiguous()
-            delta = torch.zeros(splits)
-            delta[1] = 1.0
-            delta[splits - 2] = 1.0
-            bias = (b - delta.reshape(splits, 1)).reshape(n)
+            b = bias.detach().to("cpu").float()[stored].view(splits, per)
+            # the exporter folded +1 into the two scale chunks (split 1 and
+            # split splits - 2); take it back off
+            for chunk in {1, splits - 2}:
+                b[chunk] -= 1.0
+            bias = b.reshape(n)
     mod = AwqPackedLinear(k, n, bias=bias is not None, compute_dtype=compute,
                           device=torch.device("cpu"))
     dev = device or "cpu"

@@ -17,16 +17,17 @@ one native host pass (``gwb_nunchaku_*`` in ``include/gwb200.h``):
 * ``proj_down`` / ``proj_up`` pack_lowrank 16-bit factors -> [K, r] / [N, r],
   or int8 / e4m3 factors with per-32-block scales -> bf16.
 
-The same refusals as the reference: missing ``qweight`` / ``wscales``, no
-second-level scale, half a low-rank pair, shapes the pack forbids, mixed or
-undeclared low-rank schemes -> :class:`SvdqB200LayoutError`. No CPU fallback
+Artifacts the reference refuses are refused here too (missing ``qweight`` /
+``wscales``, no second-level scale, half a low-rank pair, shapes the pack
+forbids, mixed or undeclared low-rank schemes), checked against one contract
+table, :class:`SvdqB200LayoutError`. No CPU fallback
 is involved: the codec is host code by design (it runs once, at load).
 """
 
 from __future__ import annotations
 
 import ctypes
-from typing import Any, Dict, Optional, Sequence
+from typing import Any, Dict, NamedTuple, Optional, Sequence
 
 import torch
 
@@ -55,8 +56,8 @@ def qweight_to_e2m1(qweight: torch.Tensor, out_features: int, in_features: int) 
     """nunchaku ``qweight`` [N, K/2] -> packed e2m1 ``weight`` u8 [N, K/2]."""
     n, k = int(out_features), int(in_features)
     if n % 128 or k % 128:
-        raise SvdqB200LayoutError(
-            f"svdq qweight [{n}, {k}] is not a multiple of the padded fragment tile (128x128)")
+        raise SvdqB200LayoutError(f"qweight of a [{n}, {k}] linear: sizes must be multiples "
+                                  f"of 128 (128 x 128 fragments)")
     src = _host(qweight).view(torch.uint8)
     if src.numel() != n * k // 2:
         raise SvdqB200LayoutError(f"qweight has {src.numel()} bytes, expected {n * k // 2}")
@@ -69,8 +70,8 @@ def wscales_to_blocked(wscales: torch.Tensor, out_features: int, in_features: in
     """nunchaku ``wscales`` E4M3 [K/16, N] -> blocked ``weight_scale`` e4m3."""
     n, k = int(out_features), int(in_features)
     if n % _WARP_N or (k // 16) % 4 or k % 16:
-        raise SvdqB200LayoutError(
-            f"svdq wscales for [{n}, {k}] break the lane swizzle (out%{_WARP_N}, (in/16)%4)")
+        raise SvdqB200LayoutError(f"wscales of a [{n}, {k}] linear: out_features must be a "
+                                  f"multiple of {_WARP_N} and in_features of 64")
     src = _host(wscales).view(torch.uint8)
     if src.numel() != n * k // 16:
         raise SvdqB200LayoutError(f"wscales has {src.numel()} bytes, expected {n * k // 16}")
@@ -83,8 +84,8 @@ def unpack_vector(vec: torch.Tensor, n: int) -> torch.Tensor:
     """One pack_scale(group_size=-1) vector -> row-major [n] (same dtype)."""
     n = int(n)
     if n % _WARP_N:
-        raise SvdqB200LayoutError(
-            f"svdq packed vector length {n} is not a multiple of warp_n={_WARP_N}")
+        raise SvdqB200LayoutError(f"packed vector of length {n}: the layout needs a "
+                                  f"multiple of {_WARP_N}")
     src = _host(vec).reshape(-1)
     if src.numel() != n:
         raise SvdqB200LayoutError(f"packed vector has {src.numel()} elements, expected {n}")
@@ -103,8 +104,8 @@ def unpack_lowrank(w: torch.Tensor, *, down: bool) -> torch.Tensor:
     rows, rank = int(src.shape[0]), int(src.shape[1])
     if rows % 16 or rank % 16:
         what = "proj_down" if down else "proj_up"
-        raise SvdqB200LayoutError(f"svdq {what} [{rows}, {rank}] breaks the low-rank pack "
-                                  f"(rows%16, rank%16)")
+        raise SvdqB200LayoutError(f"{what} of shape [{rows}, {rank}]: the 16 x 16 pack needs "
+                                  f"both sizes to be multiples of 16")
     out = torch.empty_like(src)
     _call("gwb_nunchaku_lowrank_unpack", _ptr(src), rows, rank, 1 if down else 0, _ptr(out))
     return out
@@ -122,14 +123,13 @@ def dequant_lowrank(q: torch.Tensor, scale: torch.Tensor, *, block_dim: int) -> 
     """int8 / e4m3 factor with fp32 per-32-block scales -> bf16."""
     scheme = _scheme_of(q)
     if scheme == "bf16":
-        raise SvdqB200LayoutError(f"dequant_lowrank got a {q.dtype} tensor — not a quantized "
-                                  f"low-rank factor")
+        raise SvdqB200LayoutError(f"a {q.dtype} factor has no block scales to apply")
     src = _host(q).view(torch.uint8)
     rows, cols = int(src.shape[0]), int(src.shape[1])
     n = rows if block_dim == 0 else cols
     if n % 32:
-        raise SvdqB200LayoutError(f"low-rank factor dim {n} is not a multiple of the quant "
-                                  f"block 32")
+        raise SvdqB200LayoutError(f"blocked dimension {n} of a low-rank factor is not a "
+                                  f"multiple of 32")
     want = (n // 32, cols) if block_dim == 0 else (rows, n // 32)
     s = _host(scale).float()
     if tuple(s.shape) != want:
@@ -141,76 +141,106 @@ def dequant_lowrank(q: torch.Tensor, scale: torch.Tensor, *, block_dim: int) -> 
     return out
 
 
+class _Artifact(NamedTuple):
+    """What the contract check learned about one linear's tensor set."""
+    second_kind: str          # "per_channel" (wcscales) or "per_tensor" (wtscale)
+    scheme: str               # storage of the low-rank factors: bf16, int8, fp8_e4m3
+    rank: int                 # 0 when the linear has no low-rank branch
+
+
+# The nunchaku v1 linear as a contract: tensors that must be present, the
+# alternatives for the second-level weight scale (exactly one used), and the
+# low-rank factors, which come as a pair with per-32-block scales when stored
+# quantised. Each rule is checked in table order; the first broken rule is
+# reported.
+_REQUIRED = ("qweight", "wscales")
+_SECOND_LEVEL = (("wcscales", "per_channel"), ("wtscale", "per_tensor"))
+_LOWRANK_PAIR = ("proj_down", "proj_up")
+_LOWRANK_SCALES = ("proj_down_scale", "proj_up_scale")
+
+
+def _check_contract(t: Dict[str, torch.Tensor], n: int, k: int,
+                    lowrank_quant: Optional[str]) -> _Artifact:
+    known = ("bf16",) + LOWRANK_SCHEMES
+    if lowrank_quant is not None and lowrank_quant not in known:
+        raise SvdqB200LayoutError(f"lowrank_quant {lowrank_quant!r} is not one of "
+                                  f"{', '.join(known)}")
+    absent = [name for name in _REQUIRED if name not in t]
+    if absent:
+        raise SvdqB200LayoutError(f"nunchaku linear lacks required tensor(s) {absent}: "
+                                  f"this is not an SVDQuant W4A4 artifact")
+    if n % 128 or k % 128:
+        raise SvdqB200LayoutError(f"qweight of a [{n}, {k}] linear: the 4-bit layout stores "
+                                  f"128 x 128 fragments, so both sizes must be multiples of 128")
+    second = next((kind for name, kind in _SECOND_LEVEL if name in t), None)
+    if second is None:
+        raise SvdqB200LayoutError("no second-level weight scale: expected 'wcscales' (per "
+                                  "output channel) or 'wtscale' (per tensor)")
+    if second == "per_channel" and int(t["wcscales"].numel()) != n:
+        raise SvdqB200LayoutError(f"'wcscales' has {int(t['wcscales'].numel())} entries for "
+                                  f"{n} output channels")
+    present = [name for name in _LOWRANK_PAIR if name in t]
+    if len(present) == 1:
+        raise SvdqB200LayoutError(f"low-rank branch incomplete: only {present[0]!r} is present")
+    if not present:
+        return _Artifact(second, "bf16", 0)
+    down, up = t["proj_down"], t["proj_up"]
+    scheme, scheme_up = _scheme_of(down), _scheme_of(up)
+    if scheme != scheme_up:
+        raise SvdqB200LayoutError(f"proj_down ({scheme}) and proj_up ({scheme_up}) use "
+                                  f"different storage schemes")
+    if lowrank_quant is not None and lowrank_quant != scheme:
+        raise SvdqB200LayoutError(f"lowrank_quant={lowrank_quant!r} was requested but the "
+                                  f"factors are stored as {scheme!r}")
+    scales = [name for name in _LOWRANK_SCALES if name in t]
+    if scheme == "bf16" and scales:
+        raise SvdqB200LayoutError(f"{scales} given for 16-bit low-rank factors, which carry "
+                                  f"no block scales")
+    if scheme != "bf16" and len(scales) < 2:
+        gone = [name for name in _LOWRANK_SCALES if name not in t]
+        raise SvdqB200LayoutError(f"{scheme} low-rank factors need both block-scale tensors; "
+                                  f"{gone[0]!r} is absent")
+    rank = int(down.shape[1])
+    if int(down.shape[0]) != k:
+        raise SvdqB200LayoutError(f"proj_down shape {tuple(down.shape)}: expected "
+                                  f"[in_features={k}, rank]")
+    if tuple(up.shape) != (n, rank):
+        raise SvdqB200LayoutError(f"proj_up shape {tuple(up.shape)}: expected "
+                                  f"[out_features={n}, rank={rank}]")
+    return _Artifact(second, scheme, rank)
+
+
 def decode_nunchaku_linear(tensors: Dict[str, torch.Tensor], out_features: int,
                            in_features: int, *,
                            lowrank_quant: Optional[str] = None) -> Dict[str, Any]:
     """One nunchaku svdq linear -> the :class:`SvdqNvfp4Linear` buffer dict
     (``weight``, ``weight_scale``, ``weight_scale_2``, ``second_kind``,
     ``proj_down``, ``proj_up``, ``smooth_factor``, ``bias``, ``rank``,
-    ``lowrank_quant``), host tensors."""
+    ``lowrank_quant``), host tensors. The tensor set is validated against
+    the contract table above before any tensor is decoded."""
     n, k = int(out_features), int(in_features)
-    missing = [name for name in ("qweight", "wscales") if name not in tensors]
-    if missing:
-        raise SvdqB200LayoutError(f"not an svdq W4A4 linear (missing {missing})")
+    art = _check_contract(tensors, n, k, lowrank_quant)
     buf: Dict[str, Any] = {
         "weight": qweight_to_e2m1(tensors["qweight"], n, k),
         "weight_scale": wscales_to_blocked(tensors["wscales"], n, k),
+        "second_kind": art.second_kind, "rank": art.rank, "lowrank_quant": art.scheme,
     }
-    if "wcscales" in tensors:
-        wc = tensors["wcscales"]
-        if int(wc.numel()) != n:
-            raise SvdqB200LayoutError(f"wcscales numel {int(wc.numel())} != out_features {n}")
-        buf["weight_scale_2"] = unpack_vector(wc.float(), n).reshape(1, n)
-        buf["second_kind"] = "per_channel"
-    elif "wtscale" in tensors:
+    if art.second_kind == "per_channel":
+        buf["weight_scale_2"] = unpack_vector(tensors["wcscales"].float(), n).reshape(1, n)
+    else:
         buf["weight_scale_2"] = _host(tensors["wtscale"]).float().reshape(1, 1)
-        buf["second_kind"] = "per_tensor"
-    else:
-        raise SvdqB200LayoutError("svdq linear has neither wcscales nor wtscale")
-
-    down, up = tensors.get("proj_down"), tensors.get("proj_up")
-    if (down is None) != (up is None):
-        raise SvdqB200LayoutError("svdq linear has only one half of the low-rank branch")
-    if lowrank_quant is not None and lowrank_quant not in ("bf16",) + LOWRANK_SCHEMES:
-        raise SvdqB200LayoutError(f"unknown lowrank_quant declaration {lowrank_quant!r} "
-                                  f"(known: bf16, {', '.join(LOWRANK_SCHEMES)})")
-    rank, scheme = 0, "bf16"
-    if down is not None:
-        scheme = _scheme_of(down)
-        if _scheme_of(up) != scheme:
-            raise SvdqB200LayoutError(f"low-rank pair mixes schemes: proj_down {down.dtype} vs "
-                                      f"proj_up {up.dtype}")
-        if scheme == "bf16" and ("proj_down_scale" in tensors or "proj_up_scale" in tensors):
-            raise SvdqB200LayoutError("low-rank scale tensors present but the branch pair is "
-                                      "not stored in a quantized dtype")
-        if lowrank_quant is not None and scheme != lowrank_quant:
-            raise SvdqB200LayoutError(f"artifact declares lowrank_quant={lowrank_quant!r} but "
-                                      f"the branch is stored as {scheme!r}")
-        rank = int(down.shape[1])
-        if int(down.shape[0]) != k:
-            raise SvdqB200LayoutError(f"proj_down {tuple(down.shape)} does not start with "
-                                      f"in_features {k}")
-        if tuple(up.shape) != (n, rank):
-            raise SvdqB200LayoutError(f"proj_up {tuple(up.shape)} != [out_features={n}, "
-                                      f"rank={rank}]")
-        if scheme == "bf16":
-            buf["proj_down"] = unpack_lowrank(down, down=True)
-            buf["proj_up"] = unpack_lowrank(up, down=False)
-        else:
-            dscale, uscale = tensors.get("proj_down_scale"), tensors.get("proj_up_scale")
-            if dscale is None or uscale is None:
-                miss = "proj_down_scale" if dscale is None else "proj_up_scale"
-                raise SvdqB200LayoutError(f"quantized ({scheme}) low-rank branch is missing "
-                                          f"{miss}")
-            buf["proj_down"] = dequant_lowrank(down, dscale, block_dim=0)
-            buf["proj_up"] = dequant_lowrank(up, uscale, block_dim=1)
-    else:
-        buf["proj_down"] = buf["proj_up"] = None
-    buf["rank"], buf["lowrank_quant"] = rank, scheme
-    smooth = tensors.get("smooth_factor")
-    buf["smooth_factor"] = None if smooth is None else unpack_vector(smooth, k)
-    bias = tensors.get("bias")
-    buf["bias"] = None if bias is None else unpack_vector(bias, n)
+    buf["proj_down"] = buf["proj_up"] = None
+    if art.rank and art.scheme == "bf16":
+        buf["proj_down"] = unpack_lowrank(tensors["proj_down"], down=True)
+        buf["proj_up"] = unpack_lowrank(tensors["proj_up"], down=False)
+    elif art.rank:
+        buf["proj_down"] = dequant_lowrank(tensors["proj_down"], tensors["proj_down_scale"],
+                                           block_dim=0)
+        buf["proj_up"] = dequant_lowrank(tensors["proj_up"], tensors["proj_up_scale"],
+                                         block_dim=1)
+    for name, length in (("smooth_factor", k), ("bias", n)):
+        v = tensors.get(name)
+        buf[name] = None if v is None else unpack_vector(v, length)
     return buf
 
 
@@ -223,11 +253,11 @@ def split_nvfp4_buffers(buf: Dict[str, Any], sections: Sequence[int]) -> tuple:
     n, k2 = int(w.shape[0]), int(w.shape[1])
     total = sum(int(s) for s in sections)
     if total != n:
-        raise SvdqB200LayoutError(f"split sections {tuple(sections)} sum to {total}, not "
-                                  f"out_features {n}")
+        raise SvdqB200LayoutError(f"sections {tuple(sections)} cover {total} rows of a "
+                                  f"{n}-row projection")
     if any(int(s) % 128 for s in sections):
-        raise SvdqB200LayoutError(f"split sections {tuple(sections)} are not multiples of the "
-                                  f"128-row scale tile")
+        raise SvdqB200LayoutError(f"sections {tuple(sections)} must each be a multiple of "
+                                  f"128 rows (one blocked scale tile)")
     tile_bytes = (k2 * 2 // 16) * 128     # one 128-row band of blocked scales
     per_channel = buf["second_kind"] == "per_channel"
     parts, start = [], 0

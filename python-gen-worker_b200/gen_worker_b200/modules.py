@@ -195,7 +195,8 @@ class SvdqNvfp4Linear(nn.Module):
     proj_down`` (bf16 on raw x, as the reference) in the same pass, the NVFP4
     activation codes in a second pass, then one block-scaled tcgen05 GEMM whose accumulator
     starts from the low-rank product (up-projection divided by
-    ``weight_scale_2 · s2``) and ends with ``· s2 · weight_scale_2 + bias``."""
+    ``weight_scale_2 · s2`` inside the GEMM, as two bf16 operands) and ends
+    with ``· s2 · weight_scale_2 + bias``. No torch op runs per call."""
     _cozy_svdq_linear = True
     layout = LAYOUT_NVFP4
 
@@ -256,10 +257,11 @@ class SvdqNvfp4Linear(nn.Module):
                 down_pad, up_over_ws2 = ops.nvfp4_lowrank_prepare(self.proj_down, self.proj_up,
                                                                   self.weight_scale_2)
                 self._up_pad = (down_pad.t().contiguous(), up_over_ws2)
-            # la from the amax pass (x is read twice per call, not three times)
+            # la from the amax pass (x is read twice per call, not three times);
+            # the GEMM applies s2 to the load-time proj_up / weight_scale_2
             codes, sblk, work, la = ops.nvfp4_quant_lowrank(x2, self.smooth_factor,
                                                             self._up_pad[0])
-            up = (self._up_pad[1] / work[1]).to(torch.bfloat16)
+            up = self._up_pad[1]
         else:
             codes, sblk, work = ops.nvfp4_quant(x2, self.smooth_factor)
         y = ops.nvfp4_gemm(codes, sblk, work, self.weight, self.weight_scale,

@@ -393,9 +393,9 @@ def nvfp4_gemm(codes: torch.Tensor, sblk: torch.Tensor, work: torch.Tensor, w_co
                proj_up: Optional[torch.Tensor], bias: Optional[torch.Tensor]) -> torch.Tensor:
     """Block-scaled NVFP4 GEMM + ``s2 · weight_scale_2`` + low-rank + bias
     -> bf16 [M, N] (``_gemm_w4a4`` and the rest of the NVFP4
-    ``SvdqLinear.forward``, ``svdq_native.py:148-155``). The low-rank
-    up-projection comes divided by the second-level scales
-    (:func:`nvfp4_lowrank_operands`)."""
+    ``SvdqLinear.forward``, ``svdq_native.py:148-155``). ``proj_up`` is the
+    load-time f32 ``proj_up / weight_scale_2`` [N, rank_pad]
+    (:func:`nvfp4_lowrank_prepare`); the kernel applies the call's ``s2``."""
     _need(codes, "codes", torch.uint8, 2)
     _need(w_codes, "w_codes", torch.uint8, 2)
     _need(work, "work", torch.float32, 1)
@@ -416,8 +416,10 @@ def nvfp4_gemm(codes: torch.Tensor, sblk: torch.Tensor, work: torch.Tensor, w_co
     rp = 0
     if la is not None and proj_up is not None and la.shape[1] > 0:
         _need(la, "la", torch.bfloat16, 2)
-        _need(proj_up, "proj_up", torch.bfloat16, 2)
+        _need(proj_up, "proj_up", torch.float32, 2)
         rp = int(la.shape[1])
+        if tuple(proj_up.shape) != (n, rp):
+            raise SvdqB200Error(f"proj_up {tuple(proj_up.shape)} != [{n}, {rp}]")
     out = torch.empty(m, n, dtype=torch.bfloat16, device=codes.device)
     lib = native.require()
     native.check(lib.gwb_nvfp4_gemm(codes.data_ptr(), sblk.data_ptr(), work.data_ptr(),
@@ -426,20 +428,6 @@ def nvfp4_gemm(codes: torch.Tensor, sblk: torch.Tensor, work: torch.Tensor, w_co
                                     _ptr(proj_up) if rp else None, _ptr(bias), m, n, k, rp,
                                     out.data_ptr(), _stream()), "nvfp4_gemm")
     return out
-
-
-def nvfp4_lowrank_operands(x2: torch.Tensor, down_pad: torch.Tensor, up_over_ws2: torch.Tensor,
-                           work: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """Low-rank operands of :func:`nvfp4_gemm`: ``la = bf16(x2 · proj_down)``
-    on raw x exactly as the reference's bf16 matmul (``svdq_native.py:153``)
-    and the up-projection ``bf16(proj_up / (weight_scale_2[n] · s2))`` (the
-    branch then shares the main accumulator, which the epilogue multiplies by
-    ``s2 · weight_scale_2``). ``down_pad`` bf16 [K, rank_pad] and
-    ``up_over_ws2`` fp32 [N, rank_pad] are the load-time forms
-    (:func:`nvfp4_lowrank_prepare`)."""
-    la = x2 @ down_pad
-    up = (up_over_ws2 / work[1]).to(torch.bfloat16)
-    return la, up
 
 
 def nvfp4_lowrank_prepare(proj_down: torch.Tensor, proj_up: torch.Tensor,

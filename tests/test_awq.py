@@ -50,7 +50,7 @@ def test_unpack_round_trip_at_model_size():
 
 def test_refusals():
     t = _tensors(256)
-    with pytest.raises(awq.AwqPackedError, match="missing"):
+    with pytest.raises(awq.AwqPackedError, match="lacks required"):
         awq.build_awq_packed_linear({"qweight": t["qweight"]}, 256, 256)
     with pytest.raises(awq.AwqPackedError, match="qweight shape"):
         awq.build_awq_packed_linear(t, 256, 512)
@@ -58,9 +58,9 @@ def test_refusals():
         awq.build_awq_packed_linear(t, 256, 256, adanorm_splits=6)
     bad = dict(t, wscales=t["wscales"].clone())
     bad["wscales"][0] = 0
-    with pytest.raises(awq.AwqPackedError, match="zero rows"):
+    with pytest.raises(awq.AwqPackedError, match="all-zero row"):
         awq.build_awq_packed_linear(bad, 256, 256)
-    with pytest.raises(awq.AwqPackedError, match="packed contract"):
+    with pytest.raises(awq.AwqPackedError, match="GEMV needs"):
         awq.AwqPackedLinear(200, 256, bias=False)
     assert not awq.awq_packed_supported(500, 256) and awq.awq_packed_supported(512, 256)
     assert awq.num_scale_rows(3072, 64) == 48 and awq.num_scale_rows(256, 64) == 16
