@@ -185,6 +185,26 @@ def build_stack(device, seed: int = 0):
     return layers
 
 
+def weight_bytes(layers) -> int:
+    """Device bytes the GEMMs read as weights per step: the stored codes and
+    scales (or their load-time operand form), the padded low-rank factors
+    and the biases."""
+    total = 0
+    for _, mods in layers:
+        for mod in mods:
+            p = mod.prepare()
+            if mod.stored:
+                total += mod.weight.numel() + mod.weight_scale.numel() * 2
+            else:
+                total += p["w_q8"].numel() + p["w_scale_k8"].numel() * 2
+            for key in ("proj_down_t", "proj_up_pad"):
+                if p.get(key) is not None:
+                    total += p[key].numel() * 2
+            if mod.bias is not None:
+                total += mod.bias.numel() * 2
+    return total
+
+
 def run_stack(layers, x, side15360, timer=None):
     """One forward of the stack. Dual block: qkv(x); out(x); fc1 -> fc2 -> x.
     Single block: qkv_mlp(x); h = out(side) (the attention/MLP concat feeding
@@ -215,12 +235,10 @@ class GemmTimer:
     def __call__(self, mod, x):
         from gen_worker_b200 import ops
         x2 = x.reshape(-1, mod.in_features)
-        p = mod.prepare()
-        codes, ascale, la = ops.svdq_w4a4_quant_mma(x2, mod.smooth_factor, p["proj_down_t"])
+        q = mod.quantize(x2)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        y = ops.svdq_w4a4_gemm(codes, ascale, p["w_q8"], p["w_scale_k8"], la,
-                               p["proj_up_pad"], mod.bias.detach(), mod.gelu)
+        y = mod.gemm(*q)
         e.record()
         self.pairs.append((s, e, 2.0 * x2.shape[0] * mod.in_features * mod.out_features))
         return y
@@ -460,11 +478,9 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
             e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
             e[0].record()
             if kind == "w4a4":
-                p = mod.prepare()
-                c, a, la = ops.svdq_w4a4_quant_mma(xb, mod.smooth_factor, p["proj_down_t"])
+                q4 = mod.quantize(xb)
                 e[1].record()
-                ops.svdq_w4a4_gemm(c, a, p["w_q8"], p["w_scale_k8"], la, p["proj_up_pad"],
-                                   mod.bias.detach(), gelu)
+                mod.gemm(*q4)
             elif kind == "nvfp4":
                 # the module's own path: load-time low-rank forms cached by a
                 # first forward, la from the amax pass
@@ -494,10 +510,8 @@ def run_case(name: str, steps: int, warmup: int) -> dict:
         # operands (warm L2, no host-side issue cost): the figure comparable
         # with a library GEMM timed the same way
         if kind == "w4a4":
-            p = mod.prepare()
-            c, a, la = ops.svdq_w4a4_quant_mma(xb, mod.smooth_factor, p["proj_down_t"])
-            gemm_call = lambda: ops.svdq_w4a4_gemm(c, a, p["w_q8"], p["w_scale_k8"], la,  # noqa: E731
-                                                   p["proj_up_pad"], mod.bias.detach(), gelu)
+            q4 = mod.quantize(xb)
+            gemm_call = lambda: mod.gemm(*q4)  # noqa: E731
         elif kind == "nvfp4":
             c, sb_, wk, la = ops.nvfp4_quant_lowrank(xb, mod.smooth_factor, mod._up_pad[0])
             upp = mod._up_pad[1]
@@ -766,6 +780,7 @@ def main() -> int:
         raise SystemExit(f"{TOKENS} tokens do not split evenly over {world} ranks")
     m = TOKENS // world
     layers = build_stack(dev)
+    wbytes = weight_bytes(layers)
     g = torch.Generator(device=dev).manual_seed(99)
     x_full = torch.randn(TOKENS, HIDDEN, generator=g, device=dev)
     idx = torch.randperm(HIDDEN, generator=g, device=dev)[:31]
@@ -864,7 +879,9 @@ def main() -> int:
             "config": {"workload": "cfg4 Flux DiT W4A4 linear stack, 19 dual + 38 single blocks",
                        "tokens": TOKENS, "tokens_per_rank": m, "hidden": HIDDEN, "rank": RANK,
                        "group": 64, "parallelism": f"token-shard x{world}, weights replicated",
-                       "l2": "no flush: per-step working set 8.1 GB of distinct weight operands (>> 126 MB L2)"},
+                       "weights_gb": wbytes / 1e9,
+                       "l2": ("no flush: per-step working set %.1f GB of distinct weights "
+                              "(>> 126 MB L2)" % (wbytes / 1e9))},
             "effective_tops": stack_ops() * TOKENS / (ms_max / 1e3) / 1e12,
             "lowrank_tops_excluded": lowrank_ops() * TOKENS / (ms_max / 1e3) / 1e12,
             "roofline": {"bound": "tensor", "kernel": "gemm_w4a4_kernel",

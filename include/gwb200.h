@@ -18,7 +18,8 @@
  *                                0 2 4 6 1 3 5 7
  * Group scales, GEMM scale-operand rows (gwb_svdq_w4a4_scale_k8 converts,
  * gwb_svdq_w4a4_quant_mma writes them directly):
- *   scale_k8     f16  [G, R, 8]  scale at k = 0, zeros at k = 1..7
+ *   scale_k8     f16  [G, R, 8]  group g's scale at k = g mod 8, zeros at
+ *                                the other seven k
  * Other tensors:
  *   x            bf16 [M, K];  smooth bf16 [K] (or NULL)
  *   proj_down_t  bf16 [rank_pad, K]   (L1 transposed; rows >= rank are zero)
@@ -112,6 +113,37 @@ int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_dow
                          const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
                          int gelu, void* a_q8, void* a_scale_k8, void* la, void* out,
                          void* stream);
+
+/* Replaces `cozy_gen_worker::svdq_gemm_w4a4_lora(qa, sa, wq_kn, ws, ...)`
+ * (reference svdq_fused.py:379-383) with the weight as stored: w_codes
+ * u8 [N, K/2] packed INT4 and w_scale f16 [N, G] (the module's `weight` /
+ * `weight_scale` buffers, no load-time repack). The kernel TMA-loads the
+ * packed weight tiles and expands them to the e4m3 operand layout in shared
+ * memory; the stored scale rows (8 groups per 16 bytes) are the B side of
+ * the scale MMA, selected per group by the one-hot activation scale rows.
+ * Activations in operand form (gwb_svdq_w4a4_quant_mma). G % 8 == 0
+ * (K % 512 == 0). */
+int gwb_svdq_w4a4_gemm_stored(const void* a_q8, const void* a_scale_k8, const void* w_codes,
+                              const void* w_scale, const void* la, const void* proj_up,
+                              const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
+                              int gelu, void* out, void* stream);
+
+/* The same with the activations as packed codes [M, K/2] too (both operands
+ * expanded in shared memory; a_scale_k8 from gwb_svdq_w4a4_scale_k8). */
+int gwb_svdq_w4a4_gemm_packed_stored(const void* codes, const void* a_scale_k8,
+                                     const void* w_codes, const void* w_scale, const void* la,
+                                     const void* proj_up, const void* bias, int64_t M, int64_t N,
+                                     int64_t K, int rank_pad, int gelu, void* out, void* stream);
+
+/* Whole SvdqLinear forward (reference svdq_native.py:140-156) on the
+ * weights as stored: gwb_svdq_w4a4_quant_mma into the caller's scratch
+ * (a_q8 [M, K], a_scale_k8 [G, M, 8], la [M, rank_pad]), then
+ * gwb_svdq_w4a4_gemm_stored. */
+int gwb_svdq_w4a4_linear_stored(const void* x, const void* smooth, const void* proj_down_t,
+                                const void* w_codes, const void* w_scale, const void* proj_up,
+                                const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
+                                int gelu, void* a_q8, void* a_scale_k8, void* la, void* out,
+                                void* stream);
 
 /* No counterpart in the reference. The same computation as
  * gwb_svdq_w4a4_linear for callers that cannot allocate device memory (their

@@ -143,13 +143,22 @@ __device__ __forceinline__ void quant_seg16(const uint32_t (&xw)[8], const float
   scale_out = sh;
 }
 
+// One scale-operand row: the 16-bit scale `bits` at k = g mod 8, zeros at the
+// other seven k (the row of group g in the one-hot [G, R, 8] form).
+__device__ __forceinline__ uint4 onehot_k8(uint32_t bits, int g) {
+  const uint32_t w = bits << (16 * (g & 1));
+  const int q = (g >> 1) & 3;
+  return make_uint4(q == 0 ? w : 0u, q == 1 ? w : 0u, q == 2 ? w : 0u, q == 3 ? w : 0u);
+}
+
 // NB = padded rank / 8 (0 = no low-rank branch); MT = m16 row tiles per CTA
 // (16 * MT rows); act_warps<MT>() warps split K round-robin in 64-wide chunks.
 // MMA_FORM = false writes the interchange form: packed codes u8 [M, K/2] and
 // ascale f16 [M, K/64]. MMA_FORM = true writes the GEMM operand form: codes
 // u8 [M, K] as e4m3 bytes of q * 2^-9 in the within-8 operand order
 // (unpack8_e4m3), and the scales as scale-operand rows f16 [K/64, M, 8]
-// (scale at k = 0, zeros at k = 1..7: one 16-byte TMA row per matrix row).
+// (group g's scale at k = g mod 8, zeros elsewhere: one 16-byte TMA row per
+// matrix row).
 // la = bf16(x · L1) on raw x: each warp accumulates its K chunks with
 // mma.sync; the per-warp partials are summed in a fixed order through
 // shared memory, so la is deterministic.
@@ -262,7 +271,7 @@ act_int4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
                 make_uint4(lo, hi, e23[0], e23[1]);
             if (c == 0)
               *reinterpret_cast<uint4*>(ascale + ((size_t)kc * M + row) * 8) =
-                  make_uint4(__half_as_ushort(sc), 0u, 0u, 0u);
+                  onehot_k8(__half_as_ushort(sc), kc);
           } else {
             *reinterpret_cast<uint2*>(codes + (size_t)row * (K / 2) + k0 / 2) = make_uint2(lo, hi);
             if (c == 0) ascale[(size_t)row * G + kc] = sc;
@@ -359,14 +368,14 @@ int launch_act_int4(const void* x, const void* smooth, const void* down_t, void*
 }
 
 // Scale interchange form f16 [R, K/64] -> GEMM scale-operand rows
-// f16 [K/64, R, 8] (scale at k = 0, zeros at k = 1..7).
+// f16 [K/64, R, 8] (group g's scale at k = g mod 8, zeros elsewhere).
 __global__ void scale_k8_kernel(const __half* __restrict__ scale, uint4* __restrict__ scale_k8,
                                 int R, int G) {
   const int64_t n = (int64_t)R * G;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / G, g = i % G;
-    scale_k8[(size_t)g * R + r] = make_uint4(__half_as_ushort(scale[i]), 0u, 0u, 0u);
+    scale_k8[(size_t)g * R + r] = onehot_k8(__half_as_ushort(scale[i]), (int)g);
   }
 }
 

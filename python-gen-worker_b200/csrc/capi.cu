@@ -120,7 +120,7 @@ int gwb_svdq_w4a4_gemm(const void* a_q8, const void* a_scale_k8, const void* w_q
   if (rc) return rc;
   gwb::W4A4Args a{a_q8, a_scale_k8, w_q8, w_scale_k8, la, proj_up, bias, out, nullptr,
                   (int)M, (int)N, (int)K, rank_pad, gelu ? 1 : 0};
-  return gwb::launch_gemm_w4a4(a, false, S(stream));
+  return gwb::launch_gemm_w4a4(a, false, false, S(stream));
 }
 
 int gwb_svdq_w4a4_gemm_packed(const void* codes, const void* a_scale_k8, const void* w_q8,
@@ -132,7 +132,7 @@ int gwb_svdq_w4a4_gemm_packed(const void* codes, const void* a_scale_k8, const v
   if (rc) return rc;
   gwb::W4A4Args a{codes, a_scale_k8, w_q8, w_scale_k8, la, proj_up, bias, out, nullptr,
                   (int)M, (int)N, (int)K, rank_pad, gelu ? 1 : 0};
-  return gwb::launch_gemm_w4a4(a, true, S(stream));
+  return gwb::launch_gemm_w4a4(a, true, false, S(stream));
 }
 
 int gwb_svdq_w4a4_group_partials(const void* codes, const void* w_q8, int64_t M, int64_t N,
@@ -143,7 +143,7 @@ int gwb_svdq_w4a4_group_partials(const void* codes, const void* w_q8, int64_t M,
   if ((K / 64) * M * N > (int64_t)1 << 31) return GWB_E_CAPACITY;
   gwb::W4A4Args a{codes, nullptr, w_q8, nullptr, nullptr, nullptr, nullptr, nullptr,
                   partials, (int)M, (int)N, (int)K, 0, 0};
-  return gwb::launch_gemm_w4a4(a, true, S(stream));
+  return gwb::launch_gemm_w4a4(a, true, false, S(stream));
 }
 
 int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_down_t,
@@ -159,6 +159,45 @@ int gwb_svdq_w4a4_linear(const void* x, const void* smooth, const void* proj_dow
   if (rc) return rc;
   return gwb_svdq_w4a4_gemm(a_q8, a_scale_k8, w_q8, w_scale_k8, la, proj_up, bias, M, N, K,
                             rank_pad, gelu, out, stream);
+}
+
+int gwb_svdq_w4a4_gemm_stored(const void* a_q8, const void* a_scale_k8, const void* w_codes,
+                              const void* w_scale, const void* la, const void* proj_up,
+                              const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
+                              int gelu, void* out, void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  int rc = check_w4a4_shape(M, N, K, rank_pad);
+  if (rc) return rc;
+  gwb::W4A4Args a{a_q8, a_scale_k8, w_codes, w_scale, la, proj_up, bias, out, nullptr,
+                  (int)M, (int)N, (int)K, rank_pad, gelu ? 1 : 0};
+  return gwb::launch_gemm_w4a4(a, false, true, S(stream));
+}
+
+int gwb_svdq_w4a4_gemm_packed_stored(const void* codes, const void* a_scale_k8,
+                                     const void* w_codes, const void* w_scale, const void* la,
+                                     const void* proj_up, const void* bias, int64_t M, int64_t N,
+                                     int64_t K, int rank_pad, int gelu, void* out, void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  int rc = check_w4a4_shape(M, N, K, rank_pad);
+  if (rc) return rc;
+  gwb::W4A4Args a{codes, a_scale_k8, w_codes, w_scale, la, proj_up, bias, out, nullptr,
+                  (int)M, (int)N, (int)K, rank_pad, gelu ? 1 : 0};
+  return gwb::launch_gemm_w4a4(a, true, true, S(stream));
+}
+
+int gwb_svdq_w4a4_linear_stored(const void* x, const void* smooth, const void* proj_down_t,
+                                const void* w_codes, const void* w_scale, const void* proj_up,
+                                const void* bias, int64_t M, int64_t N, int64_t K, int rank_pad,
+                                int gelu, void* a_q8, void* a_scale_k8, void* la, void* out,
+                                void* stream) {
+  if (M == 0) return GWB_SUCCESS;
+  int rc = check_w4a4_shape(M, N, K, rank_pad);
+  if (rc) return rc;
+  rc = gwb_svdq_w4a4_quant_mma(x, smooth, proj_down_t, M, K, rank_pad, a_q8, a_scale_k8, la,
+                               stream);
+  if (rc) return rc;
+  return gwb_svdq_w4a4_gemm_stored(a_q8, a_scale_k8, w_codes, w_scale, la, proj_up, bias, M, N, K,
+                                   rank_pad, gelu, out, stream);
 }
 
 int gwb_w8a8_quant(const void* x, int64_t M, int64_t K, void* q, void* scale, void* stream) {

@@ -16,6 +16,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <cstdlib>
 #include "gwb.h"
 #include "ptx.cuh"
 
@@ -226,26 +227,39 @@ gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 // W4A4 (INT4 group-64, unpacked to int8 in shared memory)
 // ======================================================================
 namespace w4 {
-constexpr int BN = 128;
-constexpr int PSTAGES = 4;                 // packed A staging ring (TMA)
-constexpr int USTAGES = 4;                 // operand ring read by the MMA
-constexpr int PA_BYTES = kBM * kBK / 2;    // 8 KB packed A per k-block
-constexpr int PSTAGE_BYTES = PA_BYTES;
+constexpr int PSTAGES = 4;                 // packed-code staging ring (TMA)
 constexpr int UA_BYTES = kBM * kBK;        // 16 KB e4m3 A (unpacked here)
-constexpr int UB_BYTES = BN * kBK;         // 16 KB e4m3 B (TMA from the expanded weight)
-// Scale operand of one group and side: [128 rows x 16 k] f16, no-swizzle
-// K-major. TMA writes the k = 0..7 half (one 16-byte row per matrix row, only
-// k = 0 non-zero); the k = 8..15 half is the shared 2 KB zero block.
-constexpr int SOP_DATA = 128 * 16;         // 2 KB
-constexpr int USTAGE_BYTES = UA_BYTES + UB_BYTES + 4 * SOP_DATA;    // 40 KB
-constexpr int ZERO_OFF = USTAGES * USTAGE_BYTES + PSTAGES * PSTAGE_BYTES;
-constexpr int SMEM_BYTES = ZERO_OFF + SOP_DATA + 1024 + 256;
-// TMEM: [0, 2*BN) f32 group sums V0/V1, [2*BN, 4*BN) f32 scale products S0/S1
+// Scale operand of one group and side: [rows x 16 k] f16, no-swizzle
+// K-major. TMA writes the k = 0..7 half (one 16-byte row per matrix row: the
+// A side one-hot at k = g mod 8, the B side one-hot alike or the stored 8
+// groups g - g mod 8 .. +7); the k = 8..15 half is the shared 2 KB zero block.
+constexpr int SOPA = kBM * 16;             // 2 KB (A side, 128 rows)
+constexpr int ZERO_BYTES = SOPA;
 constexpr int TMEM_COLS = 512;
 constexpr int UNPACK_WARPS = 6;            // warps 2-7 (packed activations only)
 constexpr int UNPACK_THREADS = 32 * UNPACK_WARPS;
 constexpr int EPI_WARPS = 8;               // the last two warpgroups
-constexpr int EC = BN / 2;                 // columns per epilogue warp
+// Tile N width BN: 128 (two TMEM group buffers of V | S) or 64 (four).
+// TMEM: [0, NBUF*BN) f32 group sums V_b, [NBUF*BN, 512) f32 scale products S_b.
+template <bool A_PACKED, bool B_PACKED, int BN> struct Cfg {
+  static constexpr int NBUF = TMEM_COLS / (2 * BN);
+  static constexpr int UB_BYTES = BN * kBK;                 // e4m3 B
+  static constexpr int SOPB = BN * 16;                      // one B scale-operand tile
+  // per k-block scale operands: two A one-hot tiles, then one stored 8-group
+  // B tile (B_PACKED) or two B one-hot tiles
+  static constexpr int SCALE_BYTES = 2 * SOPA + (B_PACKED ? 1 : 2) * SOPB;
+  static constexpr int USTAGE_BYTES = UA_BYTES + UB_BYTES + SCALE_BYTES;
+  static constexpr int PA_STAGE = A_PACKED ? kBM * kBK / 2 : 0;   // packed A per k-block
+  static constexpr int PB_STAGE = B_PACKED ? BN * kBK / 2 : 0;    // packed B per k-block
+  static constexpr int FIXED = PSTAGES * (PA_STAGE + PB_STAGE) + ZERO_BYTES + 1024 + 256;
+  static constexpr int FIT = (232448 - FIXED) / USTAGE_BYTES;      // operand stages that fit
+  static constexpr int USTAGES = FIT < 6 ? FIT : 6;               // operand ring read by the MMA
+  static constexpr int ZERO_OFF = USTAGES * USTAGE_BYTES + PSTAGES * (PA_STAGE + PB_STAGE);
+  static constexpr int SMEM_BYTES = ZERO_OFF + ZERO_BYTES + 1024 + 256;
+  static constexpr int EC = BN / 2;                         // columns per epilogue warp
+  static_assert(USTAGES >= 3, "W4A4 operand ring too small");
+  static_assert(SMEM_BYTES <= 232448, "W4A4 shared memory exceeds 227 KB");
+};
 // packed activations: 16 warps (producer, MMA, 6 unpack, 8 epilogue);
 // operand-form activations: 12 warps (producer, MMA, 2 idle, 8 epilogue)
 template <bool A_PACKED> __host__ __device__ constexpr int threads() { return A_PACKED ? 512 : 384; }
@@ -257,7 +271,6 @@ constexpr float kUnscale = 262144.0f;      // 2^18
 constexpr float kRescale = 1.0f / 262144.0f;
 }  // namespace w4
 
-static_assert(w4::SMEM_BYTES <= 232448, "W4A4 shared memory exceeds 227 KB");
 
 // Unpack `chunks` 16-byte packed chunks (rows of 64 packed bytes, row-major,
 // no swizzle) into rows of 128 e4m3 bytes in the SWIZZLE_128B K-major layout.
@@ -314,40 +327,53 @@ __device__ __forceinline__ uint64_t sdesc_scale(uint32_t saddr, uint32_t lbo) {
   return d;
 }
 
-// A_PACKED: activations arrive as packed INT4 codes (TMA into a staging ring,
-// expanded to the operand layout by the unpack warps); otherwise as the
+// A_PACKED: activations arrive as packed INT4 codes (TMA into the staging
+// ring, expanded to the operand layout by the unpack warps); otherwise as the
 // operand form itself (u8 [M, K], TMA straight into the operand ring).
-template <bool A_PACKED>
-__global__ void __launch_bounds__(w4::threads<A_PACKED>(), 1)
+// B_PACKED: the weight arrives as stored, packed INT4 codes u8 [N, K/2]
+// (expanded in shared memory by the unpack warps) with its group scales as
+// stored, f16 [N, G]: TMA brings 8 groups per row (16 bytes, the no-swizzle
+// K-major core-matrix layout) and that tile is the B side of the scale MMA
+// of both groups of the k-block; the A side (one-hot at k = g mod 8, written
+// by the quantiser) selects the group. Otherwise the weight is the load-time
+// operand form (w_q8 u8 [N, K], w_scale_k8 one-hot rows).
+template <bool A_PACKED, bool B_PACKED, int BN>
+__global__ void __launch_bounds__(w4::threads<A_PACKED || B_PACKED>(), 1)
 gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmAS, const __grid_constant__ CUtensorMap tmBS,
                  const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmUP,
                  const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out,
                  int32_t* __restrict__ partials, int M, int N, int K, int rank_pad, int gelu) {
   using namespace w4;
-  constexpr int THREADS = threads<A_PACKED>();
-  constexpr int EPI0 = epi_warp0<A_PACKED>();
+  using C = Cfg<A_PACKED, B_PACKED, BN>;
+  constexpr bool UNPACK = A_PACKED || B_PACKED;
+  constexpr int NBUF = C::NBUF, USTAGES = C::USTAGES, USTAGE_BYTES = C::USTAGE_BYTES;
+  constexpr int UB_BYTES = C::UB_BYTES, SOPB = C::SOPB, SCALE_BYTES = C::SCALE_BYTES;
+  constexpr int PA = C::PA_STAGE, PB = C::PB_STAGE;
+  constexpr int EC = C::EC;
+  constexpr int THREADS = threads<UNPACK>();
+  constexpr int EPI0 = epi_warp0<UNPACK>();
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment by offsetting the __shared__ array itself, so the
   // compiler keeps emitting shared-space (not generic) loads and stores
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* ustage = smem;
   uint8_t* pstage = smem + USTAGES * USTAGE_BYTES;
-  uint8_t* zero = smem + ZERO_OFF;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(zero + SOP_DATA);
-  uint64_t* p_full = bars;                  // [PSTAGES] packed A landed (TMA)
+  uint8_t* zero = smem + C::ZERO_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(zero + ZERO_BYTES);
+  uint64_t* p_full = bars;                  // [PSTAGES] packed codes landed (TMA)
   uint64_t* p_empty = p_full + PSTAGES;     // [PSTAGES] unpack done reading
-  uint64_t* u_full = p_empty + PSTAGES;     // [USTAGES] unpack written + B/scales landed
+  uint64_t* u_full = p_empty + PSTAGES;     // [USTAGES] unpack written + TMA landed
   uint64_t* u_empty = u_full + USTAGES;     // [USTAGES] MMA done reading
-  uint64_t* acc_full = u_empty + USTAGES;   // [2]
-  uint64_t* acc_empty = acc_full + 2;       // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* acc_full = u_empty + USTAGES;   // [NBUF]
+  uint64_t* acc_empty = acc_full + NBUF;    // [NBUF]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + NBUF);
   uint32_t* unpack_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = K / kBK;
   const int G = K / 64;
-  const bool dump = partials != nullptr;
+  const bool dump = !B_PACKED && partials != nullptr;
   const int has_lr = (!dump && rank_pad > 0) ? 1 : 0;
   // the low-rank operands take one ring slot per 64 ranks (128-byte rows)
   const int lr_slots = has_lr ? (rank_pad + 63) / 64 : 0;
@@ -357,16 +383,16 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const int tiles_n = N / BN;
   const int ntiles = ((M + kBM - 1) / kBM) * tiles_n;
 
-  for (int i = threadIdx.x; i < SOP_DATA / 16; i += THREADS)
+  for (int i = threadIdx.x; i < ZERO_BYTES / 16; i += THREADS)
     reinterpret_cast<uint4*>(zero)[i] = make_uint4(0, 0, 0, 0);
   fence_proxy_async_smem();
   if (threadIdx.x == 0) {
     for (int i = 0; i < PSTAGES; ++i) { mbar_init(&p_full[i], 1); mbar_init(&p_empty[i], 1); }
     for (int i = 0; i < USTAGES; ++i) {
-      mbar_init(&u_full[i], A_PACKED ? 2 : 1);
+      mbar_init(&u_full[i], UNPACK ? 2 : 1);
       mbar_init(&u_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], EPI_WARPS); }
+    for (int i = 0; i < NBUF; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], EPI_WARPS); }
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -380,12 +406,12 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) GWB_TRACE_AT(7, 0);
 
-  // register hand-off. Packed activations: the launch gives 512 x 128 = 65536
+  // register hand-off. With unpack warps the launch gives 512 x 128 = 65536
   // registers; warpgroups 0-1 (producer, MMA, unpack) drop to 56 (14336) and
-  // the two epilogue warpgroups rise to 200 (51200). Operand form: 384 x 168 =
-  // 64512; warpgroup 0 drops to 48 (6144), the epilogue rises to 224 (57344).
+  // the two epilogue warpgroups rise to 200 (51200). Operand form only: 384 x
+  // 168 = 64512; warpgroup 0 drops to 48 (6144), the epilogue rises to 224 (57344).
   if (warp < EPI0) {
-    if constexpr (A_PACKED) regs_dec<56>();
+    if constexpr (UNPACK) regs_dec<56>();
     else regs_dec<48>();
     if (warp == 0 && lane == 0) {
       // -------------------------------------------------------------- TMA
@@ -399,22 +425,23 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         ok = mbar_wait(&u_empty[u], ((ui / USTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER);
         if (!ok) break;
         mbar_arrive_expect_tx(&u_full[u], kBM * 128 + BN * 128);
-        if (A_PACKED) mbar_arrive(&u_full[u]);
+        if (UNPACK) mbar_arrive(&u_full[u]);
         uint8_t* us = ustage + u * USTAGE_BYTES;
         tma_load_2d(us, &tmLA, &u_full[u], 64 * h, m0);
         tma_load_2d(us + UA_BYTES, &tmUP, &u_full[u], 64 * h, n0);
       }
       if (!ok) break;
       for (int kb = 0; kb < nk; ++kb, ++ui) {
-        if (A_PACKED) {
+        if (UNPACK) {
           const int s = pk % PSTAGES;
           if (!mbar_wait(&p_empty[s], ((pk / PSTAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) {
             ok = false;
             break;
           }
-          uint8_t* ps = pstage + s * PSTAGE_BYTES;
-          mbar_arrive_expect_tx(&p_full[s], PSTAGE_BYTES);
-          tma_load_2d(ps, &tmA, &p_full[s], kb * (kBK / 2), m0);
+          uint8_t* ps = pstage + s * (PA + PB);
+          mbar_arrive_expect_tx(&p_full[s], PA + PB);
+          if (A_PACKED) tma_load_2d(ps, &tmA, &p_full[s], kb * (kBK / 2), m0);
+          if (B_PACKED) tma_load_2d(ps + PA, &tmB, &p_full[s], kb * (kBK / 2), n0);
           ++pk;
         }
         GWB_TRACE_AT(0, ui);
@@ -424,17 +451,24 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           break;
         }
         uint8_t* us = ustage + u * USTAGE_BYTES;
-        const uint32_t a_tx = A_PACKED ? 0u : (uint32_t)UA_BYTES;
-        mbar_arrive_expect_tx(&u_full[u], a_tx + (dump ? UB_BYTES : UB_BYTES + 4 * SOP_DATA));
+        const uint32_t tx = (A_PACKED ? 0u : (uint32_t)UA_BYTES) +
+                            (B_PACKED ? 0u : (uint32_t)UB_BYTES) + (dump ? 0u : SCALE_BYTES);
+        mbar_arrive_expect_tx(&u_full[u], tx);
         if (!A_PACKED) tma_load_2d(us, &tmA, &u_full[u], kb * kBK, m0);
-        tma_load_2d(us + UA_BYTES, &tmB, &u_full[u], kb * kBK, n0);
+        if (!B_PACKED) tma_load_2d(us + UA_BYTES, &tmB, &u_full[u], kb * kBK, n0);
         if (!dump) {
+          // scale area: [A g0 | A g1 | B]; B = the stored 8-group rows
+          // (B_PACKED) or the two groups' one-hot rows
           uint8_t* so = us + UA_BYTES + UB_BYTES;
 #pragma unroll
-          for (int gs = 0; gs < 2; ++gs) {
-            const int g = 2 * kb + gs;
-            tma_load_2d(so + (2 * gs) * SOP_DATA, &tmAS, &u_full[u], 0, g * M + m0);
-            tma_load_2d(so + (2 * gs + 1) * SOP_DATA, &tmBS, &u_full[u], 0, g * N + n0);
+          for (int gs = 0; gs < 2; ++gs)
+            tma_load_2d(so + gs * SOPA, &tmAS, &u_full[u], 0, (2 * kb + gs) * M + m0);
+          if (B_PACKED) {
+            tma_load_2d(so + 2 * SOPA, &tmBS, &u_full[u], 8 * (kb >> 2), n0);
+          } else {
+#pragma unroll
+            for (int gs = 0; gs < 2; ++gs)
+              tma_load_2d(so + 2 * SOPA + gs * SOPB, &tmBS, &u_full[u], 0, (2 * kb + gs) * N + n0);
           }
         }
       }
@@ -450,11 +484,11 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
       if (has_lr) {
         // the tile's first group slot <- la · proj_upᵀ (f32), 64 ranks per ring slot
-        const int b = gi & 1;
+        const int b = gi % NBUF;
         for (int h = 0; h < lr_slots; ++h, ++ui) {
           const int u = ui % USTAGES;
           ok = mbar_wait(&u_full[u], (ui / USTAGES) & 1, GWB_ERR_TIMEOUT_MMA) &&
-               (h > 0 || mbar_wait(&acc_empty[b], ((gi >> 1) & 1) ^ 1, GWB_ERR_TIMEOUT_MMA));
+               (h > 0 || mbar_wait(&acc_empty[b], ((gi / NBUF) & 1) ^ 1, GWB_ERR_TIMEOUT_MMA));
           if (!ok) break;
           tc_fence_after();
           const uint32_t a_base = smem_u32(ustage + u * USTAGE_BYTES), b_base = a_base + UA_BYTES;
@@ -477,8 +511,8 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         const uint32_t b_base = a_base + UA_BYTES;
         const uint32_t s_base = b_base + UB_BYTES;
         for (int gs = 0; gs < 2 && ok; ++gs, ++gi) {
-          const int b = gi & 1;
-          if (!mbar_wait(&acc_empty[b], ((gi >> 1) & 1) ^ 1, GWB_ERR_TIMEOUT_MMA)) {
+          const int b = gi % NBUF;
+          if (!mbar_wait(&acc_empty[b], ((gi / NBUF) & 1) ^ 1, GWB_ERR_TIMEOUT_MMA)) {
             ok = false;
             break;
           }
@@ -490,8 +524,9 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                  1u);
           if (!dump) {
             // S_b = a_scale[:, g] ⊗ w_scale[:, g], exact in f32 (11-bit x 11-bit)
-            const uint32_t sa = s_base + 2 * gs * SOP_DATA, sb = sa + SOP_DATA;
-            mma_f16(tmem + 2 * BN + b * BN, sdesc_scale(sa, zero_addr - sa),
+            const uint32_t sa = s_base + gs * SOPA;
+            const uint32_t sb = s_base + 2 * SOPA + (B_PACKED ? 0 : gs * SOPB);
+            mma_f16(tmem + NBUF * BN + b * BN, sdesc_scale(sa, zero_addr - sa),
                     sdesc_scale(sb, zero_addr - sb), idesc_s, 0u);
           }
           mma_commit(&acc_full[b]);
@@ -499,7 +534,7 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         mma_commit(&u_empty[u]);
       }
       }
-    } else if (A_PACKED && warp >= 2) {
+    } else if (UNPACK && warp >= 2) {
       // -------------------------------------------------------------- unpack
       const int tid = threadIdx.x - 64;
       int ui = 0, pk = 0;
@@ -519,9 +554,10 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         asm volatile("bar.sync 1, %0;" ::"n"(UNPACK_THREADS) : "memory");
         if (*reinterpret_cast<volatile uint32_t*>(unpack_flag) == 0u) { live = false; break; }
         if (tid == 0) GWB_TRACE_AT(3, ui);
-        const uint8_t* ps = pstage + s * PSTAGE_BYTES;
+        const uint8_t* ps = pstage + s * (PA + PB);
         uint8_t* us = ustage + u * USTAGE_BYTES;
-        unpack_tile<kBM>(ps, us, tid);
+        if (A_PACKED) unpack_tile<kBM>(ps, us, tid);
+        if (B_PACKED) unpack_tile<BN>(ps + PA, us + UA_BYTES, tid);
         fence_proxy_async_smem();
         asm volatile("bar.sync 1, %0;" ::"n"(UNPACK_THREADS) : "memory");
         if (tid == 0) {
@@ -533,7 +569,7 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       }
     }
   } else {
-    if constexpr (A_PACKED) regs_inc<200>();
+    if constexpr (UNPACK) regs_inc<200>();
     else regs_inc<224>();
     // ---------------------------------------------------------------- epilogue
     // Per group: load the f32 group sum V (= 2^-18 * v, exact) of this warp's
@@ -557,8 +593,8 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
     for (int j = 0; j < EC / 2; ++j) acc[j] = make_float2(0.f, 0.f);
     for (int gt = 0; gt < total; ++gt, ++gi) {
-      const int b = gi & 1;
-      if (!mbar_wait(&acc_full[b], (gi >> 1) & 1, GWB_ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      const int b = gi % NBUF;
+      if (!mbar_wait(&acc_full[b], (gi / NBUF) & 1, GWB_ERR_TIMEOUT_EPILOGUE)) { ok = false; break; }
       if (warp == EPI0 && lane == 0) GWB_TRACE_AT(5, gi);
       tc_fence_after();
       const uint32_t col0 = lane_base + b * BN + cb;
@@ -568,7 +604,7 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       for (int c = 0; c < EC; c += 32) tmem_ld32(col0 + c, v + c);
       if (!lr && !dump) {
 #pragma unroll
-        for (int c = 0; c < EC; c += 32) tmem_ld32(col0 + 2 * BN + c, sc + c);
+        for (int c = 0; c < EC; c += 32) tmem_ld32(col0 + NBUF * BN + c, sc + c);
       }
       tmem_wait_ld();
       tc_fence_before();
@@ -1001,28 +1037,20 @@ int launch_gemm_w8a8(const W8A8Args& a, bool fp8, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }
 
-int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, cudaStream_t st) {
-  if (a.M <= 0 || a.K <= 0 || a.K % kBK || a.N % w4::BN) return GWB_E_SHAPE;
-  if (a.rank_pad < 0 || a.rank_pad > 128 || a.rank_pad % 16) return GWB_E_SHAPE;
-  if (a.rank_pad > 0 && !a.partials && (!a.la || !a.up)) return GWB_E_SHAPE;
-  if (!a.partials && !a.out) return GWB_E_SHAPE;
-  if (!a.a_codes || !a.w_q8) return GWB_E_SHAPE;
-  if (!a.partials && (!a.a_scale_k8 || !a.w_scale_k8)) return GWB_E_SHAPE;
+template <bool A_PACKED, bool B_PACKED, int BN>
+static int launch_gemm_w4a4_cfg(const W4A4Args& a, cudaStream_t st) {
+  using C = w4::Cfg<A_PACKED, B_PACKED, BN>;
   const int G = a.K / 64;
-  if ((int64_t)G * a.M > 0x7fffffff || (int64_t)G * a.N > 0x7fffffff) return GWB_E_SHAPE;
-  if (!al16(a.a_codes) || !al16(a.w_q8) || (a.out && !al16(a.out)) ||
-      (a.bias && !al16(a.bias)) ||
-      (a.la && !al16(a.la)) || (a.up && !al16(a.up)) || (a.partials && !al16(a.partials)) ||
-      (!a.partials && (!al16(a.a_scale_k8) || !al16(a.w_scale_k8))))
-    return GWB_E_ALIGN;
   CUtensorMap tA, tB, tAS, tBS, tLA, tUP;
-  int rc = a_packed ? make_tmap(&tA, a.a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K / 2, a.M,
+  int rc = A_PACKED ? make_tmap(&tA, a.a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K / 2, a.M,
                                kBK / 2, kBM, CU_TENSOR_MAP_SWIZZLE_NONE)
                      : make_tmap(&tA, a.a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.M, kBK,
                                  kBM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = make_tmap(&tB, a.w_q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.N, kBK, w4::BN,
-                 CU_TENSOR_MAP_SWIZZLE_128B);
+  rc = B_PACKED ? make_tmap(&tB, a.w_q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K / 2, a.N, kBK / 2,
+                            BN, CU_TENSOR_MAP_SWIZZLE_NONE)
+                : make_tmap(&tB, a.w_q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K, a.N, kBK, BN,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   tAS = tA;
   tBS = tB;
@@ -1032,35 +1060,73 @@ int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, cudaStream_t st) {
     rc = make_tmap(&tAS, a.a_scale_k8, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 8, (uint64_t)G * a.M,
                    8, kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    rc = make_tmap(&tBS, a.w_scale_k8, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 8, (uint64_t)G * a.N,
-                   8, w4::BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+    // stored weight scales f16 [N, G] (8 groups per box row), or the
+    // one-hot rows f16 [G, N, 8]
+    rc = B_PACKED ? make_tmap(&tBS, a.w_scale_k8, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, G, a.N, 8,
+                              BN, CU_TENSOR_MAP_SWIZZLE_NONE)
+                  : make_tmap(&tBS, a.w_scale_k8, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 8,
+                              (uint64_t)G * a.N, 8, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   }
   if (a.rank_pad > 0 && !a.partials) {
     rc = make_tmap(&tLA, a.la, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.rank_pad, a.M, 64, kBM,
                    CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    rc = make_tmap(&tUP, a.up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.rank_pad, a.N, 64, w4::BN,
+    rc = make_tmap(&tUP, a.up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.rank_pad, a.N, 64, BN,
                    CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
+  auto kern = gemm_w4a4_kernel<A_PACKED, B_PACKED, BN>;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(gemm_w4a4_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         w4::SMEM_BYTES);
-    cudaFuncSetAttribute(gemm_w4a4_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         w4::SMEM_BYTES);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     attr = true;
   }
-  const int ntiles = ((a.M + kBM - 1) / kBM) * (a.N / w4::BN);
+  const int ntiles = ((a.M + kBM - 1) / kBM) * (a.N / BN);
   const int n_sm = sm_count();
   const int grid = ntiles < n_sm ? ntiles : n_sm;
-  auto kern = a_packed ? gemm_w4a4_kernel<true> : gemm_w4a4_kernel<false>;
-  kern<<<grid, a_packed ? w4::threads<true>() : w4::threads<false>(), w4::SMEM_BYTES, st>>>(
+  kern<<<grid, w4::threads<A_PACKED || B_PACKED>(), C::SMEM_BYTES, st>>>(
       tA, tB, tAS, tBS, tLA, tUP, static_cast<const __nv_bfloat16*>(a.bias),
       static_cast<__nv_bfloat16*>(a.out), a.partials, a.M, a.N, a.K,
       a.partials ? 0 : a.rank_pad, a.gelu);
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
+}
+
+// Tile width of the W4A4 GEMM (128 or 64; GWB_W4A4_BN overrides, for measurement).
+static int w4a4_tile_n() {
+  static int bn = 0;
+  if (bn == 0) {
+    const char* e = getenv("GWB_W4A4_BN");
+    bn = (e && atoi(e) == 64) ? 64 : 128;
+  }
+  return bn;
+}
+
+int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, bool b_packed, cudaStream_t st) {
+  if (a.M <= 0 || a.K <= 0 || a.K % kBK || a.N % 128) return GWB_E_SHAPE;
+  if (a.rank_pad < 0 || a.rank_pad > 128 || a.rank_pad % 16) return GWB_E_SHAPE;
+  if (a.rank_pad > 0 && !a.partials && (!a.la || !a.up)) return GWB_E_SHAPE;
+  if (!a.partials && !a.out) return GWB_E_SHAPE;
+  if (!a.a_codes || !a.w_q8) return GWB_E_SHAPE;
+  if (!a.partials && (!a.a_scale_k8 || !a.w_scale_k8)) return GWB_E_SHAPE;
+  if (b_packed && a.partials) return GWB_E_SHAPE;
+  const int G = a.K / 64;
+  if ((int64_t)G * a.M > 0x7fffffff || (int64_t)G * a.N > 0x7fffffff) return GWB_E_SHAPE;
+  if (!al16(a.a_codes) || !al16(a.w_q8) || (a.out && !al16(a.out)) ||
+      (a.bias && !al16(a.bias)) ||
+      (a.la && !al16(a.la)) || (a.up && !al16(a.up)) || (a.partials && !al16(a.partials)) ||
+      (!a.partials && (!al16(a.a_scale_k8) || !al16(a.w_scale_k8))))
+    return GWB_E_ALIGN;
+  // stored weight scales [N, G]: each row must start on a 16-byte boundary
+  if (b_packed && (G % 8)) return GWB_E_SHAPE;
+  const bool bn64 = w4a4_tile_n() == 64;
+  if (a_packed && b_packed)
+    return bn64 ? launch_gemm_w4a4_cfg<true, true, 64>(a, st) : launch_gemm_w4a4_cfg<true, true, 128>(a, st);
+  if (a_packed)
+    return bn64 ? launch_gemm_w4a4_cfg<true, false, 64>(a, st) : launch_gemm_w4a4_cfg<true, false, 128>(a, st);
+  if (b_packed)
+    return bn64 ? launch_gemm_w4a4_cfg<false, true, 64>(a, st) : launch_gemm_w4a4_cfg<false, true, 128>(a, st);
+  return bn64 ? launch_gemm_w4a4_cfg<false, false, 64>(a, st) : launch_gemm_w4a4_cfg<false, false, 128>(a, st);
 }
 
 int launch_gemm_nvfp4(const NvFp4Args& a, cudaStream_t st) {

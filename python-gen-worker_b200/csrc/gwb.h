@@ -50,9 +50,10 @@ int launch_gemm_nvfp4(const NvFp4Args& a, cudaStream_t st);
 
 struct W4A4Args {
   const void* a_codes;     // u8 [M, K/2] packed INT4 (a_packed) or u8 [M, K] operand form
-  const void* a_scale_k8;  // f16 [K/64, M, 8] (scale at k = 0)
-  const void* w_q8;        // u8 [N, K] expanded weight (launch_w4a4_weight_expand)
-  const void* w_scale_k8;  // f16 [K/64, N, 8]
+  const void* a_scale_k8;  // f16 [K/64, M, 8] (group g's scale at k = g mod 8)
+  const void* w_q8;        // u8 [N, K] expanded weight (launch_w4a4_weight_expand), or
+                           // the stored packed weight u8 [N, K/2] (b_packed)
+  const void* w_scale_k8;  // f16 [K/64, N, 8] one-hot rows, or the stored f16 [N, K/64] (b_packed)
   const void* la;          // bf16 [M, rank_pad] or null
   const void* up;          // bf16 [N, rank_pad] or null
   const void* bias;        // bf16 [N] or null
@@ -60,7 +61,7 @@ struct W4A4Args {
   int32_t* partials;       // optional debug: s32 [K/64, M, N]; disables the epilogue
   int M, N, K, rank_pad, gelu;
 };
-int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, cudaStream_t st);
+int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, bool b_packed, cudaStream_t st);
 int launch_w4a4_weight_expand(const void* w_codes, void* w_q8, int64_t N, int64_t K,
                               cudaStream_t st);
 

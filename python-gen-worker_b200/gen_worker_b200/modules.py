@@ -105,16 +105,43 @@ class SvdqInt4Linear(nn.Module):
             self.bias = None
         self._packed: Optional[Dict[str, Any]] = None
 
+    @property
+    def stored(self) -> bool:
+        """True when the GEMM reads ``weight`` / ``weight_scale`` as stored
+        (in_features % 512 == 0); otherwise the weight is expanded once into
+        the e4m3 operand form at load time."""
+        return ops.stored_weights_supported(self.in_features)
+
     def prepare(self) -> Dict[str, Any]:
-        """Kernel-layout copies of the scale and low-rank buffers (built once,
-        on the buffers' device)."""
+        """Kernel-layout copies of the low-rank buffers (and, when the stored
+        weights cannot be read directly, of the weight and its scales), built
+        once on the buffers' device."""
         dev = self.weight.device
         if self._packed is None or self._packed["device"] != dev:
             p = ops.prepare_w4a4_weights(self.weight_scale, self.proj_down, self.proj_up,
-                                         weight=self.weight)
+                                         weight=self.weight, operand_form=not self.stored)
             p["device"] = dev
             self._packed = p
         return self._packed
+
+    def quantize(self, x2: torch.Tensor) -> tuple:
+        """First launch of the forward: smoothing, INT4 codes and scales in
+        operand form, and la = x2 · proj_down on raw x."""
+        p = self.prepare()
+        codes, a_sk8, la = ops.svdq_w4a4_quant_mma(x2, self.smooth_factor, p["proj_down_t"])
+        return codes, a_sk8, (la if p["proj_down_t"] is not None else None)
+
+    def gemm(self, a_q8: torch.Tensor, a_scale_k8: torch.Tensor,
+             la: Optional[torch.Tensor]) -> torch.Tensor:
+        """Second launch of the forward: the GEMM with the fused promotion,
+        low-rank, bias and GELU epilogue."""
+        p = self.prepare()
+        bias = self.bias.detach() if self.bias is not None else None
+        if self.stored:
+            return ops.svdq_w4a4_gemm_stored(a_q8, a_scale_k8, self.weight, self.weight_scale, la,
+                                             p["proj_up_pad"], bias, self.gelu)
+        return ops.svdq_w4a4_gemm(a_q8, a_scale_k8, p["w_q8"], p["w_scale_k8"], la,
+                                  p["proj_up_pad"], bias, self.gelu)
 
     def _apply(self, fn, recurse=True):  # noqa: ANN001 — drop stale repacks on .to()
         self._packed = None
@@ -125,13 +152,7 @@ class SvdqInt4Linear(nn.Module):
         x2 = x.reshape(-1, self.in_features)
         if not x2.is_contiguous():
             x2 = x2.contiguous()
-        p = self.prepare()
-        codes, a_sk8, la = ops.svdq_w4a4_quant_mma(x2, self.smooth_factor, p["proj_down_t"])
-        y = ops.svdq_w4a4_gemm(codes, a_sk8, p["w_q8"], p["w_scale_k8"],
-                               la if p["proj_down_t"] is not None else None,
-                               p["proj_up_pad"],
-                               self.bias.detach() if self.bias is not None else None,
-                               self.gelu)
+        y = self.gemm(*self.quantize(x2))
         return y.reshape(*shape[:-1], self.out_features)
 
     def extra_repr(self) -> str:

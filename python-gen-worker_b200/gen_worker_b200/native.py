@@ -39,6 +39,15 @@ _SIGNATURES = {
     "gwb_svdq_w4a4_gemm_packed": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_void_p, c_i64, c_i64, c_i64, c_int, c_int, c_void_p,
                                   c_void_p],
+    "gwb_svdq_w4a4_gemm_stored": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                  c_void_p, c_i64, c_i64, c_i64, c_int, c_int, c_void_p,
+                                  c_void_p],
+    "gwb_svdq_w4a4_gemm_packed_stored": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_i64, c_i64, c_i64, c_int, c_int,
+                                         c_void_p, c_void_p],
+    "gwb_svdq_w4a4_linear_stored": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                    c_void_p, c_i64, c_i64, c_i64, c_int, c_int, c_void_p,
+                                    c_void_p, c_void_p, c_void_p, c_void_p],
     "gwb_svdq_w4a4_group_partials": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_void_p,
                                      c_void_p],
     "gwb_svdq_w4a4_linear": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

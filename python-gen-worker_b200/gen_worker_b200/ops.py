@@ -204,6 +204,76 @@ def _(codes, a_scale_k8, w_q8, w_scale_k8, la, proj_up, bias, gelu):
     return codes.new_empty(codes.shape[0], w_q8.shape[0], dtype=torch.bfloat16)
 
 
+def _w4a4_gemm_stored(fn: str, a: torch.Tensor, k: int, a_scale_k8, weight, weight_scale, la,
+                      proj_up, bias, gelu) -> torch.Tensor:
+    _need(a_scale_k8, "a_scale_k8", torch.float16, 3)
+    _need(weight, "weight", torch.uint8, 2)
+    _need(weight_scale, "weight_scale", torch.float16, 2)
+    _need(bias, "bias", torch.bfloat16, 1)
+    m = a.shape[0]
+    n = weight.shape[0]
+    if int(weight.shape[1]) * 2 != k or tuple(weight_scale.shape) != (n, k // GROUP):
+        raise SvdqB200Error(f"stored weight {tuple(weight.shape)} / weight_scale "
+                            f"{tuple(weight_scale.shape)} do not match activation K {k}")
+    rp = 0
+    if la is not None and proj_up is not None and la.shape[1] > 0:
+        _need(la, "la", torch.bfloat16, 2)
+        _need(proj_up, "proj_up", torch.bfloat16, 2)
+        rp = int(la.shape[1])
+        if int(proj_up.shape[1]) != rp:
+            raise SvdqB200Error(f"la rank {rp} != proj_up rank {proj_up.shape[1]}")
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=a.device)
+    lib = native.require()
+    native.check(getattr(lib, fn)(a.data_ptr(), a_scale_k8.data_ptr(), weight.data_ptr(),
+                                  weight_scale.data_ptr(), _ptr(la) if rp else None,
+                                  _ptr(proj_up) if rp else None, _ptr(bias), m, n, k, rp,
+                                  int(bool(gelu)), out.data_ptr(), _stream()), fn)
+    return out
+
+
+def stored_weights_supported(in_features: int) -> bool:
+    """The stored-weight GEMM reads 8 groups of scales per 16-byte row:
+    in_features must be a multiple of 512."""
+    return in_features % (8 * GROUP) == 0
+
+
+@torch.library.custom_op("gwb200::svdq_w4a4_gemm_stored", mutates_args=())
+def svdq_w4a4_gemm_stored(a_q8: torch.Tensor, a_scale_k8: torch.Tensor, weight: torch.Tensor,
+                          weight_scale: torch.Tensor, la: Optional[torch.Tensor],
+                          proj_up: Optional[torch.Tensor], bias: Optional[torch.Tensor],
+                          gelu: bool) -> torch.Tensor:
+    """INT4 group-64 GEMM on the weight AS STORED (``weight`` u8 [N, K/2],
+    ``weight_scale`` f16 [N, K/64]; expanded in shared memory) and
+    operand-form activations (``svdq_w4a4_quant_mma``) + promotion +
+    low-rank up-projection + bias (+ GELU) -> bf16 [M, N]
+    (``svdq_gemm_w4a4_lora``, ``svdq_fused.py:379-383``)."""
+    _need(a_q8, "a_q8", torch.uint8, 2)
+    return _w4a4_gemm_stored("gwb_svdq_w4a4_gemm_stored", a_q8, int(a_q8.shape[1]), a_scale_k8,
+                             weight, weight_scale, la, proj_up, bias, gelu)
+
+
+@svdq_w4a4_gemm_stored.register_fake
+def _(a_q8, a_scale_k8, weight, weight_scale, la, proj_up, bias, gelu):
+    return a_q8.new_empty(a_q8.shape[0], weight.shape[0], dtype=torch.bfloat16)
+
+
+@torch.library.custom_op("gwb200::svdq_w4a4_gemm_packed_stored", mutates_args=())
+def svdq_w4a4_gemm_packed_stored(codes: torch.Tensor, a_scale_k8: torch.Tensor,
+                                 weight: torch.Tensor, weight_scale: torch.Tensor,
+                                 la: Optional[torch.Tensor], proj_up: Optional[torch.Tensor],
+                                 bias: Optional[torch.Tensor], gelu: bool) -> torch.Tensor:
+    """The stored-weight GEMM on packed activation codes u8 [M, K/2] (both
+    operands expanded in shared memory)."""
+    _need(codes, "codes", torch.uint8, 2)
+    return _w4a4_gemm_stored("gwb_svdq_w4a4_gemm_packed_stored", codes, int(codes.shape[1]) * 2,
+                             a_scale_k8, weight, weight_scale, la, proj_up, bias, gelu)
+
+
+@svdq_w4a4_gemm_packed_stored.register_fake
+def _(codes, a_scale_k8, weight, weight_scale, la, proj_up, bias, gelu):
+    return codes.new_empty(codes.shape[0], weight.shape[0], dtype=torch.bfloat16)
+
+
 @torch.library.custom_op("gwb200::svdq_w4a4_group_partials", mutates_args=())
 def svdq_w4a4_group_partials(codes: torch.Tensor, w_q8: torch.Tensor) -> torch.Tensor:
     """Debug: every 64-group integer partial sum of the tcgen05 GEMM,
@@ -452,7 +522,8 @@ def _(codes, sblk, work, w_codes, w_sblk, w_scale_2, la, proj_up, bias):
 # ---------------------------------------------------------------- load-time repacks
 def prepare_w4a4_weights(w_scale: Optional[torch.Tensor], proj_down: Optional[torch.Tensor],
                          proj_up: Optional[torch.Tensor],
-                         weight: Optional[torch.Tensor] = None) -> dict:
+                         weight: Optional[torch.Tensor] = None,
+                         operand_form: bool = True) -> dict:
     """Load-time repack of the module buffers into the kernel operand layouts
     (the reference repacks at load too: ``to_buffers``,
     ``svdq_layout.py:473-483``):
@@ -460,11 +531,14 @@ def prepare_w4a4_weights(w_scale: Optional[torch.Tensor], proj_down: Optional[to
       weight_scale f16 [N, K/64] -> w_scale_k8 f16 [K/64, N, 8] (CUDA only;
                                     None when w_scale is None or on the CPU)
       proj_down bf16 [K, r]      -> proj_down_t bf16 [rank_pad, K] (zero rows)
-      proj_up bf16 [N, r]        -> proj_up_pad bf16 [N, rank_pad] (zero cols)"""
+      proj_up bf16 [N, r]        -> proj_up_pad bf16 [N, rank_pad] (zero cols)
+    With ``operand_form=False`` the weight and its scales stay as stored
+    (the stored-weight GEMM reads them directly) and only the low-rank
+    factors are repacked."""
     out: dict = {"w_scale_k8": None, "w_q8": None}
-    if weight is not None and weight.is_cuda:
+    if operand_form and weight is not None and weight.is_cuda:
         out["w_q8"] = expand_w4a4_weight(weight.contiguous())
-    if w_scale is not None and w_scale.is_cuda:
+    if operand_form and w_scale is not None and w_scale.is_cuda:
         out["w_scale_k8"] = svdq_w4a4_scale_k8(w_scale.to(torch.float16).contiguous())
     if proj_down is not None and proj_up is not None and proj_down.shape[1] > 0:
         k, r = proj_down.shape

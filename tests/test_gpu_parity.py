@@ -62,8 +62,11 @@ def test_int4_activation_codes_and_scales_bit_exact(cuda_ready, m, k):
     want_k8 = ops.svdq_w4a4_scale_k8(ascale)
     assert torch.equal(c2, ops.expand_w4a4_weight(codes))
     assert torch.equal(sk8.view(torch.int16), want_k8.view(torch.int16))
-    assert torch.all(sk8[:, :, 1:] == 0)
-    assert torch.equal(sk8[:, :, 0].t().contiguous().view(torch.int16),
+    # one-hot rows: group g's scale at k = g mod 8, zeros elsewhere
+    g = torch.arange(k // 64, device=sk8.device)
+    onehot = torch.nn.functional.one_hot(g % 8, 8).bool()[:, None, :]
+    assert torch.all(sk8.masked_fill(onehot, 0) == 0)
+    assert torch.equal(sk8[g, :, g % 8].t().contiguous().view(torch.int16),
                        ascale.view(torch.int16))
     assert torch.equal(la2, la)
 
@@ -369,3 +372,29 @@ def test_w4a4_full_size_rows_match_oracle(cuda_ready, k, n):
     assert O.max_abs_beyond_bf16(y, want["y64"]) <= ABS_TOL
     assert native.device_error() == 0
 
+
+
+@pytest.mark.parametrize("m,k,n,rank,gelu", [(300, 512, 256, 32, False), (128, 3072, 384, 0, True),
+                                             (77, 1024, 128, 128, False),
+                                             (1000, 3072, 1024, 48, False)])
+def test_stored_weight_gemm_matches_operand_form(cuda_ready, m, k, n, rank, gelu):
+    """gwb_svdq_w4a4_gemm_stored (weight and scales as stored, expanded in
+    shared memory) and gwb_svdq_w4a4_gemm_packed_stored (activations packed
+    too) give bit-identical outputs to the operand-form GEMM: the stored
+    8-group scale rows against the one-hot activation rows form the same
+    exact scale products."""
+    x, L = _layer_case(m, k, n, rank, seed=13 * m + k)
+    p, codes, ascale, la = _quant_gpu(x, L)
+    w = L["w_packed"].cuda()
+    ws = L["w_scale"].cuda()
+    a_q8, a_sk8, la2 = ops.svdq_w4a4_quant_mma(x.cuda(), L["smooth"].cuda(), p["proj_down_t"])
+    lr = la2 if rank else None
+    bias = L["bias"].cuda()
+    ref = ops.svdq_w4a4_gemm(a_q8, a_sk8, ops.expand_w4a4_weight(w), p["w_scale_k8"], lr,
+                             p["proj_up_pad"], bias, gelu)
+    got = ops.svdq_w4a4_gemm_stored(a_q8, a_sk8, w, ws, lr, p["proj_up_pad"], bias, gelu)
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+    got2 = ops.svdq_w4a4_gemm_packed_stored(codes, ops.svdq_w4a4_scale_k8(ascale), w, ws, lr,
+                                            p["proj_up_pad"], bias, gelu)
+    assert torch.equal(got2.view(torch.int16), ref.view(torch.int16))
+    assert native.device_error() == 0
