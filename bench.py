@@ -300,6 +300,34 @@ def cpu_reference(steps: int, warmup: int, sample_tokens: int = 64) -> dict:
             "ms_per_stack_sample": per_stack * 1e3}
 
 
+def cpu_reference_cfg0(reps: int = 20) -> dict:
+    """BASELINE config 0 on the host cores, the CPU config SURVEY mandates:
+    one svdq linear (M 256, K = N = 3072, rank 32, smoothing, bias) folded to
+    one dense bf16 ``nn.Linear`` (``fold_to_dense``, reference
+    svdq_native.py:200-221); median of ``reps`` calls after warm-up,
+    reported as effective TOP/s (2·M·N·K per call) and ms per call."""
+    from oracle import svdq_oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    m, k, n = 256, 3072, 3072
+    x = O.synth_activation(m, k, seed=0)
+    L = O.synth_svdq_layer(k, n, 32, seed=1, x_calib=x)
+    lin = O.FoldedLinear(L["w_packed"], L["w_scale"], L["smooth"], L["proj_down"],
+                         L["proj_up"], L["bias"])
+    for _ in range(3):
+        lin(x)
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        lin(x)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"config": "cfg0: 256x3072 -> 3072, rank 32, folded bf16 nn.Linear",
+            "ms_per_call": t * 1e3, "tops": 2.0 * m * n * k / t / 1e12, "cores": threads,
+            "kind": "port", "sample": f"median of {reps} calls"}
+
+
 # --------------------------------------------------------------------------- per-config cases
 CASES = {
     # name: list of (kind, M, K, N, rank, gelu)
@@ -900,6 +928,7 @@ def main() -> int:
         if not args.no_cpu_baseline:
             r = cpu_reference(steps=3, warmup=1)
             line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            line["cpu_baseline_cfg0"] = cpu_reference_cfg0()
         print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()

@@ -162,6 +162,20 @@ int gwb_svdq_w4a4_linear_noalloc(const void* x, const void* smooth, const void* 
                                  const void* proj_up, const void* bias, int64_t M, int64_t N,
                                  int64_t K, int rank_pad, int gelu, void* out, void* stream);
 
+/* Failure handling (counterpart of the reference's collective timeout and
+ * stall detection, src/gen_worker/parallel/group.py:26, :265-285). Every
+ * pipeline wait in the kernels is bounded: after `cycles` SM clock cycles it
+ * records a GWB_ERR_TIMEOUT_* code (read with gwb_device_error), every role
+ * unwinds, TMEM is freed and the kernel returns. cycles <= 0 restores the
+ * default (4e9, ~2 s). */
+int gwb_set_wait_limit(long long cycles);
+
+/* Test entry (no reference counterpart): a kernel whose wait can never
+ * complete (an mbarrier nothing arrives on, while it holds TMEM), so that
+ * a test can make the bounded wait run out and check the recorded `code`
+ * and that the next launch works. */
+int gwb_test_stalled_wait(int code, void* stream);
+
 /* Replaces the W8A8 activation quantiser `_quant_src` rowwise branch
  * (reference src/gen_worker/models/w8a8.py:261-273): per-token symmetric
  * INT8, q s8 [M, K], scale f32 [M]. */

@@ -26,6 +26,32 @@ __global__ void probe_add_one_kernel(const float* __restrict__ x, float* __restr
 
 inline cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
 
+// A wait that can never complete, run with the kernels' own bounded wait:
+// every warp waits on an mbarrier nothing arrives on while the CTA holds
+// TMEM, exactly as a GEMM role waits on its pipeline. Each wait gives up
+// after gwb_wait_limit cycles and records `code` in gwb_dev_error; the CTA
+// then meets at a barrier and frees its TMEM, so the context stays usable.
+__global__ void stalled_wait_kernel(int code) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t slot;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    gwb::mbar_init(&bar, 1);
+    gwb::fence_barrier_init();
+  }
+  if (warp == 0) {
+    gwb::tmem_alloc(&slot, 32);
+    gwb::tmem_relinquish();
+  }
+  gwb::tc_fence_before();
+  __syncthreads();
+  gwb::tc_fence_after();
+  if (lane == 0) (void)gwb::mbar_wait(&bar, 0, code);
+  gwb::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) gwb::tmem_dealloc(slot, 32);
+}
+
 inline bool fits_int(int64_t v) { return v >= 0 && v <= 0x7fffffff; }
 
 inline int check_w4a4_shape(int64_t M, int64_t N, int64_t K, int rank_pad) {
@@ -359,6 +385,18 @@ int gwb_awq_w4a16_mm(const void* x, const void* weight, const void* wscales, con
       static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), (int)M, (int)N,
       (int)K, S(stream));
   return e == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
+}
+
+int gwb_set_wait_limit(long long cycles) {
+  const long long v = cycles > 0 ? cycles : (long long)GWB_WAIT_LIMIT_CYCLES;
+  return cudaMemcpyToSymbol(gwb_wait_limit, &v, sizeof(v)) == cudaSuccess ? GWB_SUCCESS
+                                                                          : GWB_E_LAUNCH;
+}
+
+int gwb_test_stalled_wait(int code, void* stream) {
+  if (code <= 0) return GWB_E_SHAPE;
+  stalled_wait_kernel<<<2, 128, 0, S(stream)>>>(code);
+  return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }
 
 int gwb_device_check(void) {

@@ -22,6 +22,9 @@ enum GwbDevError : int {
 
 // Device-side error flag (the library is built as one translation unit).
 __device__ int gwb_dev_error = 0;
+// Cycles a bounded wait spins before it gives up (runtime-settable through
+// gwb_set_wait_limit; the default is GWB_WAIT_LIMIT_CYCLES).
+__device__ long long gwb_wait_limit = GWB_WAIT_LIMIT_CYCLES;
 
 namespace gwb {
 
@@ -76,11 +79,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int err) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
+  const long long limit = *((volatile long long*)&gwb_wait_limit);
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 15u) == 0u) {
       if (error_seen()) return false;
-      if (clock64() - start > GWB_WAIT_LIMIT_CYCLES) break;
+      if (clock64() - start > limit) break;
     }
   }
   set_error(err);

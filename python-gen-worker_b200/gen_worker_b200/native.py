@@ -81,6 +81,8 @@ _SIGNATURES = {
     "gwb_w8a8_linear": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_int,
                         c_void_p, c_void_p, c_void_p, c_void_p],
     "gwb_device_error": [ctypes.POINTER(c_int)],
+    "gwb_set_wait_limit": [ctypes.c_longlong],
+    "gwb_test_stalled_wait": [c_int, c_void_p],
     "gwb_device_check": [],
     "gwb_status_string": [c_int],
 }
@@ -114,6 +116,24 @@ def lib() -> ctypes.CDLL:
         fn.argtypes = argtypes
         fn.restype = ctypes.c_char_p if name == "gwb_status_string" else c_int
     return handle
+
+
+TORCH_LIB = _DEFAULT.parent / "libgwb200_torch.so"
+
+
+@functools.lru_cache(maxsize=1)
+def torch_ops():
+    """Load the TORCH_LIBRARY(cozy_kernels) extension (``libgwb200_torch.so``,
+    beside the C-ABI library; the file the reference's loader takes from
+    ``GEN_WORKER_NATIVE_KERNELS_LIB``) and return ``torch.ops.cozy_kernels``."""
+    import torch
+
+    if not TORCH_LIB.exists():
+        raise NativeKernelError(f"torch extension {TORCH_LIB} does not exist; build it with "
+                                f"`python python-gen-worker_b200/csrc/build.py`")
+    lib()   # the C-ABI library it links against, from the same folder
+    torch.ops.load_library(str(TORCH_LIB))
+    return torch.ops.cozy_kernels
 
 
 def status_string(code: int) -> str:
