@@ -16,7 +16,6 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
-#include <cstdlib>
 #include "gwb.h"
 #include "ptx.cuh"
 
@@ -236,8 +235,12 @@ constexpr int UA_BYTES = kBM * kBK;        // 16 KB e4m3 A (unpacked here)
 constexpr int SOPA = kBM * 16;             // 2 KB (A side, 128 rows)
 constexpr int ZERO_BYTES = SOPA;
 constexpr int TMEM_COLS = 512;
-constexpr int UNPACK_WARPS = 6;            // warps 2-7 (packed activations only)
-constexpr int UNPACK_THREADS = 32 * UNPACK_WARPS;
+// unpack warps from warp 2 on: six (warps 2-7) when the activations arrive
+// packed, else two (warps 2-3, the warpgroup's otherwise idle pair) for a
+// packed weight alone
+template <bool A_PACKED> __host__ __device__ constexpr int unpack_threads() {
+  return A_PACKED ? 192 : 64;
+}
 constexpr int EPI_WARPS = 8;               // the last two warpgroups
 // Tile N width BN: 128 (two TMEM group buffers of V | S) or 64 (four).
 // TMEM: [0, NBUF*BN) f32 group sums V_b, [NBUF*BN, 512) f32 scale products S_b.
@@ -261,7 +264,7 @@ template <bool A_PACKED, bool B_PACKED, int BN> struct Cfg {
   static_assert(SMEM_BYTES <= 232448, "W4A4 shared memory exceeds 227 KB");
 };
 // packed activations: 16 warps (producer, MMA, 6 unpack, 8 epilogue);
-// operand-form activations: 12 warps (producer, MMA, 2 idle, 8 epilogue)
+// operand-form activations: 12 warps (producer, MMA, 2 unpack or idle, 8 epilogue)
 template <bool A_PACKED> __host__ __device__ constexpr int threads() { return A_PACKED ? 512 : 384; }
 template <bool A_PACKED> __host__ __device__ constexpr int epi_warp0() { return A_PACKED ? 8 : 4; }
 // Both operands hold q * 2^-9 (e4m3 subnormals), so a group sum is
@@ -274,21 +277,26 @@ constexpr float kRescale = 1.0f / 262144.0f;
 
 // Unpack `chunks` 16-byte packed chunks (rows of 64 packed bytes, row-major,
 // no swizzle) into rows of 128 e4m3 bytes in the SWIZZLE_128B K-major layout.
-template <int kRows>
+template <int kRows, int kThreads>
 __device__ __forceinline__ void unpack_tile(const uint8_t* __restrict__ src, uint8_t* dst,
                                             int tid) {
   constexpr int kChunks = kRows * 4;
-  constexpr int kPer = (kChunks + w4::UNPACK_THREADS - 1) / w4::UNPACK_THREADS;
-  uint4 p[kPer];
+  constexpr int kPer = (kChunks + kThreads - 1) / kThreads;
+  constexpr int kBatch = kPer < 4 ? kPer : 4;   // loads in flight per thread
 #pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int i = tid + j * w4::UNPACK_THREADS;
-    if (i < kChunks) p[j] = *reinterpret_cast<const uint4*>(src + (i >> 2) * 64 + (i & 3) * 16);
+  for (int j0 = 0; j0 < kPer; j0 += kBatch) {
+  uint4 p[kBatch];
+#pragma unroll
+  for (int jj = 0; jj < kBatch; ++jj) {
+    const int i = tid + (j0 + jj) * kThreads;
+    if (j0 + jj < kPer && i < kChunks)
+      p[jj] = *reinterpret_cast<const uint4*>(src + (i >> 2) * 64 + (i & 3) * 16);
   }
 #pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int i = tid + j * w4::UNPACK_THREADS;
-    if (i < kChunks) {
+  for (int jj = 0; jj < kBatch; ++jj) {
+    const int j = jj;
+    const int i = tid + (j0 + jj) * kThreads;
+    if (j0 + jj < kPer && i < kChunks) {
       const int r = i >> 2, cj = i & 3;
       uint4 o0, o1;
       unpack8_e4m3(p[j].x, o0.x, o0.y);
@@ -299,6 +307,7 @@ __device__ __forceinline__ void unpack_tile(const uint8_t* __restrict__ src, uin
       *reinterpret_cast<uint4*>(dst + swz128(r, cj * 32 + 16)) = o1;
     }
   }
+}
 }
 
 // Load-time weight expansion: packed sign-magnitude nibbles u8 [N, K/2] ->
@@ -338,7 +347,7 @@ __device__ __forceinline__ uint64_t sdesc_scale(uint32_t saddr, uint32_t lbo) {
 // by the quantiser) selects the group. Otherwise the weight is the load-time
 // operand form (w_q8 u8 [N, K], w_scale_k8 one-hot rows).
 template <bool A_PACKED, bool B_PACKED, int BN>
-__global__ void __launch_bounds__(w4::threads<A_PACKED || B_PACKED>(), 1)
+__global__ void __launch_bounds__(w4::threads<A_PACKED>(), 1)
 gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmAS, const __grid_constant__ CUtensorMap tmBS,
                  const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmUP,
@@ -351,8 +360,9 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   constexpr int UB_BYTES = C::UB_BYTES, SOPB = C::SOPB, SCALE_BYTES = C::SCALE_BYTES;
   constexpr int PA = C::PA_STAGE, PB = C::PB_STAGE;
   constexpr int EC = C::EC;
-  constexpr int THREADS = threads<UNPACK>();
-  constexpr int EPI0 = epi_warp0<UNPACK>();
+  constexpr int THREADS = threads<A_PACKED>();
+  constexpr int EPI0 = epi_warp0<A_PACKED>();
+  constexpr int UNPACK_THREADS = unpack_threads<A_PACKED>();
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment by offsetting the __shared__ array itself, so the
   // compiler keeps emitting shared-space (not generic) loads and stores
@@ -406,13 +416,13 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) GWB_TRACE_AT(7, 0);
 
-  // register hand-off. With unpack warps the launch gives 512 x 128 = 65536
-  // registers; warpgroups 0-1 (producer, MMA, unpack) drop to 56 (14336) and
-  // the two epilogue warpgroups rise to 200 (51200). Operand form only: 384 x
-  // 168 = 64512; warpgroup 0 drops to 48 (6144), the epilogue rises to 224 (57344).
+  // register hand-off. Packed activations: the launch gives 512 x 128 =
+  // 65536 registers; warpgroups 0-1 (producer, MMA, unpack) drop to 56 (14336)
+  // and the two epilogue warpgroups rise to 200 (51200). Otherwise 384 x 168 =
+  // 64512; warpgroup 0 (producer, MMA, two unpack warps or idle) drops to 56
+  // (7168) and the epilogue rises to 224 (57344).
   if (warp < EPI0) {
-    if constexpr (UNPACK) regs_dec<56>();
-    else regs_dec<48>();
+    regs_dec<56>();
     if (warp == 0 && lane == 0) {
       // -------------------------------------------------------------- TMA
       int ui = 0, pk = 0;   // operand-ring and packed-ring slots used so far
@@ -556,8 +566,8 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         if (tid == 0) GWB_TRACE_AT(3, ui);
         const uint8_t* ps = pstage + s * (PA + PB);
         uint8_t* us = ustage + u * USTAGE_BYTES;
-        if (A_PACKED) unpack_tile<kBM>(ps, us, tid);
-        if (B_PACKED) unpack_tile<BN>(ps + PA, us + UA_BYTES, tid);
+        if (A_PACKED) unpack_tile<kBM, UNPACK_THREADS>(ps, us, tid);
+        if (B_PACKED) unpack_tile<BN, UNPACK_THREADS>(ps + PA, us + UA_BYTES, tid);
         fence_proxy_async_smem();
         asm volatile("bar.sync 1, %0;" ::"n"(UNPACK_THREADS) : "memory");
         if (tid == 0) {
@@ -569,7 +579,7 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       }
     }
   } else {
-    if constexpr (UNPACK) regs_inc<200>();
+    if constexpr (A_PACKED) regs_inc<200>();
     else regs_inc<224>();
     // ---------------------------------------------------------------- epilogue
     // Per group: load the f32 group sum V (= 2^-18 * v, exact) of this warp's
@@ -1085,21 +1095,11 @@ static int launch_gemm_w4a4_cfg(const W4A4Args& a, cudaStream_t st) {
   const int ntiles = ((a.M + kBM - 1) / kBM) * (a.N / BN);
   const int n_sm = sm_count();
   const int grid = ntiles < n_sm ? ntiles : n_sm;
-  kern<<<grid, w4::threads<A_PACKED || B_PACKED>(), C::SMEM_BYTES, st>>>(
+  kern<<<grid, w4::threads<A_PACKED>(), C::SMEM_BYTES, st>>>(
       tA, tB, tAS, tBS, tLA, tUP, static_cast<const __nv_bfloat16*>(a.bias),
       static_cast<__nv_bfloat16*>(a.out), a.partials, a.M, a.N, a.K,
       a.partials ? 0 : a.rank_pad, a.gelu);
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
-}
-
-// Tile width of the W4A4 GEMM (128 or 64; GWB_W4A4_BN overrides, for measurement).
-static int w4a4_tile_n() {
-  static int bn = 0;
-  if (bn == 0) {
-    const char* e = getenv("GWB_W4A4_BN");
-    bn = (e && atoi(e) == 64) ? 64 : 128;
-  }
-  return bn;
 }
 
 int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, bool b_packed, cudaStream_t st) {
@@ -1119,14 +1119,12 @@ int launch_gemm_w4a4(const W4A4Args& a, bool a_packed, bool b_packed, cudaStream
     return GWB_E_ALIGN;
   // stored weight scales [N, G]: each row must start on a 16-byte boundary
   if (b_packed && (G % 8)) return GWB_E_SHAPE;
-  const bool bn64 = w4a4_tile_n() == 64;
-  if (a_packed && b_packed)
-    return bn64 ? launch_gemm_w4a4_cfg<true, true, 64>(a, st) : launch_gemm_w4a4_cfg<true, true, 128>(a, st);
-  if (a_packed)
-    return bn64 ? launch_gemm_w4a4_cfg<true, false, 64>(a, st) : launch_gemm_w4a4_cfg<true, false, 128>(a, st);
-  if (b_packed)
-    return bn64 ? launch_gemm_w4a4_cfg<false, true, 64>(a, st) : launch_gemm_w4a4_cfg<false, true, 128>(a, st);
-  return bn64 ? launch_gemm_w4a4_cfg<false, false, 64>(a, st) : launch_gemm_w4a4_cfg<false, false, 128>(a, st);
+  // tile 128 x 128: a 64-wide tile (four TMEM group buffers) measured half
+  // the throughput, the per-group issue and hand-off latency being fixed
+  if (a_packed && b_packed) return launch_gemm_w4a4_cfg<true, true, 128>(a, st);
+  if (a_packed) return launch_gemm_w4a4_cfg<true, false, 128>(a, st);
+  if (b_packed) return launch_gemm_w4a4_cfg<false, true, 128>(a, st);
+  return launch_gemm_w4a4_cfg<false, false, 128>(a, st);
 }
 
 int launch_gemm_nvfp4(const NvFp4Args& a, cudaStream_t st) {
