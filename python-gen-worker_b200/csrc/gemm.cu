@@ -873,16 +873,21 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       // ------------------------------------------------ low-rank B operands
       // per tile and 64-rank chunk: u_hi then u_lo ([BN rows x 64 ranks]
       // bf16, SWIZZLE_128B K-major) from up_w2 f32 [N, rank_pad] and s2
+      // Thread 0 also waits on `empty` for every k-block stage it does not
+      // fill: a parity wait only tells phases apart one phase ahead, so a
+      // waiter that skipped uses of a stage could mistake an older
+      // completion for the one it needs and overwrite a stage in use.
       const int tid = threadIdx.x - 64;
       const float inv_s2 = 1.0f / a_work[1];
       int ui = 0;
-      bool live = true;
+      bool live = true, live0 = true;
       for (int tile = blockIdx.x; live && tile < ntiles; tile += gridDim.x) {
         const int n0 = (tile % tiles_n) * BN;
         for (int h = 0; h < lr_slots; ++h, ++ui) {
           const int u = ui % STAGES;
           if (tid == 0)
-            *lr_flag = mbar_wait(&empty[u], ((ui / STAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_UNPACK) ? 1u : 0u;
+            *lr_flag = (live0 && mbar_wait(&empty[u], ((ui / STAGES) & 1) ^ 1,
+                                           GWB_ERR_TIMEOUT_UNPACK)) ? 1u : 0u;
           asm volatile("bar.sync 2, %0;" ::"n"(LR_THREADS) : "memory");
           if (*reinterpret_cast<volatile uint32_t*>(lr_flag) == 0u) { live = false; break; }
           const int c0 = 64 * (h >> 1);
@@ -914,7 +919,10 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           asm volatile("bar.sync 2, %0;" ::"n"(LR_THREADS) : "memory");
           if (tid == 0) mbar_arrive(&full[u]);
         }
-        ui += nk;   // the k-block stages are filled by the TMA warp alone
+        // the k-block stages are filled by the TMA warp alone; follow their phases
+        for (int kb = 0; kb < nk; ++kb, ++ui)
+          if (tid == 0 && live0)
+            live0 = mbar_wait(&empty[ui % STAGES], ((ui / STAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_UNPACK);
       }
     }
   } else {
