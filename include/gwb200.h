@@ -231,8 +231,11 @@ int gwb_nvfp4_quant(const void* x, const void* smooth, int64_t M, int64_t K, voi
  * `SvdqLinear.forward` (la = x2 @ proj_down on raw x, svdq_native.py:153),
  * computed in the pass that takes amax, so x is read twice instead of three
  * times: down_t bf16 [rank_pad, K] (proj_down transposed, zero-padded rows),
- * la bf16 [M, rank_pad] = bf16(x · proj_down) with f32 accumulation.
- * rank_pad in {16, 32, 48, 64}; other arguments as gwb_nvfp4_quant. */
+ * la: the three-part form bf16 [M, 3 * rank_pad] = [u_hi | u_lo | u_hi]
+ * with u = bf16(x · proj_down) / s2 (f32 accumulation, then the bf16
+ * rounding of the reference's matmul) split into two bf16 parts.
+ * rank_pad a multiple of 16, at most 128; other arguments as
+ * gwb_nvfp4_quant. */
 int gwb_nvfp4_quant_lowrank(const void* x, const void* smooth, const void* down_t, int64_t M,
                             int64_t K, int rank_pad, void* codes, void* sblk, float* work,
                             void* la, void* stream);
@@ -243,12 +246,12 @@ int gwb_nvfp4_quant_lowrank(const void* x, const void* smooth, const void* down_
  * * s2 * w_scale_2[n] + la·proj_up^T + bias -> bf16 [M, N]. w_codes / w_sblk
  * / w_scale_2 are the reference module's `weight` / `weight_scale` /
  * `weight_scale_2` buffers as stored (w_scale_2 per channel [N] when
- * ws2_per_channel, else [1]). The low-rank branch shares the accumulator:
- * la = bf16(x · proj_down) [M, rank_pad] on raw x (as the reference) and
- * proj_up = f32 proj_up / w_scale_2[n] [N, rank_pad] (the load-time form);
- * the kernel divides it by the call's s2 (a_work[1]) and splits it into two
- * bf16 operands in shared memory. K % 256 == 0, N % 128 == 0,
- * rank_pad <= 128. */
+ * ws2_per_channel, else [1]). The low-rank branch shares the accumulator
+ * in its units (divided by s2 * w_scale_2[n]): la = the three-part la3
+ * [M, 3 * rank_pad] of gwb_nvfp4_quant_lowrank, proj_up = the three-part
+ * up3 bf16 [N, 3 * rank_pad] = [w_hi | w_hi | w_lo], w = proj_up /
+ * w_scale_2[n] split into two bf16 parts (load time); la3 · up3ᵀ keeps the
+ * product to ~2^-17. K % 256 == 0, N % 128 == 0, rank_pad <= 128. */
 int gwb_nvfp4_gemm(const void* a_codes, const void* a_sblk, const float* a_work,
                    const void* w_codes, const void* w_sblk, const float* w_scale_2,
                    int ws2_per_channel, const void* la, const void* proj_up, const void* bias,

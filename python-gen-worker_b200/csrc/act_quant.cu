@@ -575,10 +575,27 @@ __device__ __forceinline__ uint32_t e2m1x2_code(float a, float b) {
 __global__ void __launch_bounds__(256)
 act_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ smooth,
                  float* __restrict__ work, uint8_t* __restrict__ codes,
-                 uint8_t* __restrict__ sblk, int M, int K) {
+                 uint8_t* __restrict__ sblk, int M, int K,
+                 __nv_bfloat16* __restrict__ la3 = nullptr, int rank_pad = 0) {
   const float amax = __uint_as_float(*reinterpret_cast<const volatile unsigned int*>(work));
   const float s2 = fmaxf(__fdiv_rn(amax, 6.0f * 448.0f), 1e-12f);
   if (blockIdx.x == 0 && threadIdx.x == 0) work[1] = s2;
+  if (la3 != nullptr) {
+    // la3 row = [u_hi | u_lo | u_hi], u = la / s2 (la = bf16(x · proj_down),
+    // in columns [0, rank_pad) of the row); one thread owns each (row, j)
+    const int64_t nla = (int64_t)M * rank_pad;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nla;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      __nv_bfloat16* r = la3 + (i / rank_pad) * 3 * rank_pad;
+      const int j = (int)(i % rank_pad);
+      const float u = __fdiv_rn(__bfloat162float(r[j]), s2);
+      const __nv_bfloat16 uh = __float2bfloat16_rn(u);
+      const __nv_bfloat16 ul = __float2bfloat16_rn(u - __bfloat162float(uh));
+      r[j] = uh;
+      r[rank_pad + j] = ul;
+      r[2 * rank_pad + j] = uh;
+    }
+  }
   const float d6 = 6.0f * s2;
   const int kb16 = K / 16;
   const int ncb = (kb16 + 3) / 4;
@@ -635,7 +652,8 @@ act_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __res
 }
 
 // amax |bf16(x / smooth)| (as nvfp4_amax_kernel) fused with the low-rank
-// down-projection la = bf16(x · L1) on RAW x, so the NVFP4 lane reads x twice
+// down-projection la = bf16(x · L1) on RAW x (written to the first rank_pad
+// columns of the [M, 3 * rank_pad] la3 rows; act_nvfp4_kernel then splits it), so the NVFP4 lane reads x twice
 // per call (this pass and the quantiser) instead of three times. Layout and
 // MMA fragments as act_int4_kernel: 16 rows per CTA, 8 warps splitting K in
 // 64-wide chunks, lane (g, c) on rows g and g + 8 and the 16 columns
@@ -729,7 +747,7 @@ nvfp4_amax_la_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
 #pragma unroll
     for (int w2 = 0; w2 < WARPS; ++w2) sum += red[w2][r][col];
     const int row = blockIdx.x * ROWS + r;
-    if (row < M) la[(size_t)row * RP + col] = __float2bfloat16_rn(sum);
+    if (row < M) la[(size_t)row * (3 * RP) + col] = __float2bfloat16_rn(sum);
   }
 }
 
@@ -794,7 +812,7 @@ int launch_act_nvfp4_lowrank(const void* x, const void* smooth, const void* down
   int64_t blocks = (nblk + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   act_nvfp4_kernel<<<(int)blocks, 256, 0, st>>>(X, Sm, work, static_cast<uint8_t*>(codes),
-                                                 static_cast<uint8_t*>(sblk), M, K);
+                                                 static_cast<uint8_t*>(sblk), M, K, L, rank_pad);
   return cudaGetLastError() == cudaSuccess ? GWB_SUCCESS : GWB_E_LAUNCH;
 }
 

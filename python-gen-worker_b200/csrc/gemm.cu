@@ -692,12 +692,14 @@ gemm_w4a4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 // tiles (SWIZZLE_128B) and three 2 KB bulk copies bring the blocked scale
 // tiles (A rows, B rows 0-127, B rows 128-255); the MMA thread copies each
 // 128 x 4 scale tile into TMEM (tcgen05.cp) and issues four K = 64 MMAs.
-// The low-rank product is issued first into the same accumulator, with the
-// up-projection divided by the second-level scales: u = proj_up[n] /
-// (weight_scale_2[n] * s2) is split into two bf16 operands u_hi + u_lo
-// (error ~2^-17 of u) that warps 2-3 build in shared memory per tile from
-// the f32 load-time form proj_up / weight_scale_2 and the call's s2, so
-// acc = main + la · uᵀ and the epilogue is y = acc * s2 * weight_scale_2[n] + bias.
+// The low-rank product is issued first into the same accumulator, in the
+// accumulator's units (divided by s2 * weight_scale_2[n]) and exact to
+// ~2^-17: the quantiser writes la3 = [u_hi | u_lo | u_hi] with u = bf16(x ·
+// proj_down) / s2 split into two bf16 parts, the load-time form of the
+// up-projection is up3 = [w_hi | w_hi | w_lo] with w = proj_up[n] /
+// weight_scale_2[n] split alike, and la3 · up3ᵀ = u_hi w_hi + u_lo w_hi +
+// u_hi w_lo (the u_lo w_lo term is below 2^-17). Both are TMA-loaded. The
+// epilogue is y = acc * s2 * weight_scale_2[n] + bias.
 namespace nv4 {
 constexpr int BN = 256;
 constexpr int KB_BYTES = 128;                 // packed bytes of one k-block row (256 codes)
@@ -712,8 +714,7 @@ constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0, SF_COL = 256;
 constexpr int SF_SLOT = 48;                   // SFA 16 columns + SFB 32 columns
 constexpr int SF_SLOTS = 4;
-constexpr int THREADS = 384;                  // warp 0 TMA, 1 MMA, 2-3 low-rank B, 4-11 epilogue
-constexpr int LR_THREADS = 64;                // warps 2-3
+constexpr int THREADS = 384;                  // warp 0 TMA, 1 MMA, 4-11 epilogue
 constexpr int EPI0 = 4;
 constexpr int EPI_WARPS = 8;
 constexpr int EC = BN / 2;
@@ -724,7 +725,7 @@ static_assert(nv4::SF_COL + nv4::SF_SLOTS * nv4::SF_SLOT <= nv4::TMEM_COLS, "TME
 
 __global__ void __launch_bounds__(nv4::THREADS, 1)
 gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                  const __grid_constant__ CUtensorMap tmLA, const float* __restrict__ up_w2,
+                  const __grid_constant__ CUtensorMap tmLA, const __grid_constant__ CUtensorMap tmUP,
                   const uint8_t* __restrict__ a_sblk, const uint8_t* __restrict__ w_sblk,
                   const float* __restrict__ a_work, const float* __restrict__ w_scale_2,
                   int ws2_per_channel, const __nv_bfloat16* __restrict__ bias,
@@ -737,25 +738,22 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
-  uint32_t* lr_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = K / 256;
   const int ncb = K / 64;                     // blocked-layout tile columns per 128 rows
   const int has_lr = rank_pad > 0 ? 1 : 0;
-  // the low-rank operands take two ring stages (u_hi, u_lo) per 64 ranks
-  // (128-byte rows); la is TMA-loaded into both
-  const int lr_chunks = has_lr ? (rank_pad + 63) / 64 : 0;
-  const int lr_slots = 2 * lr_chunks;
+  // the three-part low-rank operands (K = 3 * rank_pad) take one ring stage
+  // per 64 of K (128-byte rows)
+  const int lr_k = 3 * rank_pad;
+  const int lr_slots = has_lr ? (lr_k + 63) / 64 : 0;
   // N % 256 == 128: the last N tile is half a tile (B rows past N read as
   // zeros by TMA; their scale tiles are not loaded and their columns not stored)
   const int tiles_n = (N + BN - 1) / BN;
   const int ntiles = ((M + kBM - 1) / kBM) * tiles_n;
 
   if (threadIdx.x == 0) {
-    // with a low-rank branch every stage's `full` also waits for the
-    // low-rank builder warps (the TMA lane arrives twice on k-block stages)
-    for (int i = 0; i < STAGES; ++i) { mbar_init(&full[i], has_lr ? 2 : 1); mbar_init(&empty[i], 1); }
+    for (int i = 0; i < STAGES; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, EPI_WARPS);
     fence_barrier_init();
@@ -786,10 +784,11 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           ok = __all_sync(0xFu, ok);
           if (!ok) break;
           if (pl == 0) {
-            // la ranks 64 (h / 2) .. +63 (the builders write u_hi or u_lo beside it)
+            // columns 64h .. 64h+63 of la3 and up3
             uint8_t* us = smem + u * STAGE_BYTES;
-            mbar_arrive_expect_tx(&full[u], kBM * 128);
-            tma_load_2d(us, &tmLA, &full[u], 64 * (h >> 1), m0);
+            mbar_arrive_expect_tx(&full[u], kBM * 128 + BN * 128);
+            tma_load_2d(us, &tmLA, &full[u], 64 * h, m0);
+            tma_load_2d(us + A_BYTES, &tmUP, &full[u], 64 * h, n0);
           }
           __syncwarp(0xFu);
         }
@@ -798,10 +797,8 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           const int u = ui % STAGES;
           ok = mbar_wait(&empty[u], ((ui / STAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER);
           if (!__all_sync(0xFu, ok)) break;
-          if (pl == 0) {
+          if (pl == 0)
             mbar_arrive_expect_tx(&full[u], half_n ? STAGE_BYTES - SFA_BYTES : STAGE_BYTES);
-            if (has_lr) mbar_arrive(&full[u]);
-          }
           __syncwarp(0xFu);
           uint8_t* us = smem + u * STAGE_BYTES;
           uint8_t* sfa = us + A_BYTES + B_BYTES;
@@ -830,14 +827,13 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         if (!mbar_wait(acc_empty, (lt & 1) ^ 1, GWB_ERR_TIMEOUT_MMA)) break;
         tc_fence_after();
         for (int h = 0; h < lr_slots; ++h, ++ui) {
-          // acc <- la · (u_hi + u_lo)ᵀ, u = proj_up / (weight_scale_2 · s2); one
-          // ring stage per 64 ranks and part
+          // acc <- la3 · up3ᵀ, one ring stage per 64 of K
           const int u = ui % STAGES;
           ok = mbar_wait(&full[u], (ui / STAGES) & 1, GWB_ERR_TIMEOUT_MMA);
           if (!ok) break;
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + u * STAGE_BYTES), b_base = a_base + A_BYTES;
-          const int nk16 = min(4, (rank_pad - 64 * (h >> 1)) / 16);
+          const int nk16 = min(4, (lr_k - 64 * h) / 16);
           for (int k = 0; k < nk16; ++k)
             mma_f16(tmem + ACC_COL, sdesc_k128(a_base + 32 * k), sdesc_k128(b_base + 32 * k),
                     idesc_lr, (h > 0 || k > 0) ? 1u : 0u);
@@ -868,61 +864,6 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           mma_commit(&empty[u]);
         }
         if (ok) mma_commit(acc_full);
-      }
-    } else if (warp >= 2 && has_lr) {
-      // ------------------------------------------------ low-rank B operands
-      // per tile and 64-rank chunk: u_hi then u_lo ([BN rows x 64 ranks]
-      // bf16, SWIZZLE_128B K-major) from up_w2 f32 [N, rank_pad] and s2
-      // Thread 0 also waits on `empty` for every k-block stage it does not
-      // fill: a parity wait only tells phases apart one phase ahead, so a
-      // waiter that skipped uses of a stage could mistake an older
-      // completion for the one it needs and overwrite a stage in use.
-      const int tid = threadIdx.x - 64;
-      const float inv_s2 = 1.0f / a_work[1];
-      int ui = 0;
-      bool live = true, live0 = true;
-      for (int tile = blockIdx.x; live && tile < ntiles; tile += gridDim.x) {
-        const int n0 = (tile % tiles_n) * BN;
-        for (int h = 0; h < lr_slots; ++h, ++ui) {
-          const int u = ui % STAGES;
-          if (tid == 0)
-            *lr_flag = (live0 && mbar_wait(&empty[u], ((ui / STAGES) & 1) ^ 1,
-                                           GWB_ERR_TIMEOUT_UNPACK)) ? 1u : 0u;
-          asm volatile("bar.sync 2, %0;" ::"n"(LR_THREADS) : "memory");
-          if (*reinterpret_cast<volatile uint32_t*>(lr_flag) == 0u) { live = false; break; }
-          const int c0 = 64 * (h >> 1);
-          const int width = min(64, rank_pad - c0);   // ranks in this chunk (multiple of 16)
-          const int cpr = width / 8;                  // 16-byte chunks per row
-          uint8_t* bs = smem + u * STAGE_BYTES + A_BYTES;
-          for (int i = tid; i < BN * cpr; i += LR_THREADS) {
-            const int r = i / cpr, cj = i % cpr;
-            const int n = n0 + r;
-            uint32_t o[4] = {0u, 0u, 0u, 0u};
-            if (n < N) {
-              const float4* src =
-                  reinterpret_cast<const float4*>(up_w2 + (size_t)n * rank_pad + c0 + 8 * cj);
-              const float4 f0 = __ldg(src), f1 = __ldg(src + 1);
-              const float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                float a = v[2 * j] * inv_s2, b = v[2 * j + 1] * inv_s2;
-                if (h & 1) {   // u_lo = bf16(u - bf16(u))
-                  a -= __bfloat162float(__float2bfloat16_rn(a));
-                  b -= __bfloat162float(__float2bfloat16_rn(b));
-                }
-                o[j] = pack_bf16x2(a, b);
-              }
-            }
-            *reinterpret_cast<uint4*>(bs + swz128(r, 16 * cj)) = make_uint4(o[0], o[1], o[2], o[3]);
-          }
-          fence_proxy_async_smem();
-          asm volatile("bar.sync 2, %0;" ::"n"(LR_THREADS) : "memory");
-          if (tid == 0) mbar_arrive(&full[u]);
-        }
-        // the k-block stages are filled by the TMA warp alone; follow their phases
-        for (int kb = 0; kb < nk; ++kb, ++ui)
-          if (tid == 0 && live0)
-            live0 = mbar_wait(&empty[ui % STAGES], ((ui / STAGES) & 1) ^ 1, GWB_ERR_TIMEOUT_UNPACK);
       }
     }
   } else {
@@ -1146,7 +1087,7 @@ int launch_gemm_nvfp4(const NvFp4Args& a, cudaStream_t st) {
       (a.up && !al16(a.up)) || (reinterpret_cast<uintptr_t>(a.a_work) & 7u) ||
       (reinterpret_cast<uintptr_t>(a.w_scale_2) & 3u))
     return GWB_E_ALIGN;
-  CUtensorMap tA, tB, tLA;
+  CUtensorMap tA, tB, tLA, tUP;
   int rc = make_tmap(&tA, a.a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.K / 2, a.M,
                      nv4::KB_BYTES, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
@@ -1154,9 +1095,13 @@ int launch_gemm_nvfp4(const NvFp4Args& a, cudaStream_t st) {
                  nv4::BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   tLA = tA;
+  tUP = tB;
   if (a.rank_pad > 0) {
-    rc = make_tmap(&tLA, a.la, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.rank_pad, a.M, 64, kBM,
+    rc = make_tmap(&tLA, a.la, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3 * a.rank_pad, a.M, 64, kBM,
                    CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_tmap(&tUP, a.up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3 * a.rank_pad, a.N, 64,
+                   nv4::BN, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
   static bool attr = false;
@@ -1168,7 +1113,7 @@ int launch_gemm_nvfp4(const NvFp4Args& a, cudaStream_t st) {
   const int ntiles = ((a.M + kBM - 1) / kBM) * ((a.N + nv4::BN - 1) / nv4::BN);
   const int n_sm = sm_count();
   gemm_nvfp4_kernel<<<ntiles < n_sm ? ntiles : n_sm, nv4::THREADS, nv4::SMEM_BYTES, st>>>(
-      tA, tB, tLA, static_cast<const float*>(a.up), static_cast<const uint8_t*>(a.a_sblk),
+      tA, tB, tLA, tUP, static_cast<const uint8_t*>(a.a_sblk),
       static_cast<const uint8_t*>(a.w_sblk), a.a_work, a.w_scale_2, a.ws2_per_channel,
       static_cast<const __nv_bfloat16*>(a.bias), static_cast<__nv_bfloat16*>(a.out), a.M, a.N,
       a.K, a.rank_pad);

@@ -28,6 +28,7 @@ int launch_act_fp8(const void* x, void* q, void* scale, int M, int K, cudaStream
 // e4m3 scales (padding rows written as zeros).
 int launch_act_nvfp4(const void* x, const void* smooth, float* work, void* codes, void* sblk,
                      int M, int K, cudaStream_t st);
+// la: the three-part la3 bf16 [M, 3 * rank_pad] (see act_nvfp4_kernel)
 int launch_act_nvfp4_lowrank(const void* x, const void* smooth, const void* down_t, float* work,
                              void* codes, void* sblk, void* la, int M, int K, int rank_pad,
                              cudaStream_t st);
@@ -40,8 +41,8 @@ struct NvFp4Args {
   const void* w_sblk;      // e4m3 block scales, blocked layout
   const float* w_scale_2;  // f32 [1] or [N]
   int ws2_per_channel;
-  const void* la;          // bf16 [M, rank_pad] or null
-  const void* up;          // f32 [N, rank_pad] = proj_up / weight_scale_2 (load time), or null
+  const void* la;          // bf16 [M, 3 * rank_pad] three-part la3 (quantiser), or null
+  const void* up;          // bf16 [N, 3 * rank_pad] three-part up3 (load time), or null
   const void* bias;        // bf16 [N] or null
   void* out;               // bf16 [M, N]
   int M, N, K, rank_pad;

@@ -215,9 +215,10 @@ class SvdqNvfp4Linear(nn.Module):
     Forward: the smoothing divide, per-tensor ``s2`` with ``la = x ·
     proj_down`` (bf16 on raw x, as the reference) in the same pass, the NVFP4
     activation codes in a second pass, then one block-scaled tcgen05 GEMM whose accumulator
-    starts from the low-rank product (up-projection divided by
-    ``weight_scale_2 · s2`` inside the GEMM, as two bf16 operands) and ends
-    with ``· s2 · weight_scale_2 + bias``. No torch op runs per call."""
+    starts from the low-rank product (divided by ``weight_scale_2 · s2``: the
+    quantiser writes la / s2 and the load-time up-projection is proj_up /
+    weight_scale_2, each as two bf16 parts, exact to ~2^-17) and ends with
+    ``· s2 · weight_scale_2 + bias``. No torch op runs per call."""
     _cozy_svdq_linear = True
     layout = LAYOUT_NVFP4
 

@@ -428,9 +428,11 @@ def _(x2, smooth):
 @torch.library.custom_op("gwb200::nvfp4_quant_lowrank", mutates_args=())
 def nvfp4_quant_lowrank(x2: torch.Tensor, smooth: Optional[torch.Tensor], down_t: torch.Tensor
                         ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    """:func:`nvfp4_quant` plus ``la = bf16(x2 · proj_down)`` on raw x from the
-    same pass over x: down_t bf16 [rank_pad, K] -> (codes, blocked scales,
-    work, la bf16 [M, rank_pad])."""
+    """:func:`nvfp4_quant` plus the low-rank activations from the same pass
+    over x: down_t bf16 [rank_pad, K] -> (codes, blocked scales, work, la3
+    bf16 [M, 3 * rank_pad]). la3 = [u_hi | u_lo | u_hi] with u = bf16(x2 ·
+    proj_down) / s2 (raw x, as the reference) split into two bf16 parts
+    (:func:`nvfp4_la_from_la3` recovers bf16(x2 · proj_down))."""
     _need(x2, "x2", torch.bfloat16, 2)
     _need(smooth, "smooth", torch.bfloat16, 1)
     _need(down_t, "down_t", torch.bfloat16, 2)
@@ -441,7 +443,7 @@ def nvfp4_quant_lowrank(x2: torch.Tensor, smooth: Optional[torch.Tensor], down_t
     codes = torch.empty(m, k // 2, dtype=torch.uint8, device=x2.device)
     sblk = torch.empty(nvfp4_blocked_numel(m, k), dtype=torch.uint8, device=x2.device)
     work = torch.empty(4 + k, dtype=torch.float32, device=x2.device)
-    la = torch.empty(m, rp, dtype=torch.bfloat16, device=x2.device)
+    la = torch.empty(m, 3 * rp, dtype=torch.bfloat16, device=x2.device)
     native.check(native.require().gwb_nvfp4_quant_lowrank(
         x2.data_ptr(), _ptr(smooth), down_t.data_ptr(), m, k, rp, codes.data_ptr(),
         sblk.data_ptr(), work.data_ptr(), la.data_ptr(), _stream()), "nvfp4_quant_lowrank")
@@ -454,7 +456,14 @@ def _(x2, smooth, down_t):
     return (x2.new_empty(m, k // 2, dtype=torch.uint8),
             x2.new_empty(nvfp4_blocked_numel(m, k), dtype=torch.uint8),
             x2.new_empty(4 + k, dtype=torch.float32),
-            x2.new_empty(m, down_t.shape[0], dtype=torch.bfloat16))
+            x2.new_empty(m, 3 * down_t.shape[0], dtype=torch.bfloat16))
+
+
+def nvfp4_la_from_la3(la3: torch.Tensor, work: torch.Tensor) -> torch.Tensor:
+    """(u_hi + u_lo) · s2: the low-rank activation bf16(x · proj_down) the
+    three-part form was built from (to ~2^-17), f32 [M, rank_pad]."""
+    rp = la3.shape[1] // 3
+    return (la3[:, :rp].float() + la3[:, rp:2 * rp].float()) * work[1]
 
 
 @torch.library.custom_op("gwb200::nvfp4_gemm", mutates_args=())
@@ -463,9 +472,10 @@ def nvfp4_gemm(codes: torch.Tensor, sblk: torch.Tensor, work: torch.Tensor, w_co
                proj_up: Optional[torch.Tensor], bias: Optional[torch.Tensor]) -> torch.Tensor:
     """Block-scaled NVFP4 GEMM + ``s2 · weight_scale_2`` + low-rank + bias
     -> bf16 [M, N] (``_gemm_w4a4`` and the rest of the NVFP4
-    ``SvdqLinear.forward``, ``svdq_native.py:148-155``). ``proj_up`` is the
-    load-time f32 ``proj_up / weight_scale_2`` [N, rank_pad]
-    (:func:`nvfp4_lowrank_prepare`); the kernel applies the call's ``s2``."""
+    ``SvdqLinear.forward``, ``svdq_native.py:148-155``). The low-rank operands
+    are three-part: la3 [M, 3 * rank_pad] from :func:`nvfp4_quant_lowrank` and
+    up3 [N, 3 * rank_pad] from :func:`nvfp4_lowrank_prepare`; la3 · up3ᵀ is
+    the low-rank product divided by ``s2 · weight_scale_2``."""
     _need(codes, "codes", torch.uint8, 2)
     _need(w_codes, "w_codes", torch.uint8, 2)
     _need(work, "work", torch.float32, 1)
@@ -486,10 +496,11 @@ def nvfp4_gemm(codes: torch.Tensor, sblk: torch.Tensor, work: torch.Tensor, w_co
     rp = 0
     if la is not None and proj_up is not None and la.shape[1] > 0:
         _need(la, "la", torch.bfloat16, 2)
-        _need(proj_up, "proj_up", torch.float32, 2)
-        rp = int(la.shape[1])
-        if tuple(proj_up.shape) != (n, rp):
-            raise SvdqB200Error(f"proj_up {tuple(proj_up.shape)} != [{n}, {rp}]")
+        _need(proj_up, "proj_up", torch.bfloat16, 2)
+        if la.shape[1] % 3 or tuple(proj_up.shape) != (n, la.shape[1]):
+            raise SvdqB200Error(f"three-part la {tuple(la.shape)} / up {tuple(proj_up.shape)} "
+                                f"do not match (want [M, 3r] and [{n}, 3r])")
+        rp = int(la.shape[1]) // 3
     out = torch.empty(m, n, dtype=torch.bfloat16, device=codes.device)
     lib = native.require()
     native.check(lib.gwb_nvfp4_gemm(codes.data_ptr(), sblk.data_ptr(), work.data_ptr(),
@@ -502,16 +513,20 @@ def nvfp4_gemm(codes: torch.Tensor, sblk: torch.Tensor, work: torch.Tensor, w_co
 
 def nvfp4_lowrank_prepare(proj_down: torch.Tensor, proj_up: torch.Tensor,
                           w_scale_2: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """Load time: ``proj_down`` bf16 padded to [K, rank_pad] and the fp32
-    ``proj_up / weight_scale_2[n]`` padded to [N, rank_pad]."""
+    """Load time: ``proj_down`` bf16 padded to [K, rank_pad], and the
+    three-part up-projection up3 bf16 [N, 3 * rank_pad] = [w_hi | w_hi |
+    w_lo] with w = proj_up / weight_scale_2[n] (f32) split into two bf16
+    parts, so that la3 · up3ᵀ = u_hi w_hi + u_lo w_hi + u_hi w_lo."""
     k, r = proj_down.shape
     n = proj_up.shape[0]
     rp = rank_pad_of(r)
     down = torch.zeros(k, rp, dtype=torch.bfloat16, device=proj_down.device)
     down[:, :r] = proj_down.to(torch.bfloat16)
-    up = torch.zeros(n, rp, dtype=torch.float32, device=proj_up.device)
-    up[:, :r] = proj_up.float() / w_scale_2.float().reshape(-1, 1)
-    return down, up
+    w = torch.zeros(n, rp, dtype=torch.float32, device=proj_up.device)
+    w[:, :r] = proj_up.float() / w_scale_2.float().reshape(-1, 1)
+    hi = w.to(torch.bfloat16)
+    lo = (w - hi.float()).to(torch.bfloat16)
+    return down, torch.cat([hi, hi, lo], dim=1).contiguous()
 
 
 @nvfp4_gemm.register_fake

@@ -191,5 +191,5 @@ def test_nvfp4_quant_lowrank_rank128(cuda_ready, m, k, rank):
     c1, b1, w1, la = ops.nvfp4_quant_lowrank(x.cuda(), sm.cuda(), down.t().contiguous().cuda())
     c0, b0, w0 = ops.nvfp4_quant(x.cuda(), sm.cuda())
     assert torch.equal(c1, c0) and torch.equal(b1, b0) and torch.equal(w1[:2], w0[:2])
-    assert la_within_bound(la.cpu(), x, down)
+    assert la_within_bound(ops.nvfp4_la_from_la3(la, w1).cpu(), x, down)
     assert native.device_error() == 0

@@ -263,7 +263,13 @@ def test_nvfp4_quant_lowrank_matches_separate_passes(cuda_ready, m, k, rank, smo
     assert torch.equal(c1, c0) and torch.equal(b1, b0)
     assert torch.equal(w1[:2], w0[:2])
     want = x.double() @ down.double()
-    assert O.rel_l2(la.cpu(), want) <= 4e-3
+    la_rec = ops.nvfp4_la_from_la3(la, w1).cpu()
+    assert O.rel_l2(la_rec, want) <= 4e-3
+    # the three-part form: u_hi repeated, and (u_hi + u_lo) * s2 within bf16
+    # rounding of the exact product (the reference rounds x · proj_down to bf16)
+    assert torch.equal(la[:, :rank], la[:, 2 * rank:])
+    bound = want.abs() * 2.0 ** -8 + (x.double().abs() @ down.double().abs()) * k * 2.0 ** -24
+    assert bool(((la_rec.double() - want).abs() <= bound + 1e-30).all())
     assert native.device_error() == 0
 
 
