@@ -150,7 +150,7 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- model
-def build_stack(device, seed: int = 0):
+def build_stack(device, seed: int = 0, weight_form: str = "stored"):
     """Random-init W4A4 stack on `device` (weights quantised on the GPU with
     the library's producer)."""
     from gen_worker_b200.modules import build_svdq_int4_linear, quantize_int4_rows
@@ -174,7 +174,7 @@ def build_stack(device, seed: int = 0):
                "proj_up": (torch.randn(n, RANK, generator=g, device=device) * 0.02).to(torch.bfloat16),
                "bias": (torch.randn(n, generator=g, device=device) * 0.02).to(torch.bfloat16)}
         del w
-        mod = build_svdq_int4_linear(buf, gelu=gelu, device=device)
+        mod = build_svdq_int4_linear(buf, gelu=gelu, device=device, weight_form=weight_form)
         mod.prepare()
         return mod
 
@@ -762,6 +762,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--weight-form", choices=["stored", "operand"], default="stored",
+                    help="W4A4 weights as stored (default) or expanded at load time")
     ap.add_argument("--case", choices=sorted(CASES) + ["awq", "peaks"], default=None,
                     help="time one BASELINE config's linears instead of the cfg4 stack")
     args = ap.parse_args()
@@ -807,7 +809,7 @@ def main() -> int:
     if TOKENS % world:
         raise SystemExit(f"{TOKENS} tokens do not split evenly over {world} ranks")
     m = TOKENS // world
-    layers = build_stack(dev)
+    layers = build_stack(dev, weight_form=args.weight_form)
     wbytes = weight_bytes(layers)
     g = torch.Generator(device=dev).manual_seed(99)
     x_full = torch.randn(TOKENS, HIDDEN, generator=g, device=dev)
@@ -907,7 +909,7 @@ def main() -> int:
             "config": {"workload": "cfg4 Flux DiT W4A4 linear stack, 19 dual + 38 single blocks",
                        "tokens": TOKENS, "tokens_per_rank": m, "hidden": HIDDEN, "rank": RANK,
                        "group": 64, "parallelism": f"token-shard x{world}, weights replicated",
-                       "weights_gb": wbytes / 1e9,
+                       "weights_gb": wbytes / 1e9, "weight_form": args.weight_form,
                        "l2": ("no flush: per-step working set %.1f GB of distinct weights "
                               "(>> 126 MB L2)" % (wbytes / 1e9))},
             "effective_tops": stack_ops() * TOKENS / (ms_max / 1e3) / 1e12,

@@ -67,8 +67,11 @@ class SvdqInt4Linear(nn.Module):
 
     def __init__(self, in_features: int, out_features: int, *, rank: int, bias: bool,
                  compute_dtype: Any = torch.bfloat16, smooth: bool = True,
-                 gelu: bool = False, device: Any = None) -> None:
+                 gelu: bool = False, device: Any = None, weight_form: str = "stored") -> None:
         super().__init__()
+        if weight_form not in ("stored", "operand"):
+            raise SvdqB200LayoutError(f"weight_form {weight_form!r} is not 'stored' or 'operand'")
+        self.weight_form = weight_form
         if in_features % _K_ALIGN or out_features % _N_ALIGN:
             raise SvdqB200LayoutError(
                 f"SvdqInt4Linear dims [{out_features}, {in_features}] break the "
@@ -108,9 +111,10 @@ class SvdqInt4Linear(nn.Module):
     @property
     def stored(self) -> bool:
         """True when the GEMM reads ``weight`` / ``weight_scale`` as stored
-        (in_features % 512 == 0); otherwise the weight is expanded once into
-        the e4m3 operand form at load time."""
-        return ops.stored_weights_supported(self.in_features)
+        (``weight_form="stored"``, the default, and in_features % 512 == 0);
+        otherwise the weight is expanded once into the e4m3 operand form at
+        load time (2.4x the device memory, ~5 % faster GEMMs)."""
+        return self.weight_form == "stored" and ops.stored_weights_supported(self.in_features)
 
     def prepare(self) -> Dict[str, Any]:
         """Kernel-layout copies of the low-rank buffers (and, when the stored
@@ -374,7 +378,8 @@ class Fp8RowwiseLinear(nn.Module):
 
 # ---------------------------------------------------------------- builders / swap
 def build_svdq_int4_linear(buf: Dict[str, Any], *, gelu: bool = False,
-                           device: Any = None) -> SvdqInt4Linear:
+                           device: Any = None,
+                           weight_form: str = "stored") -> SvdqInt4Linear:
     """A device-resident module from a buffer dict with the ``SvdqBuffers``
     field names (``svdq_layout.py:66-78``; ``build_svdq_linear``,
     ``svdq_native.py:173-197``)."""
@@ -384,7 +389,7 @@ def build_svdq_int4_linear(buf: Dict[str, Any], *, gelu: bool = False,
     rank = 0 if down is None else int(down.shape[1])
     mod = SvdqInt4Linear(k2 * 2, n, rank=rank, bias=buf.get("bias") is not None,
                          smooth=buf.get("smooth_factor") is not None, gelu=gelu,
-                         device=torch.device("cpu"))
+                         device=torch.device("cpu"), weight_form=weight_form)
     dev = device or w.device
     ws = buf["weight_scale"]
     if tuple(ws.shape) != (n, k2 * 2 // GROUP):
