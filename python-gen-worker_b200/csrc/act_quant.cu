@@ -16,9 +16,12 @@
 
 namespace gwb {
 
-// warps per CTA (splitting K round-robin in 64-wide chunks); with 128
-// registers per thread two CTAs share an SM
-template <int MT> __host__ __device__ constexpr int act_warps() { return 8; }
+// warps per CTA (splitting K round-robin in 64-wide chunks): 16 warps of
+// 128 registers fill an SM with one CTA, so a small token count (one CTA per
+// 16 rows, e.g. 132 CTAs for a 2112-token shard) still runs 16 warps per SM;
+// ranks above 64 keep 8 warps with the larger register budget. The count
+// never depends on M, so a row's results do not depend on the shard size.
+template <int NB> __host__ __device__ constexpr int act_warps() { return NB > 8 ? 8 : 16; }
 
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
@@ -152,7 +155,7 @@ __device__ __forceinline__ uint4 onehot_k8(uint32_t bits, int g) {
 }
 
 // NB = padded rank / 8 (0 = no low-rank branch); MT = m16 row tiles per CTA
-// (16 * MT rows); act_warps<MT>() warps split K round-robin in 64-wide chunks.
+// (16 * MT rows); act_warps<NB>() warps split K round-robin in 64-wide chunks.
 // MMA_FORM = false writes the interchange form: packed codes u8 [M, K/2] and
 // ascale f16 [M, K/64]. MMA_FORM = true writes the GEMM operand form: codes
 // u8 [M, K] as e4m3 bytes of q * 2^-9 in the within-8 operand order
@@ -163,13 +166,13 @@ __device__ __forceinline__ uint4 onehot_k8(uint32_t bits, int g) {
 // mma.sync; the per-warp partials are summed in a fixed order through
 // shared memory, so la is deterministic.
 template <int NB, bool MMA_FORM, int MT>
-__global__ void __launch_bounds__(act_warps<MT>() * 32, NB > 8 ? 1 : 2)
+__global__ void __launch_bounds__(act_warps<NB>() * 32, 1)
 act_int4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ smooth,
                 const __nv_bfloat16* __restrict__ down_t, uint8_t* __restrict__ codes,
                 __half* __restrict__ ascale, __nv_bfloat16* __restrict__ la, int M, int K) {
   constexpr int RP = NB * 8;
   constexpr int ROWS = 16 * MT;
-  constexpr int kActWarps = act_warps<MT>();
+  constexpr int kActWarps = act_warps<NB>();
   extern __shared__ float smem_f[];   // [K] smoothing reciprocals, then [kActWarps][ROWS][RP]
   float* rs = smem_f;
   float* red = smem_f + K;
@@ -325,18 +328,19 @@ template <bool MMA_FORM, int MT>
 static int launch_act_int4_mt(const void* x, const void* smooth, const void* down_t, void* codes,
                               void* ascale, void* la, int M, int K, int rank_pad,
                               cudaStream_t st) {
-  constexpr int kActWarps = act_warps<MT>();
-  dim3 grid((M + 16 * MT - 1) / (16 * MT)), block(kActWarps * 32);
+  dim3 grid((M + 16 * MT - 1) / (16 * MT));
   auto X = static_cast<const __nv_bfloat16*>(x);
   auto S = static_cast<const __nv_bfloat16*>(smooth);
   auto D = static_cast<const __nv_bfloat16*>(down_t);
   auto C = static_cast<uint8_t*>(codes);
   auto A = static_cast<__half*>(ascale);
   auto L = static_cast<__nv_bfloat16*>(la);
-  const size_t smem = ((size_t)K + (size_t)kActWarps * 16 * MT * rank_pad) * sizeof(float);
 #define GWB_ACT_CASE(RPAD, NBV)                                                              \
   case RPAD: {                                                                               \
     auto k = act_int4_kernel<NBV, MMA_FORM, MT>;                                             \
+    const dim3 block(act_warps<NBV>() * 32);                                                 \
+    const size_t smem = ((size_t)K + (size_t)act_warps<NBV>() * 16 * MT * rank_pad) *        \
+                        sizeof(float);                                                       \
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                                (int)smem);                                   \
     k<<<grid, block, smem, st>>>(X, S, D, C, A, L, M, K);                                    \
