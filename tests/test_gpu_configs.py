@@ -193,3 +193,39 @@ def test_nvfp4_quant_lowrank_rank128(cuda_ready, m, k, rank):
     assert torch.equal(c1, c0) and torch.equal(b1, b0) and torch.equal(w1[:2], w0[:2])
     assert la_within_bound(ops.nvfp4_la_from_la3(la, w1).cpu(), x, down)
     assert native.device_error() == 0
+
+
+def test_dual_block_chain_matches_oracle(cuda_ready):
+    """The bench's dual-stream block as a chain (out -> fc1 with GELU -> fc2,
+    each layer fed with the previous layer's bf16 output) at 192 tokens,
+    against the oracle running the same chain on its own outputs: every
+    layer's output meets the single-linear bar against the oracle fed with
+    the GPU's input, and the chain's end result stays within rel-L2 5e-3 of
+    the all-oracle chain (quantisation codes may flip where an input differs
+    in its last bf16 bit, so the end-to-end bar is looser)."""
+    m = 192
+    x = O.synth_activation(m, 3072, seed=501)
+    specs = [(3072, 3072, False), (3072, 12288, True), (12288, 3072, False)]
+    layers = []
+    calib = x[:128]
+    for i, (k, n, gelu) in enumerate(specs):
+        if i:
+            calib = O.synth_activation(128, k, seed=510 + i)
+        L = O.synth_svdq_layer(k, n, 32, seed=520 + i, x_calib=calib)
+        mod = build_svdq_int4_linear({"weight": L["w_packed"], "weight_scale": L["w_scale"],
+                                      "smooth_factor": L["smooth"], "proj_down": L["proj_down"],
+                                      "proj_up": L["proj_up"], "bias": L["bias"]},
+                                     gelu=gelu, device="cuda")
+        layers.append((L, mod, gelu))
+    h_gpu, h_ref = x.cuda(), x
+    for L, mod, gelu in layers:
+        y = mod(h_gpu)
+        step = O.svdq_int4_linear(h_gpu.cpu(), L["smooth"], L["w_packed"], L["w_scale"],
+                                  L["proj_down"], L["proj_up"], L["bias"], gelu=gelu)
+        assert O.rel_l2(y.cpu(), step["y"]) <= REL_TOL
+        assert O.max_abs_beyond_bf16(y.cpu(), step["y64"]) <= ABS_TOL
+        h_ref = O.svdq_int4_linear(h_ref, L["smooth"], L["w_packed"], L["w_scale"],
+                                   L["proj_down"], L["proj_up"], L["bias"], gelu=gelu)["y"]
+        h_gpu = y
+    assert O.rel_l2(h_gpu.cpu(), h_ref) <= 5e-3
+    assert native.device_error() == 0
