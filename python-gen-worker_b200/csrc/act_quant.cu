@@ -87,6 +87,41 @@ __device__ __forceinline__ void q8x2(float2 v, float2 s, float2 rs, uint32_t& b0
   b1 = (__float_as_uint(m.y) & 7u) | (q.y < -0.5f ? 0x80u : 0u);
 }
 
+// Two f32 -> e4m3 bytes, round to nearest even, saturating: `hi` in bits
+// 8-15, `lo` in bits 0-7.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float hi, float lo) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Clear the sign of every byte whose magnitude bits are zero (a negative
+// quotient that rounds to 0 converts to e4m3 -0; the operand byte is +0).
+__device__ __forceinline__ uint32_t e4m3_no_neg_zero(uint32_t w) {
+  const uint32_t nz = (w & 0x7F7F7F7Fu) + 0x7F7F7F7Fu;   // bit 7 set where bits 0-6 != 0
+  return w & (nz | 0x7F7F7F7Fu);
+}
+
+// GEMM operand bytes of 16 elements whose quotients satisfy |v/s| <= 7.25:
+// d = RN(v/s) * 2^-9 by the div_rn steps on exactly scaled operands
+// (s * 2^9 and RN(1/s) * 2^-9 are exact, so every step is the unscaled step
+// times 2^-9; only quotients below 2^-117 could differ, and those convert to
+// 0 either way), then e4m3 RN of d = rint(v/s) * 2^-9, the subnormal code
+// 0 000 |q|. Byte order as q8x2: lo = elements 0 2 4 6, hi = 1 3 5 7,
+// e23 = 8 10 12 14 | 9 11 13 15.
+__device__ __forceinline__ void e4m3_seg16(const float2 (&v)[8], float s, float rs,
+                                           uint32_t& lo, uint32_t& hi, uint32_t* e23) {
+  const float2 sp = make_float2(s * 512.0f, s * 512.0f);
+  const float2 rp = make_float2(rs * 0.001953125f, rs * 0.001953125f);
+  float2 d[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) d[j] = div2_rn(v[j], sp, rp);
+  lo = e4m3_no_neg_zero(cvt_e4m3x2(d[1].x, d[0].x) | (cvt_e4m3x2(d[3].x, d[2].x) << 16));
+  hi = e4m3_no_neg_zero(cvt_e4m3x2(d[1].y, d[0].y) | (cvt_e4m3x2(d[3].y, d[2].y) << 16));
+  e23[0] = e4m3_no_neg_zero(cvt_e4m3x2(d[5].x, d[4].x) | (cvt_e4m3x2(d[7].x, d[6].x) << 16));
+  e23[1] = e4m3_no_neg_zero(cvt_e4m3x2(d[5].y, d[4].y) | (cvt_e4m3x2(d[7].y, d[6].y) << 16));
+}
+
 // Quantise 16 consecutive raw elements (8 bf16x2 words) of one row-group
 // segment: smoothing divide rounded to bf16, then the group's INT4 codes.
 // The 4 lanes of a quad hold the 64 elements of one group. E4M3: write the
@@ -124,6 +159,14 @@ __device__ __forceinline__ void quant_seg16(const uint32_t (&xw)[8], const float
   lo = 0;
   hi = 0;
   if constexpr (E4M3) {
+    if (amax <= 7.25f * s) {
+      // |v/s| <= 7.25, so rint(v/s) needs no clamp and the e4m3 conversion
+      // of (v/s) * 2^-9 (subnormal range, spacing 2^-9, round half to even)
+      // is the operand byte itself
+      e4m3_seg16(v, s, rs, lo, hi, e23);
+      scale_out = sh;
+      return;
+    }
     uint32_t e2 = 0, e3 = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -154,8 +197,43 @@ __device__ __forceinline__ uint4 onehot_k8(uint32_t bits, int g) {
   return make_uint4(q == 0 ? w : 0u, q == 1 ? w : 0u, q == 2 ? w : 0u, q == 3 ? w : 0u);
 }
 
-// NB = padded rank / 8 (0 = no low-rank branch); MT = m16 row tiles per CTA
-// (16 * MT rows); act_warps<NB>() warps split K round-robin in 64-wide chunks.
+// Host helpers defined with the GEMM launches (same translation unit).
+static int make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize,
+                     uint64_t cols, uint64_t rows, uint32_t bx, uint32_t by,
+                     CUtensorMapSwizzle sw);
+static int sm_count();
+
+namespace actq {
+// x arrives by TMA in 16-row x 64-column bf16 boxes (2 KB, 128-byte rows,
+// SWIZZLE_128B), one private ring of kStages boxes per warp.
+#ifndef GWB_ACT_STAGES
+#define GWB_ACT_STAGES 2
+#endif
+constexpr int kStages = GWB_ACT_STAGES;
+constexpr int kBoxBytes = 16 * 128;
+template <int NB> __host__ __device__ constexpr size_t smem_bytes() {
+  return 1024 + (size_t)act_warps<NB>() * kStages * kBoxBytes   // x rings
+         + (size_t)act_warps<NB>() * 64 * sizeof(float)          // per-warp 1/smooth
+         + (size_t)act_warps<NB>() * 16 * NB * 8 * sizeof(float)  // low-rank partials
+         + (size_t)act_warps<NB>() * kStages * sizeof(uint64_t);  // ring barriers
+}
+}  // namespace actq
+
+// Wait for a copy still in flight while unwinding after a failed wait:
+// bounded, and not cut short by the error flag the failure already set.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const long long start = clock64();
+  const long long limit = *((volatile long long*)&gwb_wait_limit);
+  while (!mbar_try_wait(bar, parity) && clock64() - start <= limit) {
+  }
+}
+
+// NB = padded rank / 8 (0 = no low-rank branch). Persistent: CTA b takes the
+// 16-row tiles b, b + gridDim.x, ...; within a tile its act_warps<NB>()
+// warps split K round-robin in 64-wide chunks (chunk kc to warp kc % W). Each
+// warp walks its (tile, chunk) items in order through a private TMA ring of
+// x boxes, so the next tile's first chunks are in flight while this tile's
+// low-rank partials are reduced.
 // MMA_FORM = false writes the interchange form: packed codes u8 [M, K/2] and
 // ascale f16 [M, K/64]. MMA_FORM = true writes the GEMM operand form: codes
 // u8 [M, K] as e4m3 bytes of q * 2^-9 in the within-8 operand order
@@ -164,111 +242,147 @@ __device__ __forceinline__ uint4 onehot_k8(uint32_t bits, int g) {
 // matrix row).
 // la = bf16(x · L1) on raw x: each warp accumulates its K chunks with
 // mma.sync; the per-warp partials are summed in a fixed order through
-// shared memory, so la is deterministic.
-template <int NB, bool MMA_FORM, int MT>
+// shared memory, so la is deterministic and independent of M and the grid.
+template <int NB, bool MMA_FORM>
 __global__ void __launch_bounds__(act_warps<NB>() * 32, 1)
-act_int4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ smooth,
+act_int4_kernel(const __grid_constant__ CUtensorMap tmX, const __nv_bfloat16* __restrict__ smooth,
                 const __nv_bfloat16* __restrict__ down_t, uint8_t* __restrict__ codes,
                 __half* __restrict__ ascale, __nv_bfloat16* __restrict__ la, int M, int K) {
+  using namespace actq;
   constexpr int RP = NB * 8;
-  constexpr int ROWS = 16 * MT;
-  constexpr int kActWarps = act_warps<NB>();
-  extern __shared__ float smem_f[];   // [K] smoothing reciprocals, then [kActWarps][ROWS][RP]
-  float* rs = smem_f;
-  float* red = smem_f + K;
+  constexpr int W = act_warps<NB>();
+  constexpr int S = kStages;
+  extern __shared__ uint8_t act_smem_raw[];
+  uint8_t* base = act_smem_raw + ((1024u - (smem_u32(act_smem_raw) & 1023u)) & 1023u);
+  uint8_t* xs = base;                                                  // [W][S][2 KB]
+  float* rsw = reinterpret_cast<float*>(xs + W * S * kBoxBytes);       // [W][64]
+  float* red = rsw + W * 64;                                           // [W][16][RP]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + W * 16 * RP);     // [W][S]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int nchunks = K / 64;
   const int G = K / 64;
+  const int ntiles = (M + 15) / 16;
   const bool has_smooth = smooth != nullptr;
-  // RN(1 / smooth[k]) once per CTA (each column's divide needs it in every row)
-  if (has_smooth) {
-    for (int i = threadIdx.x; i < K / 2; i += blockDim.x) {
-      const uint32_t pair = __ldg(reinterpret_cast<const uint32_t*>(smooth) + i);
-      rs[2 * i] = __frcp_rn(bf_lo(pair));
-      rs[2 * i + 1] = __frcp_rn(bf_hi(pair));
-    }
-    __syncthreads();
-  }
+  uint8_t* my_xs = xs + warp * S * kBoxBytes;
+  uint64_t* my_bar = bars + warp * S;
+  float* my_rs = rsw + warp * 64;
 
-  int rows[MT][2];
-  bool valid[MT][2];
-  const uint4* xr[MT][2];
-#pragma unroll
-  for (int t = 0; t < MT; ++t)
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&my_bar[s], 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmX);
+  }
+  __syncwarp();
+
+  // this warp's chunks per tile and tiles: item i = (tile i / per, chunk i % per)
+  const int per = nchunks > warp ? (nchunks - warp + W - 1) / W : 0;
+  const int my_tiles =
+      ntiles > (int)blockIdx.x ? (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+  const int total = per * my_tiles;
+  int issued = 0;
+  auto issue = [&](int i) {
+    if (i >= total) return;
+    if (lane == 0) {
+      const int tile = blockIdx.x + (i / per) * gridDim.x;
+      const int kc = warp + (i % per) * W;
+      const int s = i % S;
+      mbar_arrive_expect_tx(&my_bar[s], kBoxBytes);
+      tma_load_2d(my_xs + s * kBoxBytes, &tmX, &my_bar[s], kc * 64, tile * 16);
+    }
+    issued = i + 1;
+  };
+  for (int i = 0; i < S; ++i) issue(i);
+
+  bool ok = true;
+  int item = 0;
+  for (int t = 0; t < my_tiles; ++t) {
+    const int tile = blockIdx.x + t * gridDim.x;
+    int rows[2];
+    bool valid[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      rows[t][h] = blockIdx.x * ROWS + 16 * t + 8 * h + g;
-      valid[t][h] = rows[t][h] < M;
-      xr[t][h] = reinterpret_cast<const uint4*>(x + (size_t)(valid[t][h] ? rows[t][h] : 0) * K);
+      rows[h] = tile * 16 + 8 * h + g;
+      valid[h] = rows[h] < M;
     }
-
-  float acc[MT][NB > 0 ? NB : 1][4];
-#pragma unroll
-  for (int t = 0; t < MT; ++t)
+    float acc[NB > 0 ? NB : 1][4];
 #pragma unroll
     for (int j = 0; j < (NB > 0 ? NB : 1); ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[t][j][e] = 0.f;
+      for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
 
-  // x words of the current chunk; the next chunk's are loaded at the top of
-  // each iteration so their latency overlaps this chunk's work
-  uint4 nx[MT][2][2];
-  auto load_x = [&](int kc_) {
-    const int kk = kc_ * 64 + 16 * c;
+    for (int jc = 0; jc < per; ++jc, ++item) {
+      const int kc = warp + jc * W;
+      const int k0 = kc * 64 + 16 * c;  // this lane's 16-element segment
+      const int s = item % S;
+      if (ok) ok = mbar_wait(&my_bar[s], (item / S) & 1, GWB_ERR_TIMEOUT_ACT);
+      float sm[16], rsm[16];
+      if (has_smooth) {
+        // RN(1 / smooth) of the chunk's 64 columns, two per lane, shared by
+        // the warp through shared memory (each column's divide needs it in
+        // all 16 rows)
+        const uint32_t pair = __ldg(reinterpret_cast<const uint32_t*>(smooth + kc * 64) + lane);
+        my_rs[2 * lane] = __frcp_rn(bf_lo(pair));
+        my_rs[2 * lane + 1] = __frcp_rn(bf_hi(pair));
+        const uint4* sp = reinterpret_cast<const uint4*>(smooth + k0);
+        const uint4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
+        const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
-    for (int t = 0; t < MT; ++t)
+        for (int j = 0; j < 8; ++j) {
+          sm[2 * j] = bf_lo(sw[j]);
+          sm[2 * j + 1] = bf_hi(sw[j]);
+        }
+      }
+      __syncwarp();
+      if (has_smooth) {
+        const float4* rp = reinterpret_cast<const float4*>(my_rs + 16 * c);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float4 r4 = rp[j];
+          rsm[4 * j] = r4.x; rsm[4 * j + 1] = r4.y; rsm[4 * j + 2] = r4.z; rsm[4 * j + 3] = r4.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) { sm[j] = 1.f; rsm[j] = 1.f; }
+      }
+      // rows g and g + 8 of the box, 32 bytes each: 16-byte chunks 2c and
+      // 2c + 1 of a 128-byte row, at (chunk ^ row % 8) after the swizzle
+      uint32_t w[2][8];
+      const uint8_t* box = my_xs + s * kBoxBytes;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const bool ok = valid[t][h] && kc_ < nchunks;
-        nx[t][h][0] = ok ? __ldg(xr[t][h] + kk / 8) : make_uint4(0, 0, 0, 0);
-        nx[t][h][1] = ok ? __ldg(xr[t][h] + kk / 8 + 1) : make_uint4(0, 0, 0, 0);
+        const uint8_t* rowp = box + (8 * h + g) * 128;
+        const uint4 p0 = *reinterpret_cast<const uint4*>(rowp + (((2 * c) ^ g) << 4));
+        const uint4 p1 = *reinterpret_cast<const uint4*>(rowp + (((2 * c + 1) ^ g) << 4));
+        w[h][0] = p0.x; w[h][1] = p0.y; w[h][2] = p0.z; w[h][3] = p0.w;
+        w[h][4] = p1.x; w[h][5] = p1.y; w[h][6] = p1.z; w[h][7] = p1.w;
       }
-  };
-  load_x(warp);
-  for (int kc = warp; kc < nchunks; kc += kActWarps) {
-    const int k0 = kc * 64 + 16 * c;  // this lane's 16-element segment
-    uint32_t w[MT][2][8];
+      // this chunk's down-projection fragments (L2): the first kEarly rank
+      // blocks are requested before the quantisation so their latency hides
+      // under it (more would spill), the rest after it
+      uint32_t dfr[NB > 0 ? NB : 1][8];
+      auto load_dfr = [&](int j) {
+        const uint4* dp = reinterpret_cast<const uint4*>(down_t + (size_t)(8 * j + g) * K + k0);
+        const uint4 d0 = __ldg(dp), d1 = __ldg(dp + 1);
+        dfr[j][0] = d0.x; dfr[j][1] = d0.y; dfr[j][2] = d0.z; dfr[j][3] = d0.w;
+        dfr[j][4] = d1.x; dfr[j][5] = d1.y; dfr[j][6] = d1.z; dfr[j][7] = d1.w;
+      };
+      constexpr int kEarly = NB < 2 ? NB : (NB <= 4 || NB > 8 ? 2 : 0);
 #pragma unroll
-    for (int t = 0; t < MT; ++t)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint4 p0 = nx[t][h][0], p1 = nx[t][h][1];
-        w[t][h][0] = p0.x; w[t][h][1] = p0.y; w[t][h][2] = p0.z; w[t][h][3] = p0.w;
-        w[t][h][4] = p1.x; w[t][h][5] = p1.y; w[t][h][6] = p1.z; w[t][h][7] = p1.w;
+      for (int j = 0; j < kEarly; ++j) load_dfr(j);
+      // every lane has read the box (and the reciprocals): refill the slot
+      __syncwarp();
+      if (ok) {
+        if (lane == 0) fence_proxy_async_smem();
+        issue(item + S);
       }
-    load_x(kc + kActWarps);
-    float sm[16], rsm[16];
-    if (has_smooth) {
-      const uint4* sp = reinterpret_cast<const uint4*>(smooth + k0);
-      const uint4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
-      const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        sm[2 * j] = bf_lo(sw[j]);
-        sm[2 * j + 1] = bf_hi(sw[j]);
-      }
-      // the segment's 16 reciprocals from shared memory (the 8 lanes of a
-      // segment read the same addresses: broadcast)
-      const float4* rp = reinterpret_cast<const float4*>(rs + k0);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float4 r4 = rp[j];
-        rsm[4 * j] = r4.x; rsm[4 * j + 1] = r4.y; rsm[4 * j + 2] = r4.z; rsm[4 * j + 3] = r4.w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) { sm[j] = 1.f; rsm[j] = 1.f; }
-    }
-#pragma unroll
-    for (int t = 0; t < MT; ++t)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t lo, hi, e23[2];
         __half sc;
-        quant_seg16<MMA_FORM>(w[t][h], sm, rsm, has_smooth, lo, hi, sc, e23);
-        if (valid[t][h]) {
-          const int row = rows[t][h];
+        quant_seg16<MMA_FORM>(w[h], sm, rsm, has_smooth, lo, hi, sc, e23);
+        if (valid[h]) {
+          const int row = rows[h];
           if constexpr (MMA_FORM) {
             *reinterpret_cast<uint4*>(codes + (size_t)row * K + k0) =
                 make_uint4(lo, hi, e23[0], e23[1]);
@@ -281,55 +395,74 @@ act_int4_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __rest
           }
         }
       }
-    if constexpr (NB > 0) {
-      // k is permuted consistently in A and B: logical fragment positions
-      // (2c,2c+1 | 2c+8,2c+9) of k16-step s map to physical 16c+4s+(0,1 | 2,3).
+      if constexpr (NB > 0) {
+        // k is permuted consistently in A and B: logical fragment positions
+        // (2c,2c+1 | 2c+8,2c+9) of k16-step s map to physical 16c+4s+(0,1 | 2,3).
+        // Ranks up to 32 and above 64: the NB accumulators are independent,
+        // so step s of every j is issued before step s + 1. Ranks 48 and 64
+        // (register-bound) load and consume one rank block at a time.
+        if constexpr (kEarly > 0) {
 #pragma unroll
-      for (int j = 0; j < NB; ++j) {
-        const uint4* dp = reinterpret_cast<const uint4*>(down_t + (size_t)(8 * j + g) * K + k0);
-        const uint4 d0 = __ldg(dp), d1 = __ldg(dp + 1);
-        const uint32_t dw[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+          for (int j = kEarly; j < NB; ++j) load_dfr(j);
 #pragma unroll
-        for (int t = 0; t < MT; ++t)
+          for (int s4 = 0; s4 < 4; ++s4) {
+            const uint32_t a[4] = {w[0][2 * s4], w[1][2 * s4], w[0][2 * s4 + 1],
+                                   w[1][2 * s4 + 1]};
 #pragma unroll
-          for (int s = 0; s < 4; ++s) {
-            const uint32_t a[4] = {w[t][0][2 * s], w[t][1][2 * s], w[t][0][2 * s + 1],
-                                   w[t][1][2 * s + 1]};
-            mma_bf16_16816(acc[t][j], a, dw[2 * s], dw[2 * s + 1]);
+            for (int j = 0; j < NB; ++j)
+              mma_bf16_16816(acc[j], a, dfr[j][2 * s4], dfr[j][2 * s4 + 1]);
           }
+        } else {
+#pragma unroll
+          for (int j = 0; j < NB; ++j) {
+            load_dfr(j);
+#pragma unroll
+            for (int s4 = 0; s4 < 4; ++s4) {
+              const uint32_t a[4] = {w[0][2 * s4], w[1][2 * s4], w[0][2 * s4 + 1],
+                                     w[1][2 * s4 + 1]};
+              mma_bf16_16816(acc[j], a, dfr[j][2 * s4], dfr[j][2 * s4 + 1]);
+            }
+          }
+        }
       }
     }
-  }
 
-  if constexpr (NB > 0) {
-#pragma unroll
-    for (int t = 0; t < MT; ++t)
+    if constexpr (NB > 0) {
 #pragma unroll
       for (int j = 0; j < NB; ++j) {
-        float* r0 = red + ((size_t)warp * ROWS + 16 * t + g) * RP + 8 * j + 2 * c;
+        float* r0 = red + ((size_t)warp * 16 + g) * RP + 8 * j + 2 * c;
         float* r1 = r0 + 8 * RP;
-        r0[0] = acc[t][j][0];
-        r0[1] = acc[t][j][1];
-        r1[0] = acc[t][j][2];
-        r1[1] = acc[t][j][3];
+        r0[0] = acc[j][0];
+        r0[1] = acc[j][1];
+        r1[0] = acc[j][2];
+        r1[1] = acc[j][3];
       }
-    __syncthreads();
-    for (int i = threadIdx.x; i < ROWS * RP; i += blockDim.x) {
-      float sum = 0.f;
+      __syncthreads();
+      for (int i = threadIdx.x; i < 16 * RP; i += blockDim.x) {
+        float sum = 0.f;
 #pragma unroll
-      for (int w2 = 0; w2 < kActWarps; ++w2) sum += red[(size_t)w2 * ROWS * RP + i];
-      const int row = blockIdx.x * ROWS + i / RP;
-      if (row < M) la[(size_t)row * RP + i % RP] = __float2bfloat16_rn(sum);
+        for (int w2 = 0; w2 < W; ++w2) sum += red[(size_t)w2 * 16 * RP + i];
+        const int row = tile * 16 + i / RP;
+        if (row < M) la[(size_t)row * RP + i % RP] = __float2bfloat16_rn(sum);
+      }
+      __syncthreads();
     }
   }
+  // after a failed wait: let the boxes still in flight land before exiting
+  if (!ok && lane == 0)
+    for (int i = item; i < issued; ++i) drain_wait(&my_bar[i % S], (i / S) & 1);
 }
 
-template <bool MMA_FORM, int MT>
-static int launch_act_int4_mt(const void* x, const void* smooth, const void* down_t, void* codes,
-                              void* ascale, void* la, int M, int K, int rank_pad,
-                              cudaStream_t st) {
-  dim3 grid((M + 16 * MT - 1) / (16 * MT));
-  auto X = static_cast<const __nv_bfloat16*>(x);
+template <bool MMA_FORM>
+static int launch_act_int4_t(const void* x, const void* smooth, const void* down_t, void* codes,
+                             void* ascale, void* la, int M, int K, int rank_pad,
+                             cudaStream_t st) {
+  CUtensorMap tmX;
+  int rc = make_tmap(&tmX, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K, (uint64_t)M, 64,
+                     16, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != GWB_SUCCESS) return rc;
+  const int ntiles = (M + 15) / 16;
+  const dim3 grid(ntiles < sm_count() ? ntiles : sm_count());
   auto S = static_cast<const __nv_bfloat16*>(smooth);
   auto D = static_cast<const __nv_bfloat16*>(down_t);
   auto C = static_cast<uint8_t*>(codes);
@@ -337,13 +470,15 @@ static int launch_act_int4_mt(const void* x, const void* smooth, const void* dow
   auto L = static_cast<__nv_bfloat16*>(la);
 #define GWB_ACT_CASE(RPAD, NBV)                                                              \
   case RPAD: {                                                                               \
-    auto k = act_int4_kernel<NBV, MMA_FORM, MT>;                                             \
+    auto k = act_int4_kernel<NBV, MMA_FORM>;                                                 \
     const dim3 block(act_warps<NBV>() * 32);                                                 \
-    const size_t smem = ((size_t)K + (size_t)act_warps<NBV>() * 16 * MT * rank_pad) *        \
-                        sizeof(float);                                                       \
-    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                               (int)smem);                                   \
-    k<<<grid, block, smem, st>>>(X, S, D, C, A, L, M, K);                                    \
+    const size_t smem = actq::smem_bytes<NBV>();                                             \
+    static bool attr = false;                                                                \
+    if (!attr) {                                                                             \
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
+      attr = true;                                                                           \
+    }                                                                                        \
+    k<<<grid, block, smem, st>>>(tmX, S, D, C, A, L, M, K);                                  \
     break;                                                                                   \
   }
   switch (rank_pad) {
@@ -365,10 +500,10 @@ static int launch_act_int4_mt(const void* x, const void* smooth, const void* dow
 int launch_act_int4(const void* x, const void* smooth, const void* down_t, void* codes,
                     void* ascale, void* la, int M, int K, int rank_pad, bool mma_form,
                     cudaStream_t st) {
-  // one m16 row tile per CTA measured fastest (M = 4608 and M = 16896)
+  if (M <= 0 || K <= 0 || K % 64) return GWB_E_SHAPE;
   if (mma_form)
-    return launch_act_int4_mt<true, 1>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st);
-  return launch_act_int4_mt<false, 1>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st);
+    return launch_act_int4_t<true>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st);
+  return launch_act_int4_t<false>(x, smooth, down_t, codes, ascale, la, M, K, rank_pad, st);
 }
 
 // Scale interchange form f16 [R, K/64] -> GEMM scale-operand rows

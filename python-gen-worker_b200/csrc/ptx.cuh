@@ -18,6 +18,7 @@ enum GwbDevError : int {
   GWB_ERR_TIMEOUT_MMA = 2,
   GWB_ERR_TIMEOUT_EPILOGUE = 3,
   GWB_ERR_TIMEOUT_UNPACK = 4,
+  GWB_ERR_TIMEOUT_ACT = 5,
 };
 
 // Device-side error flag (the library is built as one translation unit).
