@@ -737,7 +737,9 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  uint64_t* sf_full = acc_empty + 1;          // [SF_SLOTS] scale tiles copied into TMEM
+  uint64_t* sf_empty = sf_full + SF_SLOTS;    // [SF_SLOTS] MMAs reading the slot done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_empty + SF_SLOTS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = K / 256;
@@ -753,9 +755,12 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
   const int ntiles = ((M + kBM - 1) / kBM) * tiles_n;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+    // a stage is free again once the MMA thread and the scale-copy thread
+    // have both released it
+    for (int i = 0; i < STAGES; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 2); }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, EPI_WARPS);
+    for (int i = 0; i < SF_SLOTS; ++i) { mbar_init(&sf_full[i], 1); mbar_init(&sf_empty[i], 1); }
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -821,7 +826,7 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       // -------------------------------------------------------------- MMA
       constexpr uint32_t idesc = idesc_mxf4(kBM, BN);
       constexpr uint32_t idesc_lr = idesc_bf16(kBM, BN);
-      int ui = 0, lt = 0;
+      int ui = 0, lt = 0, kbi = 0;   // ring stages, tiles, k-blocks (scale slots) used
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++lt) {
         if (!mbar_wait(acc_empty, (lt & 1) ^ 1, GWB_ERR_TIMEOUT_MMA)) break;
@@ -840,14 +845,61 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
           mma_commit(&empty[u]);
         }
         if (!ok) break;
-        for (int kb = 0; kb < nk; ++kb, ++ui) {
+        for (int kb = 0; kb < nk; ++kb, ++ui, ++kbi) {
           const int u = ui % STAGES;
-          if (!mbar_wait(&full[u], (ui / STAGES) & 1, GWB_ERR_TIMEOUT_MMA)) { ok = false; break; }
+          const int sl = kbi % SF_SLOTS;
+          if (!mbar_wait(&full[u], (ui / STAGES) & 1, GWB_ERR_TIMEOUT_MMA) ||
+              !mbar_wait(&sf_full[sl], (kbi / SF_SLOTS) & 1, GWB_ERR_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + u * STAGE_BYTES);
           const uint32_t b_base = a_base + A_BYTES;
-          const uint32_t sfa_s = b_base + B_BYTES, sfb_s = sfa_s + SFA_BYTES;
-          const uint32_t sfa_t = tmem + SF_COL + (ui % SF_SLOTS) * SF_SLOT, sfb_t = sfa_t + 16;
+          const uint32_t sfa_t = tmem + SF_COL + sl * SF_SLOT, sfb_t = sfa_t + 16;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            mma_mxf4(tmem + ACC_COL, sdesc_k128(a_base + 32 * ks), sdesc_k128(b_base + 32 * ks),
+                     idesc, sfa_t + 4 * ks, sfb_t + 8 * ks,
+                     (has_lr || kb > 0 || ks > 0) ? 1u : 0u);
+          mma_commit(&empty[u]);
+          mma_commit(&sf_empty[sl]);
+        }
+        if (ok) mma_commit(acc_full);
+      }
+    } else if (warp == 2 && lane == 0) {
+      // ----------------------------------------------------- scale copies
+      // Copies each k-block's blocked scale tiles from its ring stage into a
+      // TMEM scale slot (tcgen05.cp), up to SF_SLOTS k-blocks ahead of the
+      // MMA thread, so the copies stay out of the MMA issue stream. The MMA
+      // thread waits sf_full (this thread's commit: copies done) before the
+      // stage's MMAs and releases the slot with its own commit (sf_empty).
+      // This thread follows every use of every ring stage, the low-rank ones
+      // included, and releases each (empty counts both threads): a parity
+      // wait cannot tell a stage's completions apart when the waiter runs a
+      // phase ahead or two behind.
+      int ui = 0, kbi = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+        for (int h = 0; h < lr_slots; ++h, ++ui) {
+          const int u = ui % STAGES;
+          ok = mbar_wait(&full[u], (ui / STAGES) & 1, GWB_ERR_TIMEOUT_PRODUCER);
+          if (!ok) break;
+          mbar_arrive(&empty[u]);
+        }
+        if (!ok) break;
+        for (int kb = 0; kb < nk; ++kb, ++ui, ++kbi) {
+          const int u = ui % STAGES;
+          const int sl = kbi % SF_SLOTS;
+          if (!mbar_wait(&full[u], (ui / STAGES) & 1, GWB_ERR_TIMEOUT_PRODUCER) ||
+              !mbar_wait(&sf_empty[sl], ((kbi / SF_SLOTS) & 1) ^ 1, GWB_ERR_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sfa_s = smem_u32(smem + u * STAGE_BYTES) + A_BYTES + B_BYTES;
+          const uint32_t sfb_s = sfa_s + SFA_BYTES;
+          const uint32_t sfa_t = tmem + SF_COL + sl * SF_SLOT, sfb_t = sfa_t + 16;
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
             // per K = 64 step: A scales 4 columns, B scales 8 columns (rows
@@ -856,14 +908,9 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             tmem_cp_32x128b_x4(sfb_t + 8 * ks, sdesc_noswz(sfb_s + 512 * ks, 0));
             tmem_cp_32x128b_x4(sfb_t + 8 * ks + 4, sdesc_noswz(sfb_s + SFA_BYTES + 512 * ks, 0));
           }
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            mma_mxf4(tmem + ACC_COL, sdesc_k128(a_base + 32 * ks), sdesc_k128(b_base + 32 * ks),
-                     idesc, sfa_t + 4 * ks, sfb_t + 8 * ks,
-                     (has_lr || kb > 0 || ks > 0) ? 1u : 0u);
+          mma_commit(&sf_full[sl]);
           mma_commit(&empty[u]);
         }
-        if (ok) mma_commit(acc_full);
       }
     }
   } else {
