@@ -80,12 +80,24 @@ def test_int4_activation_bit_exact_over_wide_value_ranges(cuda_ready):
     mant = torch.rand(m, k, generator=gen) + 0.5
     expo = torch.randint(-20, 12, (m, k), generator=gen).float()
     sign = torch.where(torch.rand(m, k, generator=gen) < 0.5, -1.0, 1.0)
-    x = (sign * mant * torch.pow(2.0, expo)).to(torch.bfloat16)
+    x = (sign * mant * torch.pow(2.0, expo))
+    # rows whose groups clamp the scale: all-zero, tiny (amax / 7 below the
+    # smallest f16 subnormal) and huge (amax / 7 above the f16 maximum)
+    x[0] = 0.0
+    x[1] = x[1] * 2.0 ** -40
+    x[2] = x[2] * 2.0 ** 12
+    x = x.to(torch.bfloat16)
     smooth = torch.pow(10.0, torch.rand(k, generator=gen) * 6 - 3).to(torch.bfloat16)
     codes, ascale, _ = ops.svdq_w4a4_quant(x.cuda(), smooth.cuda(), None)
     want_codes, want_scale = O.quant_int4(O.smooth_bf16(x, smooth))
     assert torch.equal(codes.cpu(), want_codes)
     assert torch.equal(ascale.cpu().view(torch.int16), want_scale.view(torch.int16))
+    # the operand-form quantiser (the GEMM's input on the hot path) on the
+    # same values: the operand bytes of the same codes, the same scales
+    c8, sk8, _ = ops.svdq_w4a4_quant_mma(x.cuda(), smooth.cuda(), None)
+    assert torch.equal(c8, ops.expand_w4a4_weight(want_codes.cuda()))
+    assert torch.equal(sk8.view(torch.int16),
+                       ops.svdq_w4a4_scale_k8(want_scale.cuda()).view(torch.int16))
 
 
 def test_int4_activation_without_smoothing(cuda_ready):
