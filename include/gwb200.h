@@ -311,7 +311,8 @@ int gwb_awq_w4a16_mm(const void* x, const void* weight, const void* wscales, con
                      const void* bias, int64_t M, int64_t N, int64_t K, void* out, void* stream);
 
 /* Reads and clears the device-side error flag set by a bounded wait that
- * expired (0 = none). Synchronises the device. */
+ * expired (0 = none; 1 TMA producer, 2 MMA thread, 3 epilogue, 4 unpack
+ * warps, 5 the INT4 quantiser's x boxes). Synchronises the device. */
 int gwb_device_error(int* code);
 
 /* 0 when the current device is sm_100 (B200), GWB_E_ARCH otherwise. */
