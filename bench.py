@@ -109,7 +109,7 @@ class ClockSampler:
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int, path: Path):
-        self.index, self.path, self.proc = index, path, None
+        self.index, self.path, self.proc, self.skip = index, path, None, 0
 
     def __enter__(self):
         try:
@@ -117,8 +117,19 @@ class ClockSampler:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.f, stderr=subprocess.DEVNULL)
+            # nvidia-smi needs a moment before its first line; the timed
+            # region opens only once it samples (bounded wait), so even a
+            # region of a few hundred ms holds samples
+            t0 = time.time()
+            while time.time() - t0 < 5.0 and self.proc.poll() is None:
+                self.f.flush()
+                if self.path.stat().st_size > 0:
+                    break
+                time.sleep(0.02)
+            self.f.flush()
+            self.skip = self.path.read_text().count("\n")   # samples before the region
         except Exception:  # noqa: BLE001
             self.proc = None
         return self
@@ -137,6 +148,9 @@ class ClockSampler:
             rows = [r.split(", ") for r in self.path.read_text().strip().splitlines() if r]
         except Exception:  # noqa: BLE001
             rows = []
+        # the samples taken inside the timed region, else (a region shorter
+        # than one sampling interval) the last one taken before it
+        rows = rows[self.skip:] if len(rows) > self.skip else rows[-1:]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = [float(r[1]) for r in rows if r[1].strip().isdigit()]
