@@ -295,7 +295,7 @@ act_int4_kernel(const __grid_constant__ CUtensorMap tmX, const __nv_bfloat16* __
   for (int i = 0; i < S; ++i) issue(i);
 
   bool ok = true;
-  int item = 0;
+  int item = 0, failed_at = -1;   // first item whose wait ran out
   for (int t = 0; t < my_tiles; ++t) {
     const int tile = blockIdx.x + t * gridDim.x;
     int rows[2];
@@ -315,7 +315,11 @@ act_int4_kernel(const __grid_constant__ CUtensorMap tmX, const __nv_bfloat16* __
       const int kc = warp + jc * W;
       const int k0 = kc * 64 + 16 * c;  // this lane's 16-element segment
       const int s = item % S;
-      if (ok) ok = mbar_wait(&my_bar[s], (item / S) & 1, GWB_ERR_TIMEOUT_ACT);
+      if (ok) {
+        // the outcome is made warp-uniform: the lanes leave together
+        ok = __all_sync(0xffffffffu, mbar_wait(&my_bar[s], (item / S) & 1, GWB_ERR_TIMEOUT_ACT));
+        if (!ok) failed_at = item;
+      }
       float sm[16], rsm[16];
       if (has_smooth) {
         // RN(1 / smooth) of the chunk's 64 columns, two per lane, shared by
@@ -448,9 +452,10 @@ act_int4_kernel(const __grid_constant__ CUtensorMap tmX, const __nv_bfloat16* __
       __syncthreads();
     }
   }
-  // after a failed wait: let the boxes still in flight land before exiting
+  // after a failed wait: let the boxes still in flight (the one that timed
+  // out and any issued after it) land before exiting
   if (!ok && lane == 0)
-    for (int i = item; i < issued; ++i) drain_wait(&my_bar[i % S], (i / S) & 1);
+    for (int i = failed_at; i < issued; ++i) drain_wait(&my_bar[i % S], (i / S) & 1);
 }
 
 template <bool MMA_FORM>
