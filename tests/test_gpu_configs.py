@@ -229,3 +229,27 @@ def test_dual_block_chain_matches_oracle(cuda_ready):
         h_gpu = y
     assert O.rel_l2(h_gpu.cpu(), h_ref) <= 5e-3
     assert native.device_error() == 0
+
+
+@pytest.mark.parametrize("rank", [32, 128])
+def test_int4_linear_is_batch_invariant(cuda_ready, rank):
+    """A row's quantised codes, scales, la and output do not depend on how
+    many rows share the call: rows 0..76 computed alone, inside 2112 rows (the
+    8-GPU shard size) and inside 4736 rows (several tiles per CTA) are
+    bit-identical. The multi-GPU shard check relies on this."""
+    k, n = 3072, 384
+    x = O.synth_activation(4736, k, seed=41 + rank)
+    L = O.synth_svdq_layer(k, n, rank, seed=43, x_calib=x[:512])
+    mod = build_svdq_int4_linear({"weight": L["w_packed"], "weight_scale": L["w_scale"],
+                                  "smooth_factor": L["smooth"], "proj_down": L["proj_down"],
+                                  "proj_up": L["proj_up"], "bias": L["bias"]}, device="cuda")
+    xc = x.cuda()
+    q_ref = mod.quantize(xc[:77].contiguous())
+    y_ref = mod(xc[:77].contiguous())
+    for m in (2112, 4736):
+        q = mod.quantize(xc[:m].contiguous())
+        assert torch.equal(q[0][:77], q_ref[0])                         # operand-form codes
+        assert torch.equal(q[1][:, :77].view(torch.int16), q_ref[1].view(torch.int16))
+        assert torch.equal(q[2][:77], q_ref[2])                         # la
+        assert torch.equal(mod(xc[:m].contiguous())[:77], y_ref)
+    assert native.device_error() == 0
