@@ -17,10 +17,10 @@
 namespace gwb {
 
 // warps per CTA (splitting K round-robin in 64-wide chunks): 16 warps of
-// 128 registers fill an SM with one CTA, so a small token count (one CTA per
-// 16 rows, e.g. 132 CTAs for a 2112-token shard) still runs 16 warps per SM;
-// ranks above 64 keep 8 warps with the larger register budget. The count
-// never depends on M, so a row's results do not depend on the shard size.
+// 128 registers fill an SM with one CTA, so a small token count (one 16-row
+// tile per CTA, e.g. 132 tiles for a 2112-token shard) still runs 16 warps
+// per SM; ranks above 64 keep 8 warps with the larger register budget. The
+// count never depends on M, so a row's results do not depend on the shard size.
 template <int NB> __host__ __device__ constexpr int act_warps() { return NB > 8 ? 8 : 16; }
 
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
