@@ -82,7 +82,7 @@ def test_gemv_matches_oracle_on_reference_layers(cuda_ready, oc, ic, splits, m):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("n,k,m", [(18432, 3072, 1), (18432, 3072, 2), (9216, 3072, 2),
-                                   (3072, 12288, 5)])
+                                   (3072, 12288, 5), (3072, 3072, 20)])
 def test_gemv_matches_oracle_at_flux_sizes(cuda_ready, n, k, m):
     g = torch.Generator().manual_seed(n + m)
     codes = torch.randint(0, 16, (n, k), generator=g, dtype=torch.uint8)
