@@ -123,3 +123,22 @@ def test_module_surface_and_swap():
     assert swap_linears(model, {"0": mod}) == 1 and model[0] is mod
     with pytest.raises(SvdqB200LayoutError):
         swap_linears(model, {"7": mod})
+
+
+def test_bench_clock_summary_keeps_the_timed_region(tmp_path):
+    """The bench's clock record: samples taken before the timed region opened
+    are dropped; a region shorter than one sampling interval falls back to
+    the last sample before it instead of reporting no clocks."""
+    import bench
+    p = tmp_path / "clocks.csv"
+    p.write_text("0, 1200, 1965, 100.0, 0x0, Not Active, Not Active, Not Active, Not Active\n"
+                 "0, 1965, 1965, 700.0, 0x4, Not Active, Not Active, Not Active, Active\n")
+    c = bench.ClockSampler(0, p)
+    c.skip = 1
+    s = c.summary()
+    assert s["samples"] == 1 and s["sm_mhz"] == 1965.0 and s["reasons"] == ["sw_power_cap"]
+    c.skip = 2
+    s = c.summary()
+    assert s["samples"] == 1 and s["sm_mhz"] == 1965.0
+    p.write_text("")
+    assert bench.ClockSampler(0, p).summary()["reasons"] == ["unsampled"]
