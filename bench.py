@@ -46,14 +46,16 @@ SINGLE = [("qkv_mlp", HIDDEN, 21504, False), ("out", 15360, HIDDEN, False)]
 N_DUAL, N_SINGLE = 19, 38
 INT8_DENSE_PEAK_TOPS = 4500.0   # B200 datasheet dense INT8 / FP8, for context
 PEAKS_FILE = ROOT / "profiles" / "tensor_peaks_b200.json"
-# DRAM bytes (read + write) of one gemm_w4a4_kernel launch at the cfg4 qkv
-# shape (M 16896, K 3072, N 9216), one ncu capture (dram__bytes_read.sum +
-# dram__bytes_write.sum, --clock-control none): 114.4 MB read (operands
-# 101 MB) + 276.7 MB written (the 311 MB bf16 output, part of it still in L2
-# when the kernel ends)
-GEMM_TRAFFIC_BYTES: Optional[float] = 114376192.0 + 276746752.0
-GEMM_TRAFFIC_NOTE = ("DRAM read+write of one launch at the cfg4 qkv shape (16896x3072->9216), "
-                     "one ncu capture; algorithmic 413 MB in the operand form (101 MB operands "
+# DRAM bytes (read + write) of one gemm_w4a4_kernel launch on the stored
+# weight at the cfg4 qkv shape (M 16896, K 3072, N 9216), one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum, --clock-control none):
+# 81.8 MB read (the algorithmic operand bytes: 51.9 MB operand-form codes,
+# 13.0 MB scale rows, 14.2 MB packed weight, 0.9 MB weight scales, 1.7 MB
+# low-rank operands) + 258.6 MB written (the 311 MB bf16 output, part of it
+# still in L2 when the kernel ends)
+GEMM_TRAFFIC_BYTES: Optional[float] = 81790208.0 + 258567168.0
+GEMM_TRAFFIC_NOTE = ("DRAM read+write of one launch on the stored weight at the cfg4 qkv shape "
+                     "(16896x3072->9216), one ncu capture; algorithmic 393 MB (81.7 MB operands "
                      "+ 311 MB bf16 output)")
 
 
